@@ -1,0 +1,579 @@
+// Split-KV GQA decode attention for sm_100a.
+//
+// Semantics follow the reference's `_decode_partials` + `_decode_merge`
+// (engine/kernels/decode_attention.py:31-127): for each (row b, KV head h) the G query
+// heads of that group attend to cache slots [0, len_b), len_b = position + 1; scores are
+// fp32 dot products scaled by scale*log2(e), softmax uses exp2 with a running maximum,
+// probabilities are rounded to bf16 before the P*V product (:90) while the denominator
+// sums the unrounded fp32 probabilities (:83), and splits are merged with a
+// log-sum-exp combine (:119-127).
+//
+// B200 design (not a translation of the Triton kernel):
+//  * Work unit = one 64-token tile of one (row, KV head). All valid tiles of all pairs
+//    form one sequence (row-major, then head, then tile); a persistent grid of `ctas`
+//    CTAs takes equal contiguous slices of it, so ragged lengths balance across SMs.
+//    Consecutive tiles of the same pair inside a CTA are one "run" with one online
+//    softmax state; a run that covers a whole pair writes the final output directly.
+//  * Warp 4 (one elected lane) streams K and V tiles with 2-D TMA loads
+//    (CU_TENSOR_MAP_SWIZZLE_128B, no multicast) into an NS-stage mbarrier ring.
+//  * Warps 0-3 each take 16 tokens of a tile. Scores are computed transposed,
+//    S^T[16 tok x 8 heads] = K * Q^T, with mma.sync m16n8k16 (Q^T held in registers for
+//    the whole run), the probabilities are transposed in registers (movmatrix) and
+//    O^T[D x 8] += V^T * P^T accumulates in registers. The swizzled layout makes every
+//    ldmatrix conflict-free.
+//  * Partials of runs that do not cover their pair go to slot (cta + pair) of the
+//    workspace; the combine kernel re-derives which CTAs touched each pair from the same
+//    integer partition, so no counters or atomics are needed and results are
+//    deterministic.
+#include "common.cuh"
+
+namespace fb {
+namespace attn {
+
+constexpr int kTile = 64;          // tokens per pipeline stage
+constexpr int kConsumerWarps = 4;  // 16 tokens each
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kMaxBatch = 1024;
+constexpr int kHeadsPad = 8;  // query heads per KV head, padded to the mma N
+
+struct Params {
+  const __nv_bfloat16* q;  // [B, Hq, D]
+  const int64_t* position;
+  int per_row;
+  __nv_bfloat16* out;  // [B, Hq, D]
+  float* acc;          // [slots, G, D]
+  float2* stats;       // [slots, G] (max, denominator)
+  int batch, q_heads, kv_heads, groups, capacity, ctas;
+  float scale_log2;
+  unsigned* err;
+};
+
+// Valid length of row b: position + 1 clamped into [0, capacity].
+__device__ __forceinline__ int row_length(const int64_t* position, int per_row, int b,
+                                          int capacity) {
+  long long p = position[per_row ? b : 0];
+  long long n = p + 1;
+  if (n < 0) n = 0;
+  if (n > capacity) n = capacity;
+  return static_cast<int>(n);
+}
+
+__device__ __forceinline__ int tiles_of(int len) { return (len + kTile - 1) / kTile; }
+
+// First tile of CTA i in a sequence of T tiles split over G CTAs.
+__device__ __forceinline__ long long slice_start(long long T, int i, int G) {
+  return (T * i) / G;
+}
+// The CTA whose slice contains tile t (largest i with slice_start(i) <= t).
+__device__ __forceinline__ int slice_owner(long long T, long long t, int G) {
+  return static_cast<int>(((t + 1) * G - 1) / T);
+}
+
+template <int D, int NS>
+struct Smem {
+  static constexpr int kBoxes = D / 64;
+  static constexpr int kTileBytes = kBoxes * kTile * 128;  // one of K or V
+  static constexpr int kStageBytes = 2 * kTileBytes;
+  // [stages][K | V] tiles, 1024-byte aligned (swizzle atom)
+  static constexpr int kStagesBytes = NS * kStageBytes;
+  static constexpr int kRedO = kConsumerWarps * D * kHeadsPad * 4;  // O^T partials per warp
+  static constexpr int kRedML = kConsumerWarps * kHeadsPad * 2 * 4;
+  static constexpr int kCum = (kMaxBatch + 1) * 4;
+  static constexpr int kBars = 2 * NS * 8;
+  static constexpr int kMisc = 64;
+  static constexpr int kTotal = 1024 + kStagesBytes + kRedO + kRedML + kCum + kBars + kMisc;
+};
+
+template <int D, int NS>
+__global__ void __launch_bounds__(kThreads, 1)
+    decode_partials_kernel(const __grid_constant__ CUtensorMap kmap,
+                           const __grid_constant__ CUtensorMap vmap, const Params p) {
+  using S = Smem<D, NS>;
+  constexpr int kBoxes = S::kBoxes;
+  constexpr int kKSteps = D / 16;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* stages = base;
+  float* red_o = reinterpret_cast<float*>(base + S::kStagesBytes);
+  float* red_ml = reinterpret_cast<float*>(base + S::kStagesBytes + S::kRedO);
+  int* cum = reinterpret_cast<int*>(base + S::kStagesBytes + S::kRedO + S::kRedML);
+  uint64_t* full = reinterpret_cast<uint64_t*>(base + S::kStagesBytes + S::kRedO + S::kRedML +
+                                               S::kCum);
+  uint64_t* empty = full + NS;
+  int* misc = reinterpret_cast<int*>(empty + NS);  // [0..3] start b,h,j ; [4] abort
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int B = p.batch, Hkv = p.kv_heads, G = p.groups;
+
+  // ---- plan: per-row tile prefix sums, this CTA's tile slice and its first tile ----
+  if (warp == 0) {
+    int running = 0;
+    if (lane == 0) cum[0] = 0;
+    for (int b0 = 0; b0 < B; b0 += 32) {
+      int b = b0 + lane;
+      int n = b < B ? tiles_of(row_length(p.position, p.per_row, b, p.capacity)) : 0;
+      int x = n;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+      }
+      if (b < B) cum[b + 1] = running + x;
+      running += __shfl_sync(0xffffffffu, x, 31);
+    }
+  }
+  if (warp == kConsumerWarps && lane == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    fence_barrier_init();
+    prefetch_tensormap(&kmap);
+    prefetch_tensormap(&vmap);
+    misc[4] = 0;
+  }
+  __syncthreads();
+
+  const long long total = static_cast<long long>(Hkv) * cum[B];
+  const long long t0 = total > 0 ? slice_start(total, blockIdx.x, p.ctas) : 0;
+  const long long t1 = total > 0 ? slice_start(total, blockIdx.x + 1, p.ctas) : 0;
+  const int count = static_cast<int>(t1 - t0);
+  if (count <= 0) return;
+
+  if (warp == 0) {
+    for (int b0 = 0; b0 < B; b0 += 32) {
+      int b = b0 + lane;
+      bool hit = false;
+      if (b < B) {
+        long long lo = static_cast<long long>(Hkv) * cum[b];
+        long long hi = static_cast<long long>(Hkv) * cum[b + 1];
+        hit = lo <= t0 && t0 < hi;
+      }
+      unsigned m = __ballot_sync(0xffffffffu, hit);
+      if (m != 0) {
+        if (lane == __ffs(m) - 1) {
+          int n = cum[b + 1] - cum[b];
+          long long off = t0 - static_cast<long long>(Hkv) * cum[b];
+          misc[0] = b;
+          misc[1] = static_cast<int>(off / n);
+          misc[2] = static_cast<int>(off % n);
+        }
+        break;
+      }
+    }
+  }
+  __syncthreads();
+
+  volatile int* abort_flag = &misc[4];
+
+  if (warp == kConsumerWarps) {
+    // ===================== producer: one lane issues every TMA =====================
+    if (lane == 0) {
+      int b = misc[0], h = misc[1], j = misc[2];
+      int n = cum[b + 1] - cum[b];
+      for (int k = 0; k < count; ++k) {
+        const int s = k % NS;
+        if (*abort_flag) break;
+        if (k >= NS) {
+          if (!mbar_wait_bounded(&empty[s], ((k / NS) - 1) & 1)) {
+            raise_error(p.err, kErrTimeoutEmpty);
+            *abort_flag = 1;
+            break;
+          }
+        }
+        uint8_t* kt = stages + s * S::kStageBytes;
+        uint8_t* vt = kt + S::kTileBytes;
+        const int row = (b * Hkv + h) * p.capacity + j * kTile;
+        mbar_arrive_expect_tx(&full[s], S::kStageBytes);
+#pragma unroll
+        for (int bx = 0; bx < kBoxes; ++bx) {
+          tma_load_2d(kt + bx * kTile * 128, &kmap, &full[s], bx * 64, row);
+          tma_load_2d(vt + bx * kTile * 128, &vmap, &full[s], bx * 64, row);
+        }
+        if (++j == n) {
+          j = 0;
+          if (++h == Hkv) {
+            h = 0;
+            do {
+              ++b;
+            } while (b < B && cum[b + 1] == cum[b]);
+            if (b < B) n = cum[b + 1] - cum[b];
+          }
+        }
+      }
+    }
+    return;
+  }
+
+  // ========================== consumers: warps 0..3 ==========================
+  const int g = lane >> 2;  // fragment row group
+  const int c = lane & 3;   // fragment column pair
+  const int ctid = threadIdx.x;  // 0..127
+
+  int b = misc[0], h = misc[1], j = misc[2];
+  int n = cum[b + 1] - cum[b];
+  int len = row_length(p.position, p.per_row, b, p.capacity);
+  int run_first = j;
+
+  uint32_t qb[kKSteps][2];
+  float o[kKSteps][4];
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+
+  auto load_q = [&](int bb, int hh) {
+    const bool live = g < G;
+    const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
+        p.q + (static_cast<size_t>(bb) * p.q_heads + hh * G + (live ? g : 0)) * D);
+#pragma unroll
+    for (int kk = 0; kk < kKSteps; ++kk) {
+      qb[kk][0] = live ? __ldg(qrow + (kk * 16 + 2 * c) / 2) : 0u;
+      qb[kk][1] = live ? __ldg(qrow + (kk * 16 + 8 + 2 * c) / 2) : 0u;
+    }
+#pragma unroll
+    for (int i = 0; i < kKSteps; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    m0 = m1 = -INFINITY;
+    l0 = l1 = 0.f;
+  };
+  load_q(b, h);
+
+  const float sl2 = p.scale_log2;
+  bool aborted = false;
+
+  for (int k = 0; k < count; ++k) {
+    const int s = k % NS;
+    if (!mbar_wait_bounded(&full[s], (k / NS) & 1)) {
+      raise_error(p.err, kErrTimeoutFull);
+      *abort_flag = 1;
+      aborted = true;
+    }
+    if (aborted || *abort_flag) {
+      aborted = true;
+      break;
+    }
+    uint8_t* kt = stages + s * S::kStageBytes;
+    uint8_t* vt = kt + S::kTileBytes;
+    const int tile_start = j * kTile;
+    const int slice = tile_start + warp * 16;  // first token of this warp's slice
+    if (slice < len) {
+      if (slice + 16 > len) {
+        // Ragged end: zero this warp's V rows at or past the valid length so that
+        // whatever the cache holds there (stale values, NaN) never meets a zero weight.
+        for (int e = lane; e < 16 * 8 * kBoxes; e += 32) {
+          const int r = e / (8 * kBoxes);
+          const int rest = e % (8 * kBoxes);
+          const int bx = rest / 8, ch = rest % 8;
+          if (slice + r >= len)
+            *reinterpret_cast<uint4*>(vt + bx * kTile * 128 + (warp * 16 + r) * 128 + ch * 16) =
+                make_uint4(0, 0, 0, 0);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+      }
+      // ---- S^T = K * Q^T for this warp's 16 tokens ----
+      float sc[4] = {0.f, 0.f, 0.f, 0.f};
+      const uint32_t krow = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+      for (int kk = 0; kk < kKSteps; ++kk) {
+        const int chunk = (kk & 3) * 2 + (lane >> 4);
+        const uint32_t addr = smem_u32(kt + (kk >> 2) * kTile * 128) + sw128(krow, chunk);
+        uint32_t a0, a1, a2, a3;
+        ldmatrix_x4(addr, a0, a1, a2, a3);
+        mma_bf16_16816(sc, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
+      }
+      // ---- online softmax over tokens (rows g, g+8), heads (2c, 2c+1) ----
+      const int tok0 = slice + g, tok1 = slice + g + 8;
+      float s0 = tok0 < len ? sc[0] * sl2 : -INFINITY;
+      float s1 = tok0 < len ? sc[1] * sl2 : -INFINITY;
+      float s2 = tok1 < len ? sc[2] * sl2 : -INFINITY;
+      float s3 = tok1 < len ? sc[3] * sl2 : -INFINITY;
+      float mx0 = fmaxf(s0, s2), mx1 = fmaxf(s1, s3);
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+      }
+      const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
+      const float pv0 = n0 == -INFINITY ? 0.f : n0;  // never form -inf - -inf
+      const float pv1 = n1 == -INFINITY ? 0.f : n1;
+      const float corr0 = exp2f(m0 - pv0), corr1 = exp2f(m1 - pv1);
+      const float p0 = exp2f(s0 - pv0), p1 = exp2f(s1 - pv1);
+      const float p2 = exp2f(s2 - pv0), p3 = exp2f(s3 - pv1);
+      l0 = l0 * corr0 + (p0 + p2);
+      l1 = l1 * corr1 + (p1 + p3);
+      m0 = n0;
+      m1 = n1;
+#pragma unroll
+      for (int i = 0; i < kKSteps; ++i) {
+        o[i][0] *= corr0;
+        o[i][1] *= corr1;
+        o[i][2] *= corr0;
+        o[i][3] *= corr1;
+      }
+      // P^T fragments (bf16, as the reference's P cast) -> B operand of the PV product.
+      const uint32_t pb0 = movmatrix_trans(pack_bf16x2(p0, p1));
+      const uint32_t pb1 = movmatrix_trans(pack_bf16x2(p2, p3));
+      // ---- O^T += V^T * P^T ----
+      const uint32_t vrow = warp * 16 + (lane & 7) + ((lane >> 4) & 1) * 8;
+#pragma unroll
+      for (int i = 0; i < kKSteps; ++i) {
+        const int cg = 2 * i + ((lane >> 3) & 1);
+        const uint32_t addr = smem_u32(vt + (cg >> 3) * kTile * 128) + sw128(vrow, cg & 7);
+        uint32_t a0, a1, a2, a3;
+        ldmatrix_x4_trans(addr, a0, a1, a2, a3);
+        mma_bf16_16816(o[i], a0, a1, a2, a3, pb0, pb1);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+
+    // ---- advance; finalize the run when the pair changes or the slice ends ----
+    const int cur_b = b, cur_h = h, cur_first = run_first, cur_last = j, cur_n = n;
+    bool run_end = (k == count - 1);
+    if (++j == n) {
+      j = 0;
+      run_end = true;
+      if (++h == Hkv) {
+        h = 0;
+        do {
+          ++b;
+        } while (b < B && cum[b + 1] == cum[b]);
+      }
+    }
+    if (run_end) {
+      // Per-warp denominators: reduce the per-thread partial sums over the 8 rows.
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) {
+        l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+      }
+      if (g == 0) {
+        red_ml[(warp * kHeadsPad + 2 * c) * 2 + 0] = m0;
+        red_ml[(warp * kHeadsPad + 2 * c) * 2 + 1] = l0;
+        red_ml[(warp * kHeadsPad + 2 * c + 1) * 2 + 0] = m1;
+        red_ml[(warp * kHeadsPad + 2 * c + 1) * 2 + 1] = l1;
+      }
+      if (2 * c < G) {
+#pragma unroll
+        for (int i = 0; i < kKSteps; ++i) {
+          float* r0 = red_o + ((warp * D) + 16 * i + g) * kHeadsPad + 2 * c;
+          float* r1 = red_o + ((warp * D) + 16 * i + g + 8) * kHeadsPad + 2 * c;
+          r0[0] = o[i][0];
+          r0[1] = o[i][1];
+          r1[0] = o[i][2];
+          r1[1] = o[i][3];
+        }
+      }
+      asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+      const bool whole = cur_first == 0 && cur_last == cur_n - 1;
+      const int pair = cur_b * Hkv + cur_h;
+      const int slot = blockIdx.x + pair;
+      for (int e = ctid; e < G * D; e += kConsumerWarps * 32) {
+        const int gq = e / D, d = e % D;
+        float mw[kConsumerWarps], M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) {
+          mw[w] = red_ml[(w * kHeadsPad + gq) * 2];
+          M = fmaxf(M, mw[w]);
+        }
+        const float piv = M == -INFINITY ? 0.f : M;
+        float L = 0.f, O = 0.f;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) {
+          const float f = exp2f(mw[w] - piv);
+          L += red_ml[(w * kHeadsPad + gq) * 2 + 1] * f;
+          O += red_o[((w * D) + d) * kHeadsPad + gq] * f;
+        }
+        if (whole) {
+          p.out[(static_cast<size_t>(cur_b) * p.q_heads + cur_h * G + gq) * D + d] =
+              __float2bfloat16_rn(O / L);
+        } else {
+          p.acc[(static_cast<size_t>(slot) * G + gq) * D + d] = O;
+          if (d == 0) p.stats[static_cast<size_t>(slot) * G + gq] = make_float2(M, L);
+        }
+      }
+      asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+      if (k != count - 1) {
+        n = cum[b + 1] - cum[b];
+        len = row_length(p.position, p.per_row, b, p.capacity);
+        run_first = j;
+        load_q(b, h);
+      }
+    }
+  }
+  if (aborted) {
+    // Let copies already issued land before the CTA's shared memory is released.
+    __syncwarp();
+  }
+}
+
+// One CTA per (row, KV head): merge the runs of CTAs that shared the pair.
+template <int D>
+__global__ void __launch_bounds__(128) decode_combine_kernel(const Params p) {
+  __shared__ int s_before, s_total, s_n;
+  const int pair = blockIdx.x;
+  const int b = pair / p.kv_heads, h = pair % p.kv_heads;
+  const int G = p.groups;
+  if (threadIdx.x == 0) {
+    s_before = 0;
+    s_total = 0;
+  }
+  __syncthreads();
+  int before = 0, total = 0, mine = 0;
+  for (int r = threadIdx.x; r < p.batch; r += blockDim.x) {
+    const int n = tiles_of(row_length(p.position, p.per_row, r, p.capacity));
+    total += n;
+    if (r < b) before += n;
+    if (r == b) mine = n;
+  }
+  atomicAdd(&s_before, before);
+  atomicAdd(&s_total, total);
+  if (threadIdx.x == (b % blockDim.x)) s_n = mine;
+  __syncthreads();
+  const int n = s_n;
+  const long long T = static_cast<long long>(p.kv_heads) * s_total;
+  __nv_bfloat16* out = p.out + (static_cast<size_t>(b) * p.q_heads + h * G) * D;
+  if (n == 0) {
+    for (int e = threadIdx.x; e < G * D; e += blockDim.x) out[e] = __float2bfloat16_rn(0.f);
+    return;
+  }
+  const long long first = static_cast<long long>(p.kv_heads) * s_before + static_cast<long long>(h) * n;
+  const int lo = slice_owner(T, first, p.ctas);
+  const int hi = slice_owner(T, first + n - 1, p.ctas);
+  if (lo == hi) return;  // one run covered the pair and wrote the output itself
+  for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
+    const int gq = e / D, d = e % D;
+    float M = -INFINITY;
+    for (int i = lo; i <= hi; ++i) {
+      if (slice_start(T, i, p.ctas) == slice_start(T, i + 1, p.ctas)) continue;
+      M = fmaxf(M, p.stats[static_cast<size_t>(i + pair) * G + gq].x);
+    }
+    const float piv = M == -INFINITY ? 0.f : M;
+    float L = 0.f, O = 0.f;
+    for (int i = lo; i <= hi; ++i) {
+      if (slice_start(T, i, p.ctas) == slice_start(T, i + 1, p.ctas)) continue;
+      const float2 st = p.stats[static_cast<size_t>(i + pair) * G + gq];
+      const float f = exp2f(st.x - piv);
+      L += st.y * f;
+      O += p.acc[(static_cast<size_t>(i + pair) * G + gq) * D + d] * f;
+    }
+    out[e] = __float2bfloat16_rn(O / L);
+  }
+}
+
+constexpr int kStages = 4;
+
+template <int D>
+int launch_partials(const CUtensorMap& km, const CUtensorMap& vm, const Params& p,
+                    cudaStream_t stream) {
+  using S = Smem<D, kStages>;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !configured[dev]) {
+    if (cudaFuncSetAttribute(decode_partials_kernel<D, kStages>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal) != cudaSuccess)
+      return FB_ERR_LAUNCH;
+    configured[dev] = true;
+  }
+  decode_partials_kernel<D, kStages><<<p.ctas, kThreads, S::kTotal, stream>>>(km, vm, p);
+  return check_launch();
+}
+
+int validate(int batch, int q_heads, int kv_heads, int head_dim, int capacity) {
+  if (batch <= 0 || q_heads <= 0 || kv_heads <= 0 || capacity <= 0) return FB_ERR_ARG;
+  if (head_dim != 64 && head_dim != 128) return FB_ERR_SHAPE;
+  if (q_heads % kv_heads != 0 || q_heads / kv_heads > kHeadsPad) return FB_ERR_SHAPE;
+  if (batch > kMaxBatch) return FB_ERR_SHAPE;
+  if (static_cast<long long>(batch) * kv_heads * capacity >= (1ll << 31)) return FB_ERR_SHAPE;
+  return FB_OK;
+}
+
+}  // namespace attn
+}  // namespace fb
+
+using namespace fb;
+using namespace fb::attn;
+
+extern "C" int fb_decode_attention_ctas(int batch, int kv_heads, int capacity, int head_dim) {
+  (void)batch;
+  (void)kv_heads;
+  (void)capacity;
+  (void)head_dim;
+  return sm_count();
+}
+
+extern "C" size_t fb_decode_attention_workspace(int batch, int q_heads, int kv_heads,
+                                                int head_dim, int ctas) {
+  if (batch <= 0 || q_heads <= 0 || kv_heads <= 0 || head_dim <= 0 || ctas <= 0) return 0;
+  const size_t G = q_heads / kv_heads;
+  const size_t slots = static_cast<size_t>(ctas) + static_cast<size_t>(batch) * kv_heads;
+  const size_t acc = slots * G * head_dim * sizeof(float);
+  const size_t stats = slots * G * sizeof(float2);
+  return ((acc + 255) & ~size_t(255)) + stats;
+}
+
+static int make_params(Params* p, const void* q, const int64_t* position, int per_row, void* out,
+                       void* workspace, size_t workspace_bytes, int batch, int q_heads,
+                       int kv_heads, int head_dim, int capacity, float scale, int ctas) {
+  int st = validate(batch, q_heads, kv_heads, head_dim, capacity);
+  if (st != FB_OK) return st;
+  if (position == nullptr || out == nullptr || workspace == nullptr || ctas <= 0) return FB_ERR_ARG;
+  const size_t need = fb_decode_attention_workspace(batch, q_heads, kv_heads, head_dim, ctas);
+  if (workspace_bytes < need) return FB_ERR_WORKSPACE;
+  const size_t G = q_heads / kv_heads;
+  const size_t slots = static_cast<size_t>(ctas) + static_cast<size_t>(batch) * kv_heads;
+  const size_t acc = slots * G * head_dim * sizeof(float);
+  p->q = static_cast<const __nv_bfloat16*>(q);
+  p->position = position;
+  p->per_row = per_row ? 1 : 0;
+  p->out = static_cast<__nv_bfloat16*>(out);
+  p->acc = static_cast<float*>(workspace);
+  p->stats = reinterpret_cast<float2*>(static_cast<uint8_t*>(workspace) + ((acc + 255) & ~size_t(255)));
+  p->batch = batch;
+  p->q_heads = q_heads;
+  p->kv_heads = kv_heads;
+  p->groups = q_heads / kv_heads;
+  p->capacity = capacity;
+  p->ctas = ctas;
+  p->scale_log2 = static_cast<float>(static_cast<double>(scale) * 1.4426950408889634);
+  p->err = error_word();
+  return FB_OK;
+}
+
+extern "C" int fb_decode_attention(const void* q, const void* k, const void* v,
+                                   const int64_t* position, int per_row, void* out, void* workspace,
+                                   size_t workspace_bytes, int batch, int q_heads, int kv_heads,
+                                   int head_dim, int capacity, float scale, int ctas,
+                                   void* stream) {
+  if (q == nullptr || k == nullptr || v == nullptr) return FB_ERR_ARG;
+  Params p;
+  int st = make_params(&p, q, position, per_row, out, workspace, workspace_bytes, batch, q_heads,
+                       kv_heads, head_dim, capacity, scale, ctas);
+  if (st != FB_OK) return st;
+  const uint64_t rows = static_cast<uint64_t>(batch) * kv_heads * capacity;
+  CUtensorMap km, vm;
+  st = encode_bf16_2d(&km, k, rows, head_dim, head_dim, 64, kTile, true);
+  if (st != FB_OK) return st;
+  st = encode_bf16_2d(&vm, v, rows, head_dim, head_dim, 64, kTile, true);
+  if (st != FB_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return head_dim == 128 ? launch_partials<128>(km, vm, p, s) : launch_partials<64>(km, vm, p, s);
+}
+
+extern "C" int fb_decode_attention_combine(const int64_t* position, int per_row, void* out,
+                                           void* workspace, size_t workspace_bytes, int batch,
+                                           int q_heads, int kv_heads, int head_dim, int capacity,
+                                           int ctas, void* stream) {
+  Params p;
+  int st = make_params(&p, nullptr, position, per_row, out, workspace, workspace_bytes, batch,
+                       q_heads, kv_heads, head_dim, capacity, 1.0f, ctas);
+  if (st != FB_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int pairs = batch * kv_heads;
+  if (head_dim == 128)
+    decode_combine_kernel<128><<<pairs, 128, 0, s>>>(p);
+  else
+    decode_combine_kernel<64><<<pairs, 128, 0, s>>>(p);
+  return check_launch();
+}

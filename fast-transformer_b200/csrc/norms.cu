@@ -1,0 +1,291 @@
+// RMSNorm family, SwiGLU and the split-K merge (sm_100a). All HBM/latency bound; one
+// CTA per row with 16-byte vector accesses. Cast points follow the reference:
+//   rms_norm       engine/kernels/rmsnorm.py:21-46   y = bf16(bf16(x*inv) * w)
+//   add_rms_norm   engine/kernels/rmsnorm.py:75-95   s = bf16(x+r); y = bf16(bf16(s*inv) * w)
+//   embed_rms_norm engine/kernels/rmsnorm.py:128-142 h = table[id]; y = rms_norm(h)
+//   swiglu         engine/kernels/swiglu.py:13-24    y = bf16(bf16(g/(1+exp(-g))) * u)
+//   merge          engine/kernels/linear.py:81-93    y = bf16(sum_s partial[s])
+// inv = 1/sqrt(mean(x^2) + eps) in fp32. Split-K fp32 inputs are summed in split order
+// and rounded to bf16 before use (engine/kernels/merged.py:37-45).
+#include "common.cuh"
+
+namespace fb {
+namespace norm {
+
+constexpr int kThreads = 256;
+
+// 8 consecutive logical bf16 values starting at element `off` of a tensor that is either
+// bf16 (splits == 1) or fp32 split partials [splits, count].
+__device__ __forceinline__ void load8(const void* src, int splits, size_t count, size_t off,
+                                      float (&x)[8]) {
+  if (splits == 1) {
+    const uint4 w = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(src) + off);
+    x[0] = bf16_lo(w.x);
+    x[1] = bf16_hi(w.x);
+    x[2] = bf16_lo(w.y);
+    x[3] = bf16_hi(w.y);
+    x[4] = bf16_lo(w.z);
+    x[5] = bf16_hi(w.z);
+    x[6] = bf16_lo(w.w);
+    x[7] = bf16_hi(w.w);
+    return;
+  }
+  const float* f = static_cast<const float*>(src) + off;
+  const float4 a = *reinterpret_cast<const float4*>(f);
+  const float4 b = *reinterpret_cast<const float4*>(f + 4);
+  x[0] = a.x;
+  x[1] = a.y;
+  x[2] = a.z;
+  x[3] = a.w;
+  x[4] = b.x;
+  x[5] = b.y;
+  x[6] = b.z;
+  x[7] = b.w;
+  for (int s = 1; s < splits; ++s) {
+    const float4 c = *reinterpret_cast<const float4*>(f + s * count);
+    const float4 d = *reinterpret_cast<const float4*>(f + s * count + 4);
+    x[0] += c.x;
+    x[1] += c.y;
+    x[2] += c.z;
+    x[3] += c.w;
+    x[4] += d.x;
+    x[5] += d.y;
+    x[6] += d.z;
+    x[7] += d.w;
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) x[e] = bf16_round(x[e]);
+}
+
+__device__ __forceinline__ void store8(__nv_bfloat16* dst, const float (&y)[8]) {
+  uint4 w;
+  w.x = pack_bf16x2(y[0], y[1]);
+  w.y = pack_bf16x2(y[2], y[3]);
+  w.z = pack_bf16x2(y[4], y[5]);
+  w.w = pack_bf16x2(y[6], y[7]);
+  *reinterpret_cast<uint4*>(dst) = w;
+}
+
+__device__ __forceinline__ void load_w8(const __nv_bfloat16* w, int col, float (&x)[8]) {
+  const uint4 v = *reinterpret_cast<const uint4*>(w + col);
+  x[0] = bf16_lo(v.x);
+  x[1] = bf16_hi(v.x);
+  x[2] = bf16_lo(v.y);
+  x[3] = bf16_hi(v.y);
+  x[4] = bf16_lo(v.z);
+  x[5] = bf16_hi(v.z);
+  x[6] = bf16_lo(v.w);
+  x[7] = bf16_hi(v.w);
+}
+
+__device__ __forceinline__ float block_sum(float v, float* scratch) {
+  v = warp_sum(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+  const int nw = blockDim.x >> 5;
+  for (int i = 0; i < nw; ++i) t += scratch[i];
+  __syncthreads();
+  return t;
+}
+
+// Per-thread register cache: up to kMaxChunks 8-wide chunks per thread (W <= 16384).
+constexpr int kMaxChunks = 8;
+
+// mode 0: rms_norm(x)  mode 1: add_rms_norm(x, residual)  mode 2: embed + rms_norm
+struct Params {
+  const void* x;
+  int splits;
+  int64_t row_stride;
+  const __nv_bfloat16* residual;
+  const __nv_bfloat16* w;
+  __nv_bfloat16* y;
+  __nv_bfloat16* sum;
+  const int64_t* ids;
+  int64_t vocab;
+  int rows, width;
+  float eps;
+  unsigned* err;
+};
+
+template <int MODE>
+__global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const Params p) {
+  __shared__ float scratch[kThreads / 32];
+  const int row = blockIdx.x;
+  const int chunks = p.width / 8;
+  float v[kMaxChunks][8];
+  const void* src = p.x;
+  size_t base = static_cast<size_t>(row) * p.width;
+  if (MODE == 0) base = static_cast<size_t>(row) * p.row_stride;
+  if (MODE == 2) {
+    const long long id = p.ids[row];
+    if (id < 0 || id >= p.vocab) {
+      if (threadIdx.x == 0) raise_error(p.err, kErrBadShape);
+      return;
+    }
+    base = static_cast<size_t>(id) * p.width;
+  }
+  const size_t count = static_cast<size_t>(p.rows) * p.width;
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxChunks; ++i) {
+    const int ch = threadIdx.x + i * kThreads;
+    if (ch < chunks) {
+      load8(src, MODE == 1 ? p.splits : 1, count, base + ch * 8, v[i]);
+      if (MODE == 1) {
+        float r[8];
+        load8(p.residual, 1, 0, static_cast<size_t>(row) * p.width + ch * 8, r);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[i][e] = bf16_round(v[i][e] + r[e]);
+        store8(p.sum + static_cast<size_t>(row) * p.width + ch * 8, v[i]);
+      }
+      if (MODE == 2) store8(p.sum + static_cast<size_t>(row) * p.width + ch * 8, v[i]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += v[i][e] * v[i][e];
+    }
+  }
+  ss = block_sum(ss, scratch);
+  const float inv = 1.0f / sqrtf(ss / static_cast<float>(p.width) + p.eps);
+#pragma unroll
+  for (int i = 0; i < kMaxChunks; ++i) {
+    const int ch = threadIdx.x + i * kThreads;
+    if (ch < chunks) {
+      float w[8], y[8];
+      load_w8(p.w, ch * 8, w);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) y[e] = bf16_round(v[i][e] * inv) * w[e];
+      const size_t out = (MODE == 0 ? static_cast<size_t>(row) * p.row_stride
+                                    : static_cast<size_t>(row) * p.width) +
+                         ch * 8;
+      store8(p.y + out, y);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads)
+    swiglu_kernel(const void* packed, int splits, __nv_bfloat16* out, int rows, int width) {
+  const int row = blockIdx.y;
+  const int ch = blockIdx.x * kThreads + threadIdx.x;
+  if (ch * 8 >= width) return;
+  const size_t count = static_cast<size_t>(rows) * 2 * width;
+  const size_t base = static_cast<size_t>(row) * 2 * width + ch * 8;
+  float g[8], u[8], y[8];
+  load8(packed, splits, count, base, g);
+  load8(packed, splits, count, base + width, u);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float act = bf16_round(g[e] / (1.0f + expf(-g[e])));
+    y[e] = act * u[e];
+  }
+  store8(out + static_cast<size_t>(row) * width + ch * 8, y);
+}
+
+__global__ void __launch_bounds__(kThreads)
+    merge_kernel(const float* partial, int splits, int64_t count, void* out, int out_fp32) {
+  const int64_t i = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) * 4;
+  if (i >= count) return;
+  float x[4];
+  const int n = count - i < 4 ? static_cast<int>(count - i) : 4;
+  for (int e = 0; e < n; ++e) x[e] = partial[i + e];
+  for (int s = 1; s < splits; ++s)
+    for (int e = 0; e < n; ++e) x[e] += partial[s * count + i + e];
+  if (out_fp32) {
+    for (int e = 0; e < n; ++e) static_cast<float*>(out)[i + e] = x[e];
+  } else {
+    for (int e = 0; e < n; ++e) static_cast<__nv_bfloat16*>(out)[i + e] = __float2bfloat16_rn(x[e]);
+  }
+}
+
+int check_width(int width) {
+  if (width <= 0 || width % 8 != 0) return FB_ERR_SHAPE;
+  if (width > 8 * kThreads * kMaxChunks) return FB_ERR_SHAPE;
+  return FB_OK;
+}
+
+}  // namespace norm
+}  // namespace fb
+
+using namespace fb;
+
+extern "C" int fb_rmsnorm(const void* x, int64_t row_stride, const void* w, void* y, int rows,
+                          int width, float eps, void* stream) {
+  if (!x || !w || !y || rows <= 0 || row_stride < width) return FB_ERR_ARG;
+  int st = norm::check_width(width);
+  if (st != FB_OK) return st;
+  if (row_stride % 8 != 0) return FB_ERR_SHAPE;
+  norm::Params p{};
+  p.x = x;
+  p.splits = 1;
+  p.row_stride = row_stride;
+  p.w = static_cast<const __nv_bfloat16*>(w);
+  p.y = static_cast<__nv_bfloat16*>(y);
+  p.rows = rows;
+  p.width = width;
+  p.eps = eps;
+  p.err = error_word();
+  norm::rmsnorm_kernel<0><<<rows, norm::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  return check_launch();
+}
+
+extern "C" int fb_add_rmsnorm(const void* x, int x_splits, const void* residual, const void* w,
+                              void* out, void* sum, int rows, int width, float eps, void* stream) {
+  if (!x || !residual || !w || !out || !sum || rows <= 0 || x_splits <= 0) return FB_ERR_ARG;
+  int st = norm::check_width(width);
+  if (st != FB_OK) return st;
+  norm::Params p{};
+  p.x = x;
+  p.splits = x_splits;
+  p.residual = static_cast<const __nv_bfloat16*>(residual);
+  p.w = static_cast<const __nv_bfloat16*>(w);
+  p.y = static_cast<__nv_bfloat16*>(out);
+  p.sum = static_cast<__nv_bfloat16*>(sum);
+  p.rows = rows;
+  p.width = width;
+  p.eps = eps;
+  p.err = error_word();
+  norm::rmsnorm_kernel<1><<<rows, norm::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  return check_launch();
+}
+
+extern "C" int fb_embed_rmsnorm(const int64_t* ids, const void* table, int64_t vocab, const void* w,
+                                void* y, void* hidden, int rows, int width, float eps,
+                                void* stream) {
+  if (!ids || !table || !w || !y || !hidden || rows <= 0 || vocab <= 0) return FB_ERR_ARG;
+  int st = norm::check_width(width);
+  if (st != FB_OK) return st;
+  norm::Params p{};
+  p.x = table;
+  p.splits = 1;
+  p.w = static_cast<const __nv_bfloat16*>(w);
+  p.y = static_cast<__nv_bfloat16*>(y);
+  p.sum = static_cast<__nv_bfloat16*>(hidden);
+  p.ids = ids;
+  p.vocab = vocab;
+  p.rows = rows;
+  p.width = width;
+  p.eps = eps;
+  p.err = error_word();
+  norm::rmsnorm_kernel<2><<<rows, norm::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  return check_launch();
+}
+
+extern "C" int fb_swiglu(const void* packed, int splits, void* out, int rows, int width,
+                         void* stream) {
+  if (!packed || !out || rows <= 0 || splits <= 0 || width <= 0) return FB_ERR_ARG;
+  if (width % 8 != 0 || rows > 65535) return FB_ERR_SHAPE;
+  dim3 grid((width / 8 + norm::kThreads - 1) / norm::kThreads, rows);
+  norm::swiglu_kernel<<<grid, norm::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      packed, splits, static_cast<__nv_bfloat16*>(out), rows, width);
+  return check_launch();
+}
+
+extern "C" int fb_merge_splits(const void* partial, int splits, int64_t count, void* out,
+                               int out_fp32, void* stream) {
+  if (!partial || !out || splits <= 0 || count <= 0) return FB_ERR_ARG;
+  const int64_t threads = (count + 3) / 4;
+  const int blocks = static_cast<int>((threads + norm::kThreads - 1) / norm::kThreads);
+  norm::merge_kernel<<<blocks, norm::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const float*>(partial), splits, count, out, out_fp32);
+  return check_launch();
+}

@@ -1,0 +1,205 @@
+// Fused per-head Q/K RMSNorm + rotate-half RoPE + KV-cache append (sm_100a).
+//
+// Arithmetic and cast points follow the reference kernel `_qk_rope_cache`
+// (engine/kernels/qk_rope.py:13-84):
+//   inv  = 1 / sqrt(mean(x^2) + eps)            fp32 (:34-36)
+//   n    = bf16(x * inv); w = bf16(n * gain)    (:45-48)
+//   rot  = [-w[D/2:], w[:D/2]]                  (:49)
+//   out  = bf16(bf16(w * cos) + bf16(rot * sin)) both products rounded (:62-66)
+// Q heads go to a token-major [B, T, Hq, D] buffer (:67-68); K heads and the matching V
+// heads (copied unchanged, :82-84) go to the cache slot of each token (:70-81).
+// Split-K fp32 inputs are summed in split order, then rounded (merged.py:37-45).
+//
+// One warp per (token row, head); each lane owns D/32 consecutive dims, so the
+// rotate-half partner of a lane's dims sits in lane ^ 16 and one shuffle pairs them.
+#include "common.cuh"
+
+namespace fb {
+namespace rope {
+
+struct Params {
+  const void* packed;
+  int splits;
+  const __nv_bfloat16* q_weight;
+  const __nv_bfloat16* k_weight;
+  float q_eps, k_eps;
+  const __nv_bfloat16* cos;
+  const __nv_bfloat16* sin;
+  const int64_t* position;
+  const int64_t* phases;
+  __nv_bfloat16* query;
+  __nv_bfloat16* keys;
+  __nv_bfloat16* values;
+  int batch, tokens, q_heads, kv_heads, capacity, mode, table;
+  unsigned* err;
+};
+
+// Loads E consecutive packed values at element offset `off` as fp32 holding bf16 values.
+template <int E>
+__device__ __forceinline__ void load_packed(const Params& p, size_t off, size_t split_stride,
+                                            float (&x)[E]) {
+  if (p.splits == 1) {
+    const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(p.packed) + off;
+    if constexpr (E == 4) {
+      uint2 w = *reinterpret_cast<const uint2*>(src);
+      x[0] = bf16_lo(w.x);
+      x[1] = bf16_hi(w.x);
+      x[2] = bf16_lo(w.y);
+      x[3] = bf16_hi(w.y);
+    } else {
+      uint32_t w = *reinterpret_cast<const uint32_t*>(src);
+      x[0] = bf16_lo(w);
+      x[1] = bf16_hi(w);
+    }
+  } else {
+    const float* src = static_cast<const float*>(p.packed) + off;
+#pragma unroll
+    for (int e = 0; e < E; ++e) x[e] = src[e];
+    for (int s = 1; s < p.splits; ++s) {
+#pragma unroll
+      for (int e = 0; e < E; ++e) x[e] += src[s * split_stride + e];
+    }
+#pragma unroll
+    for (int e = 0; e < E; ++e) x[e] = bf16_round(x[e]);
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(128) qk_rope_kernel(const Params p) {
+  constexpr int E = D / 32;
+  const int warp_global = blockIdx.x * 4 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int heads = p.q_heads + p.kv_heads;
+  const int rows = p.batch * p.tokens;
+  if (warp_global >= rows * heads) return;
+  const int row = warp_global / heads;
+  const int head = warp_global % heads;
+  const int b = row / p.tokens;
+  const int t = row % p.tokens;
+  const int width = (p.q_heads + 2 * p.kv_heads) * D;
+  const size_t split_stride = static_cast<size_t>(rows) * width;
+  const int d0 = lane * E;
+
+  float x[E];
+  load_packed<E>(p, static_cast<size_t>(row) * width + head * D + d0, split_stride, x);
+  float ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < E; ++e) ss += x[e] * x[e];
+  ss = warp_sum(ss);
+  const bool is_q = head < p.q_heads;
+  const float eps = is_q ? p.q_eps : p.k_eps;
+  const float inv = 1.0f / sqrtf(ss / static_cast<float>(D) + eps);
+  const __nv_bfloat16* gain = is_q ? p.q_weight : p.k_weight;
+
+  float w[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const float n = bf16_round(x[e] * inv);
+    w[e] = bf16_round(n * __bfloat162float(gain[d0 + e]));
+  }
+  // Rotate-half partner: dims (d + D/2) mod D live in lane ^ 16.
+  float partner[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) partner[e] = __shfl_xor_sync(0xffffffffu, w[e], 16);
+  const bool low_half = lane < 16;
+
+  long long phase;
+  if (p.table) {
+    phase = p.position[b] + p.phases[row];
+  } else {
+    phase = p.mode == 2 ? row : t;
+  }
+  const __nv_bfloat16* cs = p.cos + phase * D + d0;
+  const __nv_bfloat16* sn = p.sin + phase * D + d0;
+  float y[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const float rot = low_half ? -partner[e] : partner[e];
+    const float direct = bf16_round(w[e] * __bfloat162float(cs[e]));
+    const float turn = bf16_round(rot * __bfloat162float(sn[e]));
+    y[e] = direct + turn;  // rounded once more by the bf16 store below
+  }
+
+  __nv_bfloat16 outv[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) outv[e] = __float2bfloat16_rn(y[e]);
+  if (is_q) {
+    __nv_bfloat16* dst = p.query + (static_cast<size_t>(row) * p.q_heads + head) * D + d0;
+#pragma unroll
+    for (int e = 0; e < E; ++e) dst[e] = outv[e];
+    return;
+  }
+  const int kvh = head - p.q_heads;
+  long long pos;
+  if (p.mode == 1)
+    pos = t;
+  else if (p.mode == 2)
+    pos = p.position[b] + t;
+  else
+    pos = p.position[0] + t;
+  if (pos < 0 || pos >= p.capacity) {
+    if (lane == 0) raise_error(p.err, kErrBadShape);
+    return;
+  }
+  const size_t slot = ((static_cast<size_t>(b) * p.kv_heads + kvh) * p.capacity + pos) * D + d0;
+#pragma unroll
+  for (int e = 0; e < E; ++e) p.keys[slot + e] = outv[e];
+  float v[E];
+  load_packed<E>(p, static_cast<size_t>(row) * width + (p.q_heads + p.kv_heads + kvh) * D + d0,
+                 split_stride, v);
+#pragma unroll
+  for (int e = 0; e < E; ++e) p.values[slot + e] = __float2bfloat16_rn(v[e]);
+}
+
+}  // namespace rope
+}  // namespace fb
+
+using namespace fb;
+
+extern "C" int fb_qk_norm_rope_append(const void* packed, int packed_splits, const void* q_weight,
+                                      const void* k_weight, float q_eps, float k_eps,
+                                      const void* cos, const void* sin, const int64_t* position,
+                                      const int64_t* phases, void* query, void* keys, void* values,
+                                      int batch, int tokens, int q_heads, int kv_heads,
+                                      int head_dim, int capacity, int mode, int table,
+                                      void* stream) {
+  if (!packed || !q_weight || !k_weight || !cos || !sin || !position || !query || !keys ||
+      !values)
+    return FB_ERR_ARG;
+  if (batch <= 0 || tokens <= 0 || q_heads <= 0 || kv_heads <= 0 || capacity <= 0 ||
+      packed_splits <= 0)
+    return FB_ERR_ARG;
+  if (mode < 0 || mode > 2 || (table && (mode != 2 || phases == nullptr))) return FB_ERR_ARG;
+  if (head_dim != 64 && head_dim != 128) return FB_ERR_SHAPE;
+  if (tokens > capacity) return FB_ERR_SHAPE;
+  rope::Params p;
+  p.packed = packed;
+  p.splits = packed_splits;
+  p.q_weight = static_cast<const __nv_bfloat16*>(q_weight);
+  p.k_weight = static_cast<const __nv_bfloat16*>(k_weight);
+  p.q_eps = q_eps;
+  p.k_eps = k_eps;
+  p.cos = static_cast<const __nv_bfloat16*>(cos);
+  p.sin = static_cast<const __nv_bfloat16*>(sin);
+  p.position = position;
+  p.phases = phases;
+  p.query = static_cast<__nv_bfloat16*>(query);
+  p.keys = static_cast<__nv_bfloat16*>(keys);
+  p.values = static_cast<__nv_bfloat16*>(values);
+  p.batch = batch;
+  p.tokens = tokens;
+  p.q_heads = q_heads;
+  p.kv_heads = kv_heads;
+  p.capacity = capacity;
+  p.mode = mode;
+  p.table = table ? 1 : 0;
+  p.err = error_word();
+  const long long warps = static_cast<long long>(batch) * tokens * (q_heads + kv_heads);
+  const int blocks = static_cast<int>((warps + 3) / 4);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (head_dim == 128)
+    rope::qk_rope_kernel<128><<<blocks, 128, 0, s>>>(p);
+  else
+    rope::qk_rope_kernel<64><<<blocks, 128, 0, s>>>(p);
+  return check_launch();
+}

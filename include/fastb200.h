@@ -1,0 +1,163 @@
+/*
+ * fastb200.h - C ABI of libfastb200.so, the sm_100a (B200) decode hot path of
+ * john-jpet/fast-transformer.
+ *
+ * Conventions shared by every entry point:
+ *  - All pointers are DEVICE pointers unless the name says host. Tensors are dense,
+ *    row-major, in the layouts documented per function (the reference's layouts).
+ *  - `stream` is a cudaStream_t (passed as void* so this header needs no CUDA include).
+ *    Every entry point only enqueues work on that stream: no allocation, no host
+ *    synchronisation, no device->host read. All of them may be captured in a CUDA graph.
+ *  - Return value: FB_OK (0) or a negative status. Arguments are validated on the host
+ *    before anything is launched; a failing call launches nothing.
+ *  - Device-side waits are bounded. A wait that gives up sets a bit in the library's
+ *    device error word and the kernel returns; fb_device_error() reads and clears it.
+ *
+ * bf16 = IEEE bfloat16 stored as uint16; fp32 = IEEE binary32; int64 = int64_t.
+ */
+#ifndef FASTB200_H_
+#define FASTB200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FB_OK 0
+#define FB_ERR_ARG (-1)         /* null pointer, negative size, bad enum */
+#define FB_ERR_SHAPE (-2)       /* shape outside what the kernels support */
+#define FB_ERR_LAUNCH (-3)      /* cudaGetLastError() after the launch */
+#define FB_ERR_DRIVER (-4)      /* tensor-map encoder unavailable / refused the map */
+#define FB_ERR_WORKSPACE (-5)   /* workspace smaller than the *_workspace() size */
+
+/* Library version, for the Python loader's sanity check. */
+int fb_version(void);
+
+/* Reads the device error word of the current device into *host_flags and clears it.
+ * Synchronises the device; call it between steps, never inside a capture. */
+int fb_device_error(unsigned int* host_flags);
+
+/* ------------------------------------------------------------------------------------
+ * Split-KV GQA decode attention (one query token per row).
+ * Replaces engine/kernels/decode_attention.py:238-257 `decode_attention`, whose body
+ * `_attend` (:130-149) launches `_decode_partials` (:31-101) then `_decode_merge`
+ * (:104-127).
+ *
+ *   q        bf16 [B, Hq, D]          (the reference's [B, Hq, 1, D])
+ *   k, v     bf16 [B, Hkv, C, D]      (one layer's cache, contiguous)
+ *   position int64: per_row == 0 -> [1], all rows attend slots [0, position[0]];
+ *                   per_row == 1 -> [B], row b attends slots [0, position[b]].
+ *            (the reference's scalar form is :246; the per-row form is the
+ *             ragged-batch extension of the same rule, valid = position + 1, :48.)
+ *   out      bf16 [B, Hq, D]          (the reference's [B, 1, Hq, D])
+ *   D in {64, 128}; G = Hq / Hkv in [1, 8].
+ *
+ * The work is a persistent grid of `ctas` CTAs that split the valid tokens of all
+ * (row, KV head) pairs evenly (64-token tiles). fb_decode_attention_ctas() gives the
+ * default CTA count; fb_decode_attention_workspace() the workspace bytes for a count.
+ * fb_decode_attention writes partials; fb_decode_attention_combine merges them into out
+ * (the log-sum-exp combine). Both must be called with the same arguments and `ctas`.
+ * ---------------------------------------------------------------------------------- */
+int fb_decode_attention_ctas(int batch, int kv_heads, int capacity, int head_dim);
+size_t fb_decode_attention_workspace(int batch, int q_heads, int kv_heads, int head_dim, int ctas);
+int fb_decode_attention(const void* q, const void* k, const void* v, const int64_t* position,
+                        int per_row, void* out, void* workspace, size_t workspace_bytes, int batch,
+                        int q_heads, int kv_heads, int head_dim, int capacity, float scale, int ctas,
+                        void* stream);
+int fb_decode_attention_combine(const int64_t* position, int per_row, void* out, void* workspace,
+                                size_t workspace_bytes, int batch, int q_heads, int kv_heads,
+                                int head_dim, int capacity, int ctas, void* stream);
+
+/* ------------------------------------------------------------------------------------
+ * Fused per-head Q/K RMSNorm + rotate-half RoPE + KV-cache append.
+ * Replaces engine/kernels/qk_rope.py:87-129 `qk_rope_cache` (kernel `_qk_rope_cache`
+ * :13-84), same cast points: bf16(x * rsqrt(mean(x^2) + eps)) -> bf16(* gain) ->
+ * bf16(bf16(w * cos) + bf16(rot(w) * sin)).
+ *
+ *   packed   bf16 [B*T, (Hq + 2 Hkv) * D] when packed_splits == 1, else fp32 split-K
+ *            partials [packed_splits, B*T, (Hq + 2 Hkv) * D] (summed in split order,
+ *            then rounded to bf16: engine/kernels/merged.py:37-45)
+ *   q_weight, k_weight bf16 [D]
+ *   cos, sin bf16: table == 0 -> [rows_of_phase, D] where the phase row of token
+ *            (b, t) is t (mode 0/1) or b*T + t (mode 2);
+ *            table == 1 -> whole tables [>= C, D], phase row position[b] + phases[b,t]
+ *   position int64: mode 0 (decode)  [1], token t of every row -> slot position[0] + t
+ *                   mode 1 (prefill) [T] (unused values), token t -> slot t
+ *                   mode 2 (rows)    [B], token t of row b -> slot position[b] + t
+ *   phases   int64 [B, T] (table == 1 only, else may be NULL)
+ *   query    bf16 [B, T, Hq, D]       (token-major Q output)
+ *   keys, values bf16 [B, Hkv, C, D]  (written in place at the slots above)
+ * ---------------------------------------------------------------------------------- */
+int fb_qk_norm_rope_append(const void* packed, int packed_splits, const void* q_weight,
+                           const void* k_weight, float q_eps, float k_eps, const void* cos,
+                           const void* sin, const int64_t* position, const int64_t* phases,
+                           void* query, void* keys, void* values, int batch, int tokens,
+                           int q_heads, int kv_heads, int head_dim, int capacity, int mode,
+                           int table, void* stream);
+
+/* ------------------------------------------------------------------------------------
+ * RMSNorm family. Replace engine/kernels/rmsnorm.py:
+ *   fb_rmsnorm        <- `rms_norm` :49-72 (kernel :21-46): y = bf16(bf16(x*rsqrt) * w)
+ *   fb_add_rmsnorm    <- `add_rms_norm` :98-125 (kernel :75-95):
+ *                        sum = bf16(x + residual); out = bf16(bf16(sum*rsqrt) * w)
+ *                        x is bf16 [rows, W] (x_splits == 1) or fp32 split partials
+ *                        [x_splits, rows, W].
+ *   fb_embed_rmsnorm  <- `embed_rms_norm` :145-162 (kernel :128-142): hidden = table[ids];
+ *                        y = rmsnorm(hidden)
+ * x/y/residual/out/sum bf16 [rows, W] contiguous (fb_rmsnorm: rows at `row_stride`
+ * elements), w bf16 [W]. W <= 16384 and W % 8 == 0.
+ * ---------------------------------------------------------------------------------- */
+int fb_rmsnorm(const void* x, int64_t row_stride, const void* w, void* y, int rows, int width,
+               float eps, void* stream);
+int fb_add_rmsnorm(const void* x, int x_splits, const void* residual, const void* w, void* out,
+                   void* sum, int rows, int width, float eps, void* stream);
+int fb_embed_rmsnorm(const int64_t* ids, const void* table, int64_t vocab, const void* w, void* y,
+                     void* hidden, int rows, int width, float eps, void* stream);
+
+/* ------------------------------------------------------------------------------------
+ * SwiGLU. Replaces engine/kernels/swiglu.py:27-40 (kernel `_swiglu` :13-24):
+ * out = bf16(bf16(g / (1 + exp(-g))) * u) for packed [.., 2I] = [gate | up].
+ *   packed bf16 [rows, 2I] (splits == 1) or fp32 partials [splits, rows, 2I]
+ *   out    bf16 [rows, I]; I % 8 == 0.
+ * ---------------------------------------------------------------------------------- */
+int fb_swiglu(const void* packed, int splits, void* out, int rows, int width, void* stream);
+
+/* ------------------------------------------------------------------------------------
+ * Skinny bf16 projection y = x @ W^T with fp32 accumulation.
+ * Replaces engine/kernels/linear.py:489-523 `linear` for rows <= 64 (the reference's
+ * Triton kinds, linear.py:27-93 and gemm.py:51-425); larger row counts stay on cuBLAS
+ * exactly as the reference does (linear.py:492-493).
+ *   x   bf16 [M, K], W bf16 [N, K] (both contiguous, K % 64 == 0, N % 8 == 0), M <= 64
+ *   out: splits == 1 and out_fp32 == 0 -> bf16 [M, N] (one rounding)
+ *        otherwise fp32 partials [splits, M, N] (split s covers K range
+ *        [s*K/splits, (s+1)*K/splits) in 64-wide chunks; consumers sum then round,
+ *        engine/kernels/merged.py:13-45)
+ * fb_linear_splits() is the default split count for a shape on the current device.
+ * ---------------------------------------------------------------------------------- */
+int fb_linear_splits(int m, int n, int k);
+int fb_linear(const void* x, const void* w, void* out, int m, int n, int k, int splits,
+              int out_fp32, void* stream);
+
+/* Sums fp32 split partials [splits, count] into bf16 [count] (or fp32 when out_fp32):
+ * the reference's `_merge_projection` (linear.py:81-93). */
+int fb_merge_splits(const void* partial, int splits, int64_t count, void* out, int out_fp32,
+                    void* stream);
+
+/* ------------------------------------------------------------------------------------
+ * First-index argmax over bf16 logits. Replaces engine/kernels/argmax.py:51-70 `argmax`
+ * (kernels `_block_argmax` :19-33 and `_first_best` :36-48): ties resolve to the lowest
+ * index, as torch.argmax.
+ *   logits bf16 [rows, vocab]; out int64 [rows]; top fp32 [rows] or NULL (winning logit).
+ *   workspace: fb_argmax_workspace(rows, vocab) bytes.
+ * ---------------------------------------------------------------------------------- */
+size_t fb_argmax_workspace(int rows, int64_t vocab);
+int fb_argmax(const void* logits, int rows, int64_t vocab, int64_t* out, float* top,
+              void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FASTB200_H_ */
