@@ -78,10 +78,11 @@ struct Smem {
   static constexpr int kStagesBytes = NS * kStageBytes;
   static constexpr int kRedO = kConsumerWarps * D * kHeadsPad * 4;  // O^T partials per warp
   static constexpr int kRedML = kConsumerWarps * kHeadsPad * 2 * 4;
-  static constexpr int kCum = (kMaxBatch + 1) * 4;
+  static constexpr int kCum = ((kMaxBatch + 1) * 4 + 15) & ~15;  // keeps the mbarriers 8-byte aligned
   static constexpr int kBars = 2 * NS * 8;
   static constexpr int kMisc = 64;
   static constexpr int kTotal = 1024 + kStagesBytes + kRedO + kRedML + kCum + kBars + kMisc;
+  static_assert((kStagesBytes + kRedO + kRedML + kCum) % 16 == 0, "mbarrier alignment");
 };
 
 template <int D, int NS>
@@ -407,28 +408,37 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// One CTA per (row, KV head): merge the runs of CTAs that shared the pair.
+// One CTA per (row, KV head): merge the runs of the CTAs that shared the pair. The
+// contributing CTAs and their per-head softmax weights exp2(m_run - M) are resolved once
+// into shared memory; the weighted sum over runs is then a coalesced sweep over the
+// partial accumulators, in increasing CTA order (deterministic).
+constexpr int kMaxCtas = 512;
+constexpr int kCombineThreads = 256;
+
 template <int D>
-__global__ void __launch_bounds__(128) decode_combine_kernel(const Params p) {
+__global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const Params p) {
   __shared__ int s_before, s_total, s_n;
+  __shared__ unsigned char s_ok[kMaxCtas];
+  __shared__ float s_w[kMaxCtas * kHeadsPad];
+  __shared__ float s_den[kHeadsPad];
   const int pair = blockIdx.x;
   const int b = pair / p.kv_heads, h = pair % p.kv_heads;
   const int G = p.groups;
   if (threadIdx.x == 0) {
     s_before = 0;
     s_total = 0;
+    s_n = 0;
   }
   __syncthreads();
-  int before = 0, total = 0, mine = 0;
+  int before = 0, total = 0;
   for (int r = threadIdx.x; r < p.batch; r += blockDim.x) {
     const int n = tiles_of(row_length(p.position, p.per_row, r, p.capacity));
     total += n;
     if (r < b) before += n;
-    if (r == b) mine = n;
+    if (r == b) s_n = n;
   }
-  atomicAdd(&s_before, before);
-  atomicAdd(&s_total, total);
-  if (threadIdx.x == (b % blockDim.x)) s_n = mine;
+  if (before) atomicAdd(&s_before, before);
+  if (total) atomicAdd(&s_total, total);
   __syncthreads();
   const int n = s_n;
   const long long T = static_cast<long long>(p.kv_heads) * s_total;
@@ -441,23 +451,40 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const Params p) {
   const int lo = slice_owner(T, first, p.ctas);
   const int hi = slice_owner(T, first + n - 1, p.ctas);
   if (lo == hi) return;  // one run covered the pair and wrote the output itself
-  for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
-    const int gq = e / D, d = e % D;
+  const int runs = hi - lo + 1;
+  // A CTA between lo and hi whose slice is empty wrote nothing for this pair.
+  for (int i = threadIdx.x; i < runs; i += blockDim.x)
+    s_ok[i] = slice_start(T, lo + i, p.ctas) < slice_start(T, lo + i + 1, p.ctas);
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int g = warp; g < G; g += kCombineThreads / 32) {
     float M = -INFINITY;
-    for (int i = lo; i <= hi; ++i) {
-      if (slice_start(T, i, p.ctas) == slice_start(T, i + 1, p.ctas)) continue;
-      M = fmaxf(M, p.stats[static_cast<size_t>(i + pair) * G + gq].x);
-    }
+    for (int i = lane; i < runs; i += 32)
+      if (s_ok[i]) M = fmaxf(M, p.stats[static_cast<size_t>(lo + i + pair) * G + g].x);
+    M = warp_max(M);
     const float piv = M == -INFINITY ? 0.f : M;
-    float L = 0.f, O = 0.f;
-    for (int i = lo; i <= hi; ++i) {
-      if (slice_start(T, i, p.ctas) == slice_start(T, i + 1, p.ctas)) continue;
-      const float2 st = p.stats[static_cast<size_t>(i + pair) * G + gq];
-      const float f = exp2f(st.x - piv);
-      L += st.y * f;
-      O += p.acc[(static_cast<size_t>(i + pair) * G + gq) * D + d] * f;
+    float L = 0.f;
+    for (int i = lane; i < runs; i += 32) {
+      float w = 0.f;
+      if (s_ok[i]) {
+        const float2 st = p.stats[static_cast<size_t>(lo + i + pair) * G + g];
+        w = exp2f(st.x - piv);
+        L += st.y * w;
+      }
+      s_w[i * kHeadsPad + g] = w;
     }
-    out[e] = __float2bfloat16_rn(O / L);
+    L = warp_sum(L);
+    if (lane == 0) s_den[g] = L;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
+    const int g = e / D, d = e % D;
+    const float* acc = p.acc + (static_cast<size_t>(lo + pair) * G + g) * D + d;
+    const size_t stride = static_cast<size_t>(G) * D;
+    float O = 0.f;
+    for (int i = 0; i < runs; ++i)
+      if (s_ok[i]) O += acc[i * stride] * s_w[i * kHeadsPad + g];
+    out[e] = __float2bfloat16_rn(O / s_den[g]);
   }
 }
 
@@ -519,6 +546,7 @@ static int make_params(Params* p, const void* q, const int64_t* position, int pe
   int st = validate(batch, q_heads, kv_heads, head_dim, capacity);
   if (st != FB_OK) return st;
   if (position == nullptr || out == nullptr || workspace == nullptr || ctas <= 0) return FB_ERR_ARG;
+  if (ctas > kMaxCtas) return FB_ERR_SHAPE;
   const size_t need = fb_decode_attention_workspace(batch, q_heads, kv_heads, head_dim, ctas);
   if (workspace_bytes < need) return FB_ERR_WORKSPACE;
   const size_t G = q_heads / kv_heads;
@@ -572,8 +600,8 @@ extern "C" int fb_decode_attention_combine(const int64_t* position, int per_row,
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int pairs = batch * kv_heads;
   if (head_dim == 128)
-    decode_combine_kernel<128><<<pairs, 128, 0, s>>>(p);
+    decode_combine_kernel<128><<<pairs, kCombineThreads, 0, s>>>(p);
   else
-    decode_combine_kernel<64><<<pairs, 128, 0, s>>>(p);
+    decode_combine_kernel<64><<<pairs, kCombineThreads, 0, s>>>(p);
   return check_launch();
 }

@@ -15,10 +15,10 @@ namespace norm {
 constexpr int kThreads = 256;
 
 // 8 consecutive logical bf16 values starting at element `off` of a tensor that is either
-// bf16 (splits == 1) or fp32 split partials [splits, count].
+// bf16 (splits == 0) or fp32 split partials [splits, count] (splits >= 1).
 __device__ __forceinline__ void load8(const void* src, int splits, size_t count, size_t off,
                                       float (&x)[8]) {
-  if (splits == 1) {
+  if (splits == 0) {
     const uint4 w = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(src) + off);
     x[0] = bf16_lo(w.x);
     x[1] = bf16_hi(w.x);
@@ -132,10 +132,10 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const Params p) {
   for (int i = 0; i < kMaxChunks; ++i) {
     const int ch = threadIdx.x + i * kThreads;
     if (ch < chunks) {
-      load8(src, MODE == 1 ? p.splits : 1, count, base + ch * 8, v[i]);
+      load8(src, MODE == 1 ? p.splits : 0, count, base + ch * 8, v[i]);
       if (MODE == 1) {
         float r[8];
-        load8(p.residual, 1, 0, static_cast<size_t>(row) * p.width + ch * 8, r);
+        load8(p.residual, 0, 0, static_cast<size_t>(row) * p.width + ch * 8, r);
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[i][e] = bf16_round(v[i][e] + r[e]);
         store8(p.sum + static_cast<size_t>(row) * p.width + ch * 8, v[i]);
@@ -165,9 +165,11 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const Params p) {
 
 __global__ void __launch_bounds__(kThreads)
     swiglu_kernel(const void* packed, int splits, __nv_bfloat16* out, int rows, int width) {
-  const int row = blockIdx.y;
-  const int ch = blockIdx.x * kThreads + threadIdx.x;
-  if (ch * 8 >= width) return;
+  const int64_t flat = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  const int per_row = width / 8;
+  if (flat >= static_cast<int64_t>(rows) * per_row) return;
+  const int row = static_cast<int>(flat / per_row);
+  const int ch = static_cast<int>(flat % per_row);
   const size_t count = static_cast<size_t>(rows) * 2 * width;
   const size_t base = static_cast<size_t>(row) * 2 * width + ch * 8;
   float g[8], u[8], y[8];
@@ -216,7 +218,7 @@ extern "C" int fb_rmsnorm(const void* x, int64_t row_stride, const void* w, void
   if (row_stride % 8 != 0) return FB_ERR_SHAPE;
   norm::Params p{};
   p.x = x;
-  p.splits = 1;
+  p.splits = 0;
   p.row_stride = row_stride;
   p.w = static_cast<const __nv_bfloat16*>(w);
   p.y = static_cast<__nv_bfloat16*>(y);
@@ -230,7 +232,7 @@ extern "C" int fb_rmsnorm(const void* x, int64_t row_stride, const void* w, void
 
 extern "C" int fb_add_rmsnorm(const void* x, int x_splits, const void* residual, const void* w,
                               void* out, void* sum, int rows, int width, float eps, void* stream) {
-  if (!x || !residual || !w || !out || !sum || rows <= 0 || x_splits <= 0) return FB_ERR_ARG;
+  if (!x || !residual || !w || !out || !sum || rows <= 0 || x_splits < 0) return FB_ERR_ARG;
   int st = norm::check_width(width);
   if (st != FB_OK) return st;
   norm::Params p{};
@@ -256,7 +258,7 @@ extern "C" int fb_embed_rmsnorm(const int64_t* ids, const void* table, int64_t v
   if (st != FB_OK) return st;
   norm::Params p{};
   p.x = table;
-  p.splits = 1;
+  p.splits = 0;
   p.w = static_cast<const __nv_bfloat16*>(w);
   p.y = static_cast<__nv_bfloat16*>(y);
   p.sum = static_cast<__nv_bfloat16*>(hidden);
@@ -272,10 +274,12 @@ extern "C" int fb_embed_rmsnorm(const int64_t* ids, const void* table, int64_t v
 
 extern "C" int fb_swiglu(const void* packed, int splits, void* out, int rows, int width,
                          void* stream) {
-  if (!packed || !out || rows <= 0 || splits <= 0 || width <= 0) return FB_ERR_ARG;
-  if (width % 8 != 0 || rows > 65535) return FB_ERR_SHAPE;
-  dim3 grid((width / 8 + norm::kThreads - 1) / norm::kThreads, rows);
-  norm::swiglu_kernel<<<grid, norm::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+  if (!packed || !out || rows <= 0 || splits < 0 || width <= 0) return FB_ERR_ARG;
+  if (width % 8 != 0) return FB_ERR_SHAPE;
+  const int64_t threads = static_cast<int64_t>(rows) * (width / 8);
+  const int64_t blocks = (threads + norm::kThreads - 1) / norm::kThreads;
+  if (blocks >= (1ll << 31)) return FB_ERR_SHAPE;
+  norm::swiglu_kernel<<<static_cast<unsigned>(blocks), norm::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       packed, splits, static_cast<__nv_bfloat16*>(out), rows, width);
   return check_launch();
 }

@@ -38,7 +38,7 @@ struct Params {
 template <int E>
 __device__ __forceinline__ void load_packed(const Params& p, size_t off, size_t split_stride,
                                             float (&x)[E]) {
-  if (p.splits == 1) {
+  if (p.splits == 0) {
     const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(p.packed) + off;
     if constexpr (E == 4) {
       uint2 w = *reinterpret_cast<const uint2*>(src);
@@ -105,7 +105,9 @@ __global__ void __launch_bounds__(128) qk_rope_kernel(const Params p) {
 
   long long phase;
   if (p.table) {
-    phase = p.position[b] + p.phases[row];
+    // whole tables: the phase row is the token's position (plus its verify-block phase)
+    const long long base = p.mode == 2 ? p.position[b] : p.position[0];
+    phase = base + (p.phases != nullptr ? p.phases[row] : t);
   } else {
     phase = p.mode == 2 ? row : t;
   }
@@ -167,9 +169,9 @@ extern "C" int fb_qk_norm_rope_append(const void* packed, int packed_splits, con
       !values)
     return FB_ERR_ARG;
   if (batch <= 0 || tokens <= 0 || q_heads <= 0 || kv_heads <= 0 || capacity <= 0 ||
-      packed_splits <= 0)
+      packed_splits < 0)
     return FB_ERR_ARG;
-  if (mode < 0 || mode > 2 || (table && (mode != 2 || phases == nullptr))) return FB_ERR_ARG;
+  if (mode < 0 || mode > 2 || (table && mode == 1)) return FB_ERR_ARG;
   if (head_dim != 64 && head_dim != 128) return FB_ERR_SHAPE;
   if (tokens > capacity) return FB_ERR_SHAPE;
   rope::Params p;

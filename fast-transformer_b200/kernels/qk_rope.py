@@ -9,7 +9,7 @@ import torch
 
 from kernels import _native
 from kernels._native import check, lib, ptr, stream
-from kernels.merged import source
+from kernels.merged import Split, source
 
 
 def qk_rope_cache(packed, q_norm, k_norm, cos, sin, position, keys, values, q_heads, prefill=False, rows=False, phases=None):
@@ -20,10 +20,11 @@ def qk_rope_cache(packed, q_norm, k_norm, cos, sin, position, keys, values, q_he
     Return a [B,Hq,T,D] view of token-major Q storage (contiguous when T is one).
     """
     batch, kv_heads, capacity, dim = keys.shape
+    split = isinstance(packed, Split)
     packed, splits, count, shape = source(packed)
     tokens = shape[1]
     assert keys.dtype == values.dtype == torch.bfloat16
-    assert packed.dtype == (torch.bfloat16 if splits == 1 else torch.float32)
+    assert packed.dtype == (torch.float32 if split else torch.bfloat16)
     assert packed.is_contiguous() and keys.is_contiguous() and values.is_contiguous()
     assert shape == (batch, tokens, (q_heads + 2 * kv_heads) * dim)
     assert 0 < tokens <= capacity
@@ -42,7 +43,7 @@ def qk_rope_cache(packed, q_norm, k_norm, cos, sin, position, keys, values, q_he
     query = torch.empty((batch, tokens, q_heads, dim), device=packed.device, dtype=keys.dtype)
     mode = 1 if prefill else 2 if rows else 0
     check(lib.fb_qk_norm_rope_append(
-        ptr(packed), splits, ptr(q_norm.weight), ptr(k_norm.weight),
+        ptr(packed), splits if packed.dtype == torch.float32 else 0, ptr(q_norm.weight), ptr(k_norm.weight),
         float(q_norm.variance_epsilon), float(k_norm.variance_epsilon), ptr(cos), ptr(sin),
         ptr(position), ptr(phases) if table else None, ptr(query), ptr(keys), ptr(values),
         batch, tokens, q_heads, kv_heads, dim, capacity, mode, 1 if table else 0, stream(),

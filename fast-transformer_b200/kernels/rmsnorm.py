@@ -9,7 +9,7 @@ import torch
 
 from kernels import _native
 from kernels._native import check, lib, ptr, stream
-from kernels.merged import source
+from kernels.merged import Split, source
 
 #: Widest row the kernels take (8 bf16 per thread chunk, 8 chunks x 256 threads).
 MAX_WIDTH = 16384
@@ -34,17 +34,17 @@ def add_rms_norm(x, residual, weight, eps):
     x_data, splits, count, shape = source(x)
     assert shape == tuple(residual.shape)
     assert residual.dtype == weight.dtype == torch.bfloat16
-    assert x_data.dtype == (torch.bfloat16 if splits == 1 else torch.float32)
+    assert x_data.dtype == (torch.float32 if isinstance(x, Split) else torch.bfloat16)
     width = shape[-1]
     if width > MAX_WIDTH or width % 8:
         raise ValueError(f"a row must fit in one block; {width} columns does not")
-    x_rows = x_data.reshape(-1, width).contiguous() if splits == 1 else x_data
+    x_rows = x_data if isinstance(x, Split) else x_data.reshape(-1, width).contiguous()
     residual_rows = residual.reshape(-1, width).contiguous()
     _native.require_cuda(x_rows, residual_rows, weight)
     out = torch.empty_like(residual_rows)
     summed = torch.empty_like(residual_rows)
     rows = residual_rows.shape[0]
-    check(lib.fb_add_rmsnorm(ptr(x_rows), splits, ptr(residual_rows), ptr(weight), ptr(out), ptr(summed),
+    check(lib.fb_add_rmsnorm(ptr(x_rows), splits if x_data.dtype == torch.float32 else 0, ptr(residual_rows), ptr(weight), ptr(out), ptr(summed),
                              rows, width, float(eps), stream()), "fb_add_rmsnorm")
     return out.reshape(shape), summed.reshape(shape)
 

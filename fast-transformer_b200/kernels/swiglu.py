@@ -7,16 +7,17 @@ import torch
 
 from kernels import _native
 from kernels._native import check, lib, ptr, stream
-from kernels.merged import source
+from kernels.merged import Split, source
 
 
 def swiglu(packed):
     """Contiguous BF16 [..., 2*I] gate/up input (or its Split partials); new contiguous [..., I] output."""
+    split = isinstance(packed, Split)
     packed, splits, count, shape = source(packed)
     width = shape[-1] // 2
-    assert packed.is_contiguous() and packed.dtype == (torch.bfloat16 if splits == 1 else torch.float32)
+    assert packed.is_contiguous() and packed.dtype == (torch.float32 if split else torch.bfloat16)
     _native.require_cuda(packed)
     output = torch.empty((*shape[:-1], width), device=packed.device, dtype=torch.bfloat16)
     rows = output.numel() // width
-    check(lib.fb_swiglu(ptr(packed), splits, ptr(output), rows, width, stream()), "fb_swiglu")
+    check(lib.fb_swiglu(ptr(packed), splits if packed.dtype == torch.float32 else 0, ptr(output), rows, width, stream()), "fb_swiglu")
     return output

@@ -76,17 +76,18 @@ int fb_decode_attention_combine(const int64_t* position, int per_row, void* out,
  * :13-84), same cast points: bf16(x * rsqrt(mean(x^2) + eps)) -> bf16(* gain) ->
  * bf16(bf16(w * cos) + bf16(rot(w) * sin)).
  *
- *   packed   bf16 [B*T, (Hq + 2 Hkv) * D] when packed_splits == 1, else fp32 split-K
+ *   packed   bf16 [B*T, (Hq + 2 Hkv) * D] when packed_splits == 0, else fp32 split-K
  *            partials [packed_splits, B*T, (Hq + 2 Hkv) * D] (summed in split order,
  *            then rounded to bf16: engine/kernels/merged.py:37-45)
  *   q_weight, k_weight bf16 [D]
  *   cos, sin bf16: table == 0 -> [rows_of_phase, D] where the phase row of token
  *            (b, t) is t (mode 0/1) or b*T + t (mode 2);
- *            table == 1 -> whole tables [>= C, D], phase row position[b] + phases[b,t]
+ *            table == 1 -> whole tables [>= C, D] (modes 0 and 2), phase row
+ *            p + (phases ? phases[b,t] : t) with p = position[b] (mode 2) or position[0]
  *   position int64: mode 0 (decode)  [1], token t of every row -> slot position[0] + t
  *                   mode 1 (prefill) [T] (unused values), token t -> slot t
  *                   mode 2 (rows)    [B], token t of row b -> slot position[b] + t
- *   phases   int64 [B, T] (table == 1 only, else may be NULL)
+ *   phases   int64 [B, T] or NULL (read only when table == 1)
  *   query    bf16 [B, T, Hq, D]       (token-major Q output)
  *   keys, values bf16 [B, Hkv, C, D]  (written in place at the slots above)
  * ---------------------------------------------------------------------------------- */
@@ -102,8 +103,8 @@ int fb_qk_norm_rope_append(const void* packed, int packed_splits, const void* q_
  *   fb_rmsnorm        <- `rms_norm` :49-72 (kernel :21-46): y = bf16(bf16(x*rsqrt) * w)
  *   fb_add_rmsnorm    <- `add_rms_norm` :98-125 (kernel :75-95):
  *                        sum = bf16(x + residual); out = bf16(bf16(sum*rsqrt) * w)
- *                        x is bf16 [rows, W] (x_splits == 1) or fp32 split partials
- *                        [x_splits, rows, W].
+ *                        x is bf16 [rows, W] (x_splits == 0) or fp32 split partials
+ *                        [x_splits, rows, W] (x_splits >= 1).
  *   fb_embed_rmsnorm  <- `embed_rms_norm` :145-162 (kernel :128-142): hidden = table[ids];
  *                        y = rmsnorm(hidden)
  * x/y/residual/out/sum bf16 [rows, W] contiguous (fb_rmsnorm: rows at `row_stride`
@@ -119,7 +120,7 @@ int fb_embed_rmsnorm(const int64_t* ids, const void* table, int64_t vocab, const
 /* ------------------------------------------------------------------------------------
  * SwiGLU. Replaces engine/kernels/swiglu.py:27-40 (kernel `_swiglu` :13-24):
  * out = bf16(bf16(g / (1 + exp(-g))) * u) for packed [.., 2I] = [gate | up].
- *   packed bf16 [rows, 2I] (splits == 1) or fp32 partials [splits, rows, 2I]
+ *   packed bf16 [rows, 2I] (splits == 0) or fp32 partials [splits, rows, 2I] (splits >= 1)
  *   out    bf16 [rows, I]; I % 8 == 0.
  * ---------------------------------------------------------------------------------- */
 int fb_swiglu(const void* packed, int splits, void* out, int rows, int width, void* stream);
