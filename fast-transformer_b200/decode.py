@@ -182,8 +182,11 @@ class DecodeState:
         self.position.copy_(saved_position)
         self.token_ids.copy_(saved_tokens)
         self.graph = torch.cuda.CUDAGraph()
+        before = _native.launches
         with torch.cuda.graph(self.graph, stream=side):
             self.decode()
+        #: libfastb200 kernels one replay launches
+        self.launches_per_step = _native.launches - before
         current.wait_stream(side)
         torch.cuda.synchronize(self.device)
 

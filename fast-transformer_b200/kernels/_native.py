@@ -69,9 +69,19 @@ def exported_names():
     return sorted(_SIGNATURES)
 
 
+#: Kernels each launching entry point enqueues (fb_argmax runs two stages).
+_KERNELS_PER_CALL = {"fb_argmax": 2}
+_NON_LAUNCHING = {"fb_device_error"}
+#: Running count of libfastb200 kernels enqueued (or recorded into a graph) by this process.
+launches = 0
+
+
 def check(status, what):
+    global launches
     if status != FB_OK:
         raise RuntimeError(f"{what}: {_STATUS.get(status, 'error')} (status {status})")
+    if what not in _NON_LAUNCHING:
+        launches += _KERNELS_PER_CALL.get(what, 1)
 
 
 def stream():
