@@ -228,7 +228,7 @@ def attention_sweep(peak):
                  torch.randn(batch, 8, capacity, 128, device="cuda").to(torch.bfloat16)) for _ in range(copies)]
         position = torch.tensor([n - 1 for n in lengths], dtype=torch.int64, device="cuda")
         ctas = _ctas((torch.device("cuda", torch.cuda.current_device()), batch, 8, capacity, 128))
-        ws = torch.empty(workspace_bytes(batch, 32, 8, 128, ctas), dtype=torch.uint8, device="cuda")
+        ws = torch.zeros(workspace_bytes(batch, 32, 8, 128, ctas), dtype=torch.uint8, device="cuda")
         out = torch.empty(batch, 1, 32, 128, dtype=torch.bfloat16, device="cuda")
 
         def run():

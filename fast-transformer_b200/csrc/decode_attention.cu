@@ -35,6 +35,7 @@ constexpr int kConsumerWarps = 4;  // 16 tokens each
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kMaxBatch = 1024;
 constexpr int kHeadsPad = 8;  // query heads per KV head, padded to the mma N
+constexpr int kMaxCtas = 512;  // persistent CTAs (runs per pair are bounded by this)
 
 struct Params {
   const __nv_bfloat16* q;  // [B, Hq, D]
@@ -43,6 +44,7 @@ struct Params {
   __nv_bfloat16* out;  // [B, Hq, D]
   float* acc;          // [slots, G, D]
   float2* stats;       // [slots, G] (max, denominator)
+  int* counters;       // [B * Hkv] runs finished per pair (fused merge); nullptr: no merge
   int batch, q_heads, kv_heads, groups, capacity, ctas;
   float scale_log2;
   unsigned* err;
@@ -69,6 +71,63 @@ __device__ __forceinline__ int slice_owner(long long T, long long t, int G) {
   return static_cast<int>(((t + 1) * G - 1) / T);
 }
 
+// Merge the runs of CTAs lo..hi on one (row, KV head) pair into its bf16 output:
+// out = sum_i acc_i * exp2(m_i - M) / sum_i l_i * exp2(m_i - M) per query head, the runs
+// taken in increasing CTA order (deterministic). A CTA in [lo, hi] whose slice is empty
+// wrote nothing and gets weight 0. Partials are read through L2 (ld.global.cg): they were
+// written by other CTAs of this launch moments ago.
+template <int D, typename Bar>
+__device__ void merge_pair(const Params& p, int pair, int lo, int hi, long long T, int tid,
+                           int threads, float* s_w, float* s_den, Bar bar) {
+  const int G = p.groups;
+  const int runs = hi - lo + 1;
+  const int warp = tid >> 5, lane = tid & 31, warps = threads >> 5;
+  // With at least one tile per CTA every slice is non-empty: skip the 64-bit tests.
+  const bool all_nonempty = T >= p.ctas;
+  for (int g = warp; g < G; g += warps) {
+    float M = -INFINITY;
+    for (int i = lane; i < runs; i += 32)
+      if (all_nonempty || slice_start(T, lo + i, p.ctas) < slice_start(T, lo + i + 1, p.ctas))
+        M = fmaxf(M, __ldcg(&p.stats[static_cast<size_t>(lo + i + pair) * G + g].x));
+    M = warp_max(M);
+    const float piv = M == -INFINITY ? 0.f : M;
+    float L = 0.f;
+    for (int i = lane; i < runs; i += 32) {
+      float w = 0.f;
+      if (all_nonempty || slice_start(T, lo + i, p.ctas) < slice_start(T, lo + i + 1, p.ctas)) {
+        const float2 st = __ldcg(&p.stats[static_cast<size_t>(lo + i + pair) * G + g]);
+        w = exp2f(st.x - piv);
+        L += st.y * w;
+      }
+      s_w[i * kHeadsPad + g] = w;
+    }
+    L = warp_sum(L);
+    if (lane == 0) s_den[g] = L;
+  }
+  bar();
+  const int b = pair / p.kv_heads, h = pair % p.kv_heads;
+  __nv_bfloat16* out = p.out + (static_cast<size_t>(b) * p.q_heads + h * G) * D;
+  constexpr int kBatch = 8;  // run loads in flight before their in-order adds
+  for (int e = tid; e < G * D; e += threads) {
+    const int g = e / D, d = e % D;
+    const float* acc = p.acc + (static_cast<size_t>(lo + pair) * G + g) * D + d;
+    const size_t stride = static_cast<size_t>(G) * D;
+    float O = 0.f;
+    for (int i0 = 0; i0 < runs; i0 += kBatch) {
+      float a[kBatch], w[kBatch];
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) {
+        w[j] = i0 + j < runs ? s_w[(i0 + j) * kHeadsPad + g] : 0.f;
+        a[j] = w[j] != 0.f ? __ldcg(acc + (i0 + j) * stride) : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j)
+        if (w[j] != 0.f) O += a[j] * w[j];
+    }
+    out[e] = __float2bfloat16_rn(O / s_den[g]);
+  }
+}
+
 template <int D, int NS>
 struct Smem {
   static constexpr int kBoxes = D / 64;
@@ -81,7 +140,8 @@ struct Smem {
   static constexpr int kCum = ((kMaxBatch + 1) * 4 + 15) & ~15;  // keeps the mbarriers 8-byte aligned
   static constexpr int kBars = 2 * NS * 8;
   static constexpr int kMisc = 64;
-  static constexpr int kTotal = 1024 + kStagesBytes + kRedO + kRedML + kCum + kBars + kMisc;
+  static constexpr int kMerge = kMaxCtas * kHeadsPad * 4 + kHeadsPad * 4;  // run weights + denominators
+  static constexpr int kTotal = 1024 + kStagesBytes + kRedO + kRedML + kCum + kBars + kMisc + kMerge;
   static_assert((kStagesBytes + kRedO + kRedML + kCum) % 16 == 0, "mbarrier alignment");
 };
 
@@ -102,7 +162,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(base + S::kStagesBytes + S::kRedO + S::kRedML +
                                                S::kCum);
   uint64_t* empty = full + NS;
-  int* misc = reinterpret_cast<int*>(empty + NS);  // [0..3] start b,h,j ; [4] abort
+  int* misc = reinterpret_cast<int*>(empty + NS);  // [0..2] start b,h,j; [4] abort; [5..7] merge
+  float* merge_w = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(misc) + S::kMisc);
+  float* merge_den = merge_w + kMaxCtas * kHeadsPad;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -137,6 +199,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   __syncthreads();
 
+  if (p.counters != nullptr && blockIdx.x == 0) {
+    // Rows with no valid slot get no run; the fused form writes their (empty) output.
+    for (int b = 0; b < B; ++b)
+      if (cum[b + 1] == cum[b])
+        for (int e = threadIdx.x; e < p.q_heads * (int)D; e += blockDim.x)
+          p.out[static_cast<size_t>(b) * p.q_heads * D + e] = __float2bfloat16_rn(0.f);
+  }
   const long long total = static_cast<long long>(Hkv) * cum[B];
   const long long t0 = total > 0 ? slice_start(total, blockIdx.x, p.ctas) : 0;
   const long long t1 = total > 0 ? slice_start(total, blockIdx.x + 1, p.ctas) : 0;
@@ -393,6 +462,34 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (d == 0) p.stats[static_cast<size_t>(slot) * G + gq] = make_float2(M, L);
         }
       }
+      if (!whole && p.counters != nullptr) {
+        // Publish this run, count it, and let the pair's last run merge them all.
+        __threadfence();
+        asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+        if (ctid == 0) {
+          const long long first = static_cast<long long>(Hkv) * cum[cur_b] + static_cast<long long>(cur_h) * cur_n;
+          const int lo = slice_owner(total, first, p.ctas);
+          const int hi = slice_owner(total, first + cur_n - 1, p.ctas);
+          int runs = hi - lo + 1;
+          if (total < p.ctas) {  // some slices are empty: count the CTAs that really ran
+            runs = 0;
+            for (int i = lo; i <= hi; ++i)
+              runs += slice_start(total, i, p.ctas) < slice_start(total, i + 1, p.ctas);
+          }
+          const int done = atomicAdd(&p.counters[pair], 1);
+          const int last = done == runs - 1;
+          if (last) p.counters[pair] = 0;  // every run of this launch has counted: reset for the next
+          misc[5] = last;
+          misc[6] = lo;
+          misc[7] = hi;
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+        if (misc[5]) {
+          __threadfence();
+          merge_pair<D>(p, pair, misc[6], misc[7], total, ctid, kConsumerWarps * 32, merge_w,
+                        merge_den, [] { asm volatile("bar.sync 1, 128;" ::: "memory"); });
+        }
+      }
       asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
       if (k != count - 1) {
         n = cum[b + 1] - cum[b];
@@ -412,13 +509,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 // contributing CTAs and their per-head softmax weights exp2(m_run - M) are resolved once
 // into shared memory; the weighted sum over runs is then a coalesced sweep over the
 // partial accumulators, in increasing CTA order (deterministic).
-constexpr int kMaxCtas = 512;
 constexpr int kCombineThreads = 256;
 
 template <int D>
 __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const Params p) {
   __shared__ int s_before, s_total, s_n;
-  __shared__ unsigned char s_ok[kMaxCtas];
   __shared__ float s_w[kMaxCtas * kHeadsPad];
   __shared__ float s_den[kHeadsPad];
   const int pair = blockIdx.x;
@@ -442,8 +537,8 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const P
   __syncthreads();
   const int n = s_n;
   const long long T = static_cast<long long>(p.kv_heads) * s_total;
-  __nv_bfloat16* out = p.out + (static_cast<size_t>(b) * p.q_heads + h * G) * D;
   if (n == 0) {
+    __nv_bfloat16* out = p.out + (static_cast<size_t>(b) * p.q_heads + h * G) * D;
     for (int e = threadIdx.x; e < G * D; e += blockDim.x) out[e] = __float2bfloat16_rn(0.f);
     return;
   }
@@ -451,41 +546,7 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const P
   const int lo = slice_owner(T, first, p.ctas);
   const int hi = slice_owner(T, first + n - 1, p.ctas);
   if (lo == hi) return;  // one run covered the pair and wrote the output itself
-  const int runs = hi - lo + 1;
-  // A CTA between lo and hi whose slice is empty wrote nothing for this pair.
-  for (int i = threadIdx.x; i < runs; i += blockDim.x)
-    s_ok[i] = slice_start(T, lo + i, p.ctas) < slice_start(T, lo + i + 1, p.ctas);
-  __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int g = warp; g < G; g += kCombineThreads / 32) {
-    float M = -INFINITY;
-    for (int i = lane; i < runs; i += 32)
-      if (s_ok[i]) M = fmaxf(M, p.stats[static_cast<size_t>(lo + i + pair) * G + g].x);
-    M = warp_max(M);
-    const float piv = M == -INFINITY ? 0.f : M;
-    float L = 0.f;
-    for (int i = lane; i < runs; i += 32) {
-      float w = 0.f;
-      if (s_ok[i]) {
-        const float2 st = p.stats[static_cast<size_t>(lo + i + pair) * G + g];
-        w = exp2f(st.x - piv);
-        L += st.y * w;
-      }
-      s_w[i * kHeadsPad + g] = w;
-    }
-    L = warp_sum(L);
-    if (lane == 0) s_den[g] = L;
-  }
-  __syncthreads();
-  for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
-    const int g = e / D, d = e % D;
-    const float* acc = p.acc + (static_cast<size_t>(lo + pair) * G + g) * D + d;
-    const size_t stride = static_cast<size_t>(G) * D;
-    float O = 0.f;
-    for (int i = 0; i < runs; ++i)
-      if (s_ok[i]) O += acc[i * stride] * s_w[i * kHeadsPad + g];
-    out[e] = __float2bfloat16_rn(O / s_den[g]);
-  }
+  merge_pair<D>(p, pair, lo, hi, T, threadIdx.x, kCombineThreads, s_w, s_den, [] { __syncthreads(); });
 }
 
 constexpr int kStages = 4;
@@ -535,14 +596,15 @@ extern "C" size_t fb_decode_attention_workspace(int batch, int q_heads, int kv_h
   if (batch <= 0 || q_heads <= 0 || kv_heads <= 0 || head_dim <= 0 || ctas <= 0) return 0;
   const size_t G = q_heads / kv_heads;
   const size_t slots = static_cast<size_t>(ctas) + static_cast<size_t>(batch) * kv_heads;
-  const size_t acc = slots * G * head_dim * sizeof(float);
-  const size_t stats = slots * G * sizeof(float2);
-  return ((acc + 255) & ~size_t(255)) + stats;
+  const size_t acc = ((slots * G * head_dim * sizeof(float)) + 255) & ~size_t(255);
+  const size_t stats = ((slots * G * sizeof(float2)) + 255) & ~size_t(255);
+  const size_t counters = static_cast<size_t>(batch) * kv_heads * sizeof(int);
+  return acc + stats + counters;
 }
 
 static int make_params(Params* p, const void* q, const int64_t* position, int per_row, void* out,
                        void* workspace, size_t workspace_bytes, int batch, int q_heads,
-                       int kv_heads, int head_dim, int capacity, float scale, int ctas) {
+                       int kv_heads, int head_dim, int capacity, float scale, int ctas, bool fused) {
   int st = validate(batch, q_heads, kv_heads, head_dim, capacity);
   if (st != FB_OK) return st;
   if (position == nullptr || out == nullptr || workspace == nullptr || ctas <= 0) return FB_ERR_ARG;
@@ -551,13 +613,16 @@ static int make_params(Params* p, const void* q, const int64_t* position, int pe
   if (workspace_bytes < need) return FB_ERR_WORKSPACE;
   const size_t G = q_heads / kv_heads;
   const size_t slots = static_cast<size_t>(ctas) + static_cast<size_t>(batch) * kv_heads;
-  const size_t acc = slots * G * head_dim * sizeof(float);
+  const size_t acc = ((slots * G * head_dim * sizeof(float)) + 255) & ~size_t(255);
+  const size_t stats = ((slots * G * sizeof(float2)) + 255) & ~size_t(255);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
   p->q = static_cast<const __nv_bfloat16*>(q);
   p->position = position;
   p->per_row = per_row ? 1 : 0;
   p->out = static_cast<__nv_bfloat16*>(out);
-  p->acc = static_cast<float*>(workspace);
-  p->stats = reinterpret_cast<float2*>(static_cast<uint8_t*>(workspace) + ((acc + 255) & ~size_t(255)));
+  p->acc = reinterpret_cast<float*>(ws);
+  p->stats = reinterpret_cast<float2*>(ws + acc);
+  p->counters = fused ? reinterpret_cast<int*>(ws + acc + stats) : nullptr;
   p->batch = batch;
   p->q_heads = q_heads;
   p->kv_heads = kv_heads;
@@ -569,15 +634,14 @@ static int make_params(Params* p, const void* q, const int64_t* position, int pe
   return FB_OK;
 }
 
-extern "C" int fb_decode_attention(const void* q, const void* k, const void* v,
-                                   const int64_t* position, int per_row, void* out, void* workspace,
-                                   size_t workspace_bytes, int batch, int q_heads, int kv_heads,
-                                   int head_dim, int capacity, float scale, int ctas,
-                                   void* stream) {
+static int launch_decode(const void* q, const void* k, const void* v, const int64_t* position,
+                         int per_row, void* out, void* workspace, size_t workspace_bytes, int batch,
+                         int q_heads, int kv_heads, int head_dim, int capacity, float scale,
+                         int ctas, void* stream, bool fused) {
   if (q == nullptr || k == nullptr || v == nullptr) return FB_ERR_ARG;
   Params p;
   int st = make_params(&p, q, position, per_row, out, workspace, workspace_bytes, batch, q_heads,
-                       kv_heads, head_dim, capacity, scale, ctas);
+                       kv_heads, head_dim, capacity, scale, ctas, fused);
   if (st != FB_OK) return st;
   const uint64_t rows = static_cast<uint64_t>(batch) * kv_heads * capacity;
   CUtensorMap km, vm;
@@ -589,13 +653,31 @@ extern "C" int fb_decode_attention(const void* q, const void* k, const void* v,
   return head_dim == 128 ? launch_partials<128>(km, vm, p, s) : launch_partials<64>(km, vm, p, s);
 }
 
+extern "C" int fb_decode_attention(const void* q, const void* k, const void* v,
+                                   const int64_t* position, int per_row, void* out, void* workspace,
+                                   size_t workspace_bytes, int batch, int q_heads, int kv_heads,
+                                   int head_dim, int capacity, float scale, int ctas,
+                                   void* stream) {
+  return launch_decode(q, k, v, position, per_row, out, workspace, workspace_bytes, batch, q_heads,
+                       kv_heads, head_dim, capacity, scale, ctas, stream, true);
+}
+
+extern "C" int fb_decode_attention_partials(const void* q, const void* k, const void* v,
+                                            const int64_t* position, int per_row, void* out,
+                                            void* workspace, size_t workspace_bytes, int batch,
+                                            int q_heads, int kv_heads, int head_dim, int capacity,
+                                            float scale, int ctas, void* stream) {
+  return launch_decode(q, k, v, position, per_row, out, workspace, workspace_bytes, batch, q_heads,
+                       kv_heads, head_dim, capacity, scale, ctas, stream, false);
+}
+
 extern "C" int fb_decode_attention_combine(const int64_t* position, int per_row, void* out,
                                            void* workspace, size_t workspace_bytes, int batch,
                                            int q_heads, int kv_heads, int head_dim, int capacity,
                                            int ctas, void* stream) {
   Params p;
   int st = make_params(&p, nullptr, position, per_row, out, workspace, workspace_bytes, batch,
-                       q_heads, kv_heads, head_dim, capacity, 1.0f, ctas);
+                       q_heads, kv_heads, head_dim, capacity, 1.0f, ctas, false);
   if (st != FB_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int pairs = batch * kv_heads;

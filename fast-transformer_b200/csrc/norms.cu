@@ -41,17 +41,30 @@ __device__ __forceinline__ void load8(const void* src, int splits, size_t count,
   x[5] = b.y;
   x[6] = b.z;
   x[7] = b.w;
-  for (int s = 1; s < splits; ++s) {
-    const float4 c = *reinterpret_cast<const float4*>(f + s * count);
-    const float4 d = *reinterpret_cast<const float4*>(f + s * count + 4);
-    x[0] += c.x;
-    x[1] += c.y;
-    x[2] += c.z;
-    x[3] += c.w;
-    x[4] += d.x;
-    x[5] += d.y;
-    x[6] += d.z;
-    x[7] += d.w;
+  // Issue the loads of up to four slabs before adding them (in split order), so a
+  // multi-split input costs ceil((S-1)/4) memory round trips rather than S-1.
+  for (int s0 = 1; s0 < splits; s0 += 4) {
+    float4 c[4], d[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (s0 + j < splits) {
+        c[j] = __ldg(reinterpret_cast<const float4*>(f + (s0 + j) * count));
+        d[j] = __ldg(reinterpret_cast<const float4*>(f + (s0 + j) * count + 4));
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (s0 + j < splits) {
+        x[0] += c[j].x;
+        x[1] += c[j].y;
+        x[2] += c[j].z;
+        x[3] += c[j].w;
+        x[4] += d[j].x;
+        x[5] += d[j].y;
+        x[6] += d[j].z;
+        x[7] += d[j].w;
+      }
+    }
   }
 #pragma unroll
   for (int e = 0; e < 8; ++e) x[e] = bf16_round(x[e]);
@@ -190,8 +203,16 @@ __global__ void __launch_bounds__(kThreads)
   float x[4];
   const int n = count - i < 4 ? static_cast<int>(count - i) : 4;
   for (int e = 0; e < n; ++e) x[e] = partial[i + e];
-  for (int s = 1; s < splits; ++s)
-    for (int e = 0; e < n; ++e) x[e] += partial[s * count + i + e];
+  for (int s0 = 1; s0 < splits; s0 += 4) {
+    float y[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      for (int e = 0; e < n; ++e) y[j][e] = s0 + j < splits ? partial[(s0 + j) * count + i + e] : 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (s0 + j < splits)
+        for (int e = 0; e < n; ++e) x[e] += y[j][e];
+  }
   if (out_fp32) {
     for (int e = 0; e < n; ++e) static_cast<float*>(out)[i + e] = x[e];
   } else {

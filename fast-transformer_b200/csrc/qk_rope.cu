@@ -53,11 +53,39 @@ __device__ __forceinline__ void load_packed(const Params& p, size_t off, size_t 
     }
   } else {
     const float* src = static_cast<const float*>(p.packed) + off;
+    const float4* src4 = reinterpret_cast<const float4*>(src);
+    float v0[E];
+    if constexpr (E == 4) {
+      const float4 a = __ldg(src4);
+      v0[0] = a.x; v0[1] = a.y; v0[2] = a.z; v0[3] = a.w;
+    } else {
+      const float2 a = __ldg(reinterpret_cast<const float2*>(src));
+      v0[0] = a.x; v0[1] = a.y;
+    }
 #pragma unroll
-    for (int e = 0; e < E; ++e) x[e] = src[e];
-    for (int s = 1; s < p.splits; ++s) {
+    for (int e = 0; e < E; ++e) x[e] = v0[e];
+    // Loads of up to four slabs in flight before their in-order adds.
+    for (int s0 = 1; s0 < p.splits; s0 += 4) {
+      float y[4][E];
 #pragma unroll
-      for (int e = 0; e < E; ++e) x[e] += src[s * split_stride + e];
+      for (int j = 0; j < 4; ++j) {
+        if (s0 + j < p.splits) {
+          const float* q = src + (s0 + j) * split_stride;
+          if constexpr (E == 4) {
+            const float4 a = __ldg(reinterpret_cast<const float4*>(q));
+            y[j][0] = a.x; y[j][1] = a.y; y[j][2] = a.z; y[j][3] = a.w;
+          } else {
+            const float2 a = __ldg(reinterpret_cast<const float2*>(q));
+            y[j][0] = a.x; y[j][1] = a.y;
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (s0 + j < p.splits) {
+#pragma unroll
+          for (int e = 0; e < E; ++e) x[e] += y[j][e];
+        }
     }
 #pragma unroll
     for (int e = 0; e < E; ++e) x[e] = bf16_round(x[e]);
@@ -80,22 +108,44 @@ __global__ void __launch_bounds__(128) qk_rope_kernel(const Params p) {
   const size_t split_stride = static_cast<size_t>(rows) * width;
   const int d0 = lane * E;
 
-  float x[E];
+  const bool is_q = head < p.q_heads;
+  const int kvh = head - p.q_heads;
+  // Every global read is issued up front (the V head before any store that could alias it).
+  float x[E], v[E];
   load_packed<E>(p, static_cast<size_t>(row) * width + head * D + d0, split_stride, x);
+  if (!is_q)
+    load_packed<E>(p, static_cast<size_t>(row) * width + (p.q_heads + p.kv_heads + kvh) * D + d0,
+                   split_stride, v);
+  const __nv_bfloat16* gain = is_q ? p.q_weight : p.k_weight;
+  float gw[E];
+  if constexpr (E == 4) {
+    const uint2 gv = __ldg(reinterpret_cast<const uint2*>(gain + d0));
+    gw[0] = bf16_lo(gv.x);
+    gw[1] = bf16_hi(gv.x);
+    gw[2] = bf16_lo(gv.y);
+    gw[3] = bf16_hi(gv.y);
+  } else {
+    const uint32_t gv = __ldg(reinterpret_cast<const uint32_t*>(gain + d0));
+    gw[0] = bf16_lo(gv);
+    gw[1] = bf16_hi(gv);
+  }
+  long long pos_base = 0;
+  if (p.mode == 2)
+    pos_base = __ldg(p.position + b);
+  else if (p.mode == 0)
+    pos_base = __ldg(p.position);
   float ss = 0.f;
 #pragma unroll
   for (int e = 0; e < E; ++e) ss += x[e] * x[e];
   ss = warp_sum(ss);
-  const bool is_q = head < p.q_heads;
   const float eps = is_q ? p.q_eps : p.k_eps;
   const float inv = 1.0f / sqrtf(ss / static_cast<float>(D) + eps);
-  const __nv_bfloat16* gain = is_q ? p.q_weight : p.k_weight;
 
   float w[E];
 #pragma unroll
   for (int e = 0; e < E; ++e) {
     const float n = bf16_round(x[e] * inv);
-    w[e] = bf16_round(n * __bfloat162float(gain[d0 + e]));
+    w[e] = bf16_round(n * gw[e]);
   }
   // Rotate-half partner: dims (d + D/2) mod D live in lane ^ 16.
   float partner[E];
@@ -106,8 +156,7 @@ __global__ void __launch_bounds__(128) qk_rope_kernel(const Params p) {
   long long phase;
   if (p.table) {
     // whole tables: the phase row is the token's position (plus its verify-block phase)
-    const long long base = p.mode == 2 ? p.position[b] : p.position[0];
-    phase = base + (p.phases != nullptr ? p.phases[row] : t);
+    phase = pos_base + (p.phases != nullptr ? p.phases[row] : t);
   } else {
     phase = p.mode == 2 ? row : t;
   }
@@ -131,14 +180,7 @@ __global__ void __launch_bounds__(128) qk_rope_kernel(const Params p) {
     for (int e = 0; e < E; ++e) dst[e] = outv[e];
     return;
   }
-  const int kvh = head - p.q_heads;
-  long long pos;
-  if (p.mode == 1)
-    pos = t;
-  else if (p.mode == 2)
-    pos = p.position[b] + t;
-  else
-    pos = p.position[0] + t;
+  const long long pos = p.mode == 1 ? t : pos_base + t;
   if (pos < 0 || pos >= p.capacity) {
     if (lane == 0) raise_error(p.err, kErrBadShape);
     return;
@@ -146,9 +188,6 @@ __global__ void __launch_bounds__(128) qk_rope_kernel(const Params p) {
   const size_t slot = ((static_cast<size_t>(b) * p.kv_heads + kvh) * p.capacity + pos) * D + d0;
 #pragma unroll
   for (int e = 0; e < E; ++e) p.keys[slot + e] = outv[e];
-  float v[E];
-  load_packed<E>(p, static_cast<size_t>(row) * width + (p.q_heads + p.kv_heads + kvh) * D + d0,
-                 split_stride, v);
 #pragma unroll
   for (int e = 0; e < E; ++e) p.values[slot + e] = __float2bfloat16_rn(v[e]);
 }

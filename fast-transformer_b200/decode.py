@@ -125,7 +125,8 @@ class DecodeState:
         self.scale = 1.0 / math.sqrt(cfg.head_dim)
         self.graph = None
         self.ctas = int(lib.fb_decode_attention_ctas(batch, weights.kv_heads, self.capacity, cfg.head_dim))
-        self.workspace = torch.empty(
+        # zeroed once: the fused attention merge keeps its per-pair counters at zero between calls
+        self.workspace = torch.zeros(
             int(lib.fb_decode_attention_workspace(batch, weights.q_heads, weights.kv_heads, cfg.head_dim, self.ctas)),
             dtype=torch.uint8, device=self.device)
         self.attn_out = torch.empty((batch, 1, weights.q_heads, cfg.head_dim), dtype=BF16, device=self.device)

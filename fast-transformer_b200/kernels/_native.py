@@ -31,6 +31,8 @@ _SIGNATURES = {
     "fb_decode_attention_workspace": (_c_size, [_c_int, _c_int, _c_int, _c_int, _c_int]),
     "fb_decode_attention": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _vp, _vp, _c_size,
                                      _c_int, _c_int, _c_int, _c_int, _c_int, _c_float, _c_int, _vp]),
+    "fb_decode_attention_partials": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _vp, _vp, _c_size,
+                                              _c_int, _c_int, _c_int, _c_int, _c_int, _c_float, _c_int, _vp]),
     "fb_decode_attention_combine": (_c_int, [_vp, _c_int, _vp, _vp, _c_size,
                                              _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _vp]),
     "fb_qk_norm_rope_append": (_c_int, [_vp, _c_int, _vp, _vp, _c_float, _c_float, _vp, _vp, _vp, _vp,

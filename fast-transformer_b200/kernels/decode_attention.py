@@ -32,25 +32,33 @@ def workspace_bytes(batch, query_heads, kv_heads, dim, ctas):
     return int(lib.fb_decode_attention_workspace(batch, query_heads, kv_heads, dim, ctas))
 
 
-def attend(query, key, value, position, scale, out=None, workspace=None, ctas=None):
-    """Launch both kernels. ``query`` [B,Hq,1,D] or [B,Hq,D]; returns ``out`` [B,1,Hq,D]."""
+def attend(query, key, value, position, scale, out=None, workspace=None, ctas=None, two_launch=False):
+    """Launch decode attention. ``query`` [B,Hq,1,D] or [B,Hq,D]; returns ``out`` [B,1,Hq,D].
+
+    One launch by default (fb_decode_attention, merge fused into the last CTA of each pair);
+    ``two_launch`` runs fb_decode_attention_partials then fb_decode_attention_combine. A
+    caller-provided ``workspace`` must have been zeroed before its first fused use.
+    """
     batch, query_heads, dim = query.shape[0], query.shape[1], query.shape[-1]
     kv_heads, capacity = key.shape[1], key.shape[2]
     if ctas is None:
         ctas = _ctas((query.device, batch, kv_heads, capacity, dim))
     need = workspace_bytes(batch, query_heads, kv_heads, dim, ctas)
     if workspace is None:
-        workspace = torch.empty(need, dtype=torch.uint8, device=query.device)
+        workspace = torch.zeros(need, dtype=torch.uint8, device=query.device)
     if out is None:
         out = torch.empty((batch, 1, query_heads, dim), device=query.device, dtype=query.dtype)
     per_row = 1 if position.numel() > 1 else 0
     s = stream()
-    check(lib.fb_decode_attention(ptr(query), ptr(key), ptr(value), ptr(position), per_row, ptr(out),
-                                  ptr(workspace), workspace.numel(), batch, query_heads, kv_heads, dim,
-                                  capacity, float(scale), ctas, s), "fb_decode_attention")
-    check(lib.fb_decode_attention_combine(ptr(position), per_row, ptr(out), ptr(workspace),
-                                          workspace.numel(), batch, query_heads, kv_heads, dim,
-                                          capacity, ctas, s), "fb_decode_attention_combine")
+    args = (ptr(query), ptr(key), ptr(value), ptr(position), per_row, ptr(out), ptr(workspace), workspace.numel(),
+            batch, query_heads, kv_heads, dim, capacity, float(scale), ctas, s)
+    if not two_launch:
+        check(lib.fb_decode_attention(*args), "fb_decode_attention")
+        return out
+    check(lib.fb_decode_attention_partials(*args), "fb_decode_attention_partials")
+    check(lib.fb_decode_attention_combine(ptr(position), per_row, ptr(out), ptr(workspace), workspace.numel(),
+                                          batch, query_heads, kv_heads, dim, capacity, ctas, s),
+          "fb_decode_attention_combine")
     return out
 
 

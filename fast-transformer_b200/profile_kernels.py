@@ -1,0 +1,126 @@
+"""Run one decode-path kernel (or one eager decode step) at a chosen shape, for Nsight Compute.
+
+    python fast-transformer_b200/profile_kernels.py attention --batch 16 --length 8320
+    python fast-transformer_b200/profile_kernels.py linear --m 16 --n 24576 --k 4096
+    python fast-transformer_b200/profile_kernels.py step --preset qwen3-8b --batch 16 --length 8192
+
+Each mode warms up, then runs the measured launches inside the NVTX range "profiled", so
+`ncu --nvtx --nvtx-include "profiled/"` captures exactly those; it also prints the CUDA-event
+time of the same launches measured without a profiler (graph-replayed, inputs larger than L2).
+"""
+
+import argparse
+import math
+import os
+import statistics
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+
+import torch  # noqa: E402
+
+
+def graph_time(fn, repeats=5):
+    fn()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fn()
+    times = []
+    for _ in range(repeats):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        graph.replay()
+        end.record()
+        end.synchronize()
+        times.append(start.elapsed_time(end))
+    return statistics.median(times)
+
+
+def attention(args):
+    from kernels.decode_attention import attend, _ctas, workspace_bytes
+    b, hq, hkv, d, n = args.batch, args.q_heads, args.kv_heads, 128, args.length
+    sets = [(torch.randn(b, hq, 1, d, device="cuda").bfloat16(), torch.randn(b, hkv, n, d, device="cuda").bfloat16(),
+             torch.randn(b, hkv, n, d, device="cuda").bfloat16()) for _ in range(args.copies)]
+    position = torch.tensor([n - 1], dtype=torch.int64, device="cuda")
+    ctas = _ctas((torch.device("cuda", 0), b, hkv, n, d))
+    ws = torch.zeros(workspace_bytes(b, hq, hkv, d, ctas), dtype=torch.uint8, device="cuda")
+    out = torch.empty(b, 1, hq, d, dtype=torch.bfloat16, device="cuda")
+
+    def run():
+        for q, k, v in sets:
+            attend(q, k, v, position, 1 / math.sqrt(d), out=out, workspace=ws, ctas=ctas)
+
+    ms = graph_time(run) / len(sets)
+    nbytes = 2 * b * hkv * n * d * 2 + 2 * b * hq * d * 2
+    print(f"attention B={b} Hq={hq} Hkv={hkv} L={n}: {ms * 1e3:.2f} us/launch, {nbytes / ms / 1e6:.0f} GB/s "
+          f"({nbytes} algorithmic bytes per launch)")
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("profiled")
+    for _ in range(args.launches):
+        attend(*sets[0], position, 1 / math.sqrt(d), out=out, workspace=ws, ctas=ctas)
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+
+
+def linear(args):
+    from kernels.linear import project, splits_for
+    x = torch.randn(args.m, args.k, device="cuda").bfloat16()
+    weights = [(torch.randn(args.n, args.k, device="cuda") * 0.02).bfloat16() for _ in range(args.copies)]
+    splits = splits_for(args.m, args.n, args.k, x.device)
+
+    def run():
+        for w in weights:
+            project(x, w, splits)
+
+    ms = graph_time(run) / len(weights)
+    nbytes = args.n * args.k * 2
+    print(f"linear M={args.m} N={args.n} K={args.k} S={splits}: {ms * 1e3:.2f} us, {nbytes / ms / 1e6:.0f} GB/s")
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("profiled")
+    for _ in range(args.launches):
+        project(x, weights[0], splits)
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+
+
+def step(args):
+    import decode as fdecode
+    import qwen3
+    cfg = qwen3.Config.make(**qwen3.PRESETS[args.preset])
+    weights = qwen3.random_init(cfg, "cuda", seed=0)
+    state = fdecode.DecodeState(weights, args.batch, args.length, 8)
+    # decode cost does not depend on cache contents: random K/V instead of a prefill
+    state.cache.store.normal_()
+    state.position.fill_(args.length)
+    for _ in range(2):
+        state.decode()
+        state.position.fill_(args.length)
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("profiled")
+    state.decode()
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    print(f"step {args.preset} B={args.batch} L={args.length}: one eager decode step profiled")
+
+
+def main():
+    parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    parser.add_argument("mode", choices=("attention", "linear", "step"))
+    parser.add_argument("--batch", type=int, default=16)
+    parser.add_argument("--q-heads", type=int, default=32)
+    parser.add_argument("--kv-heads", type=int, default=8)
+    parser.add_argument("--length", type=int, default=8320)
+    parser.add_argument("--m", type=int, default=16)
+    parser.add_argument("--n", type=int, default=24576)
+    parser.add_argument("--k", type=int, default=4096)
+    parser.add_argument("--preset", default="qwen3-8b")
+    parser.add_argument("--copies", type=int, default=2)
+    parser.add_argument("--launches", type=int, default=2)
+    args = parser.parse_args()
+    {"attention": attention, "linear": linear, "step": step}[args.mode](args)
+
+
+if __name__ == "__main__":
+    main()

@@ -56,9 +56,15 @@ int fb_device_error(unsigned int* host_flags);
  *
  * The work is a persistent grid of `ctas` CTAs that split the valid tokens of all
  * (row, KV head) pairs evenly (64-token tiles). fb_decode_attention_ctas() gives the
- * default CTA count; fb_decode_attention_workspace() the workspace bytes for a count.
- * fb_decode_attention writes partials; fb_decode_attention_combine merges them into out
- * (the log-sum-exp combine). Both must be called with the same arguments and `ctas`.
+ * default CTA count (<= 512); fb_decode_attention_workspace() the workspace bytes for a count.
+ *
+ * fb_decode_attention: the whole operation in one launch; the CTA that finishes a pair last
+ *   merges its runs (log-sum-exp combine) in CTA order. The workspace ends with one int
+ *   counter per pair: zero it once before its first use; every call leaves it zero again.
+ *   Calls that share a workspace must not overlap on the GPU.
+ * fb_decode_attention_partials + fb_decode_attention_combine: the same result in two
+ *   launches (partials, then the merge kernel), the reference's _decode_partials/_decode_merge
+ *   split; no counter state. Both take the same arguments and `ctas`.
  * ---------------------------------------------------------------------------------- */
 int fb_decode_attention_ctas(int batch, int kv_heads, int capacity, int head_dim);
 size_t fb_decode_attention_workspace(int batch, int q_heads, int kv_heads, int head_dim, int ctas);
@@ -66,6 +72,10 @@ int fb_decode_attention(const void* q, const void* k, const void* v, const int64
                         int per_row, void* out, void* workspace, size_t workspace_bytes, int batch,
                         int q_heads, int kv_heads, int head_dim, int capacity, float scale, int ctas,
                         void* stream);
+int fb_decode_attention_partials(const void* q, const void* k, const void* v,
+                                 const int64_t* position, int per_row, void* out, void* workspace,
+                                 size_t workspace_bytes, int batch, int q_heads, int kv_heads,
+                                 int head_dim, int capacity, float scale, int ctas, void* stream);
 int fb_decode_attention_combine(const int64_t* position, int per_row, void* out, void* workspace,
                                 size_t workspace_bytes, int batch, int q_heads, int kv_heads,
                                 int head_dim, int capacity, int ctas, void* stream);

@@ -240,3 +240,23 @@ def test_argmax_matches_reference():
         ids = argmax(logits.to(DEV), top=top).cpu()
         assert torch.equal(ids, fx[case[0]]["out"])
         assert torch.equal(top.cpu(), fx[case[0]]["top"])
+
+
+def test_decode_attention_fused_equals_two_launch_and_counters_reset():
+    """fb_decode_attention (last CTA merges) equals fb_decode_attention_partials +
+    fb_decode_attention_combine bit for bit, and leaves its per-pair counters at zero."""
+    from kernels.decode_attention import _ctas, attend, workspace_bytes
+    for lengths, q_heads in (([1, 700, 8192, 65], 32), ([30000], 16), ([300, 301, 302, 303, 1, 2, 3, 4], 16)):
+        q, k, v, position = _ragged(len(lengths), q_heads, 8, 128, lengths, seed=sum(lengths))
+        ctas = _ctas((q.device, len(lengths), 8, k.shape[2], 128))
+        ws = torch.zeros(workspace_bytes(len(lengths), q_heads, 8, 128, ctas), dtype=torch.uint8, device=DEV)
+        fused = attend(q, k, v, position, 0.088, workspace=ws.clone(), ctas=ctas)
+        again_ws = torch.zeros_like(ws)
+        attend(q, k, v, position, 0.088, workspace=again_ws, ctas=ctas)
+        second = attend(q, k, v, position, 0.088, workspace=again_ws, ctas=ctas)  # reuses the counters
+        two = attend(q, k, v, position, 0.088, workspace=ws.clone(), ctas=ctas, two_launch=True)
+        torch.cuda.synchronize()
+        assert torch.equal(fused, two)
+        assert torch.equal(second, fused)
+        counters = again_ws[-len(lengths) * 8 * 4:].view(torch.int32)
+        assert int(counters.abs().sum()) == 0
