@@ -25,6 +25,8 @@
 //    workspace; the combine kernel re-derives which CTAs touched each pair from the same
 //    integer partition, so no counters or atomics are needed and results are
 //    deterministic.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace fb {
@@ -686,4 +688,73 @@ extern "C" int fb_decode_attention_combine(const int64_t* position, int per_row,
   else
     decode_combine_kernel<64><<<pairs, kCombineThreads, 0, s>>>(p);
   return check_launch();
+}
+
+// ---------------------------------------------------------------------------------------
+// Decode attention whose scratch is a fixed array inside this library, for callers that
+// cannot allocate device memory (no counterpart in the reference). Such a caller owns all
+// device memory itself - for example a serving runtime with a fixed, pre-reserved pool that
+// hands kernels only their input and output buffers, or a plugin host whose allocator must
+// not be called from the plugin - so it cannot provide fb_decode_attention's workspace.
+// ---------------------------------------------------------------------------------------
+namespace fb {
+namespace attn {
+
+constexpr int kNoAllocMaxPairs = 512;  // batch * kv_heads
+constexpr int kNoAllocMaxCtas = 160;   // persistent CTAs used by this entry point
+// Sized for the largest request accepted: (ctas + pairs) run slots of up to 8 heads x 128
+// dims of fp32 partials, their (max, sum) stats, and one counter per pair.
+constexpr size_t kNoAllocScratchBytes =
+    ((static_cast<size_t>(kNoAllocMaxCtas + kNoAllocMaxPairs) * kHeadsPad * 128 * 4 + 255) &
+     ~size_t(255)) +
+    ((static_cast<size_t>(kNoAllocMaxCtas + kNoAllocMaxPairs) * kHeadsPad * 8 + 255) & ~size_t(255)) +
+    static_cast<size_t>(kNoAllocMaxPairs) * 4;
+
+// Every GPU that loads the library holds this array until the process exits. In host code
+// the name is only a stand-in: the device address comes from cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mutex;
+void* g_noalloc_address[64] = {nullptr};
+
+// Device address of the scratch array on the current device, looked up once per device
+// (with that device current). nullptr if the lookup fails.
+void* noalloc_scratch() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_address[dev] == nullptr) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr) return nullptr;
+    g_noalloc_address[dev] = ptr;
+  }
+  return g_noalloc_address[dev];
+}
+
+}  // namespace attn
+}  // namespace fb
+
+extern "C" int fb_decode_attention_noalloc(const void* q, const void* k, const void* v,
+                                           const int64_t* position, int per_row, void* out,
+                                           int batch, int q_heads, int kv_heads, int head_dim,
+                                           int capacity, float scale, void* stream) {
+  int st = validate(batch, q_heads, kv_heads, head_dim, capacity);
+  if (st != FB_OK) return st;
+  if (q == nullptr || k == nullptr || v == nullptr || position == nullptr || out == nullptr)
+    return FB_ERR_ARG;
+  if (static_cast<long long>(batch) * kv_heads > kNoAllocMaxPairs) return FB_ERR_TOO_LARGE;
+  int ctas = sm_count();
+  if (ctas > kNoAllocMaxCtas) ctas = kNoAllocMaxCtas;
+  const size_t need = fb_decode_attention_workspace(batch, q_heads, kv_heads, head_dim, ctas);
+  if (need == 0 || need > kNoAllocScratchBytes) return FB_ERR_TOO_LARGE;
+  void* scratch = noalloc_scratch();
+  if (scratch == nullptr) return FB_ERR_LAUNCH;
+  // The per-pair counters (the workspace's tail) must start at zero: clear them here, since
+  // the array keeps whatever the previous call left.
+  const size_t counters = static_cast<size_t>(batch) * kv_heads * sizeof(int);
+  if (cudaMemsetAsync(static_cast<uint8_t*>(scratch) + need - counters, 0, counters,
+                      static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return FB_ERR_LAUNCH;
+  return launch_decode(q, k, v, position, per_row, out, scratch, need, batch, q_heads, kv_heads,
+                       head_dim, capacity, scale, ctas, stream, true);
 }

@@ -19,6 +19,7 @@ _STATUS = {
     -3: "kernel launch failed",
     -4: "tensor-map encoder unavailable or refused the map",
     -5: "workspace too small",
+    -6: "request larger than the entry point's fixed limit",
 }
 
 _c_int, _c_float, _c_size, _c_i64, _vp = ctypes.c_int, ctypes.c_float, ctypes.c_size_t, ctypes.c_int64, ctypes.c_void_p
@@ -33,6 +34,8 @@ _SIGNATURES = {
                                      _c_int, _c_int, _c_int, _c_int, _c_int, _c_float, _c_int, _vp]),
     "fb_decode_attention_partials": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _vp, _vp, _c_size,
                                               _c_int, _c_int, _c_int, _c_int, _c_int, _c_float, _c_int, _vp]),
+    "fb_decode_attention_noalloc": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _vp, _c_int, _c_int, _c_int, _c_int,
+                                             _c_int, _c_float, _vp]),
     "fb_decode_attention_combine": (_c_int, [_vp, _c_int, _vp, _vp, _c_size,
                                              _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _vp]),
     "fb_qk_norm_rope_append": (_c_int, [_vp, _c_int, _vp, _vp, _c_float, _c_float, _vp, _vp, _vp, _vp,

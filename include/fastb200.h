@@ -31,6 +31,7 @@ extern "C" {
 #define FB_ERR_LAUNCH (-3)      /* cudaGetLastError() after the launch */
 #define FB_ERR_DRIVER (-4)      /* tensor-map encoder unavailable / refused the map */
 #define FB_ERR_WORKSPACE (-5)   /* workspace smaller than the *_workspace() size */
+#define FB_ERR_TOO_LARGE (-6)   /* request exceeds a fixed-size entry point's limit */
 
 /* Library version, for the Python loader's sanity check. */
 int fb_version(void);
@@ -79,6 +80,28 @@ int fb_decode_attention_partials(const void* q, const void* k, const void* v,
 int fb_decode_attention_combine(const int64_t* position, int per_row, void* out, void* workspace,
                                 size_t workspace_bytes, int batch, int q_heads, int kv_heads,
                                 int head_dim, int capacity, int ctas, void* stream);
+
+/* ------------------------------------------------------------------------------------
+ * Decode attention without allocation. No counterpart in the reference.
+ * Some callers cannot allocate device memory on the call path: a host runtime that owns a
+ * fixed, pre-reserved device pool and hands this library only input and output buffers,
+ * or a plugin host whose allocator may not be called from the plugin. They cannot provide
+ * fb_decode_attention's workspace, so this entry point uses a fixed scratch array inside
+ * the library instead (about 2.7 MiB, held on every GPU that loads the library until the
+ * process exits). Same arguments and result as fb_decode_attention, minus the workspace
+ * and the CTA count (it uses min(SM count, 160) CTAs). It calls no cudaMalloc/cudaFree.
+ *   Limit: batch * kv_heads <= 512 (and the fb_decode_attention limits); a larger request
+ *   returns FB_ERR_TOO_LARGE and launches nothing.
+ *   The first call on a device looks up the array's device address for that device (it must
+ *   be the current device); make that first call before any stream capture.
+ *   Every call shares the one array, which keeps the last call's contents; each call clears
+ *   the part that must start at zero. Calls that overlap on the GPU (several streams, or
+ *   several host threads on one device) race on the array: serialise them.
+ * ---------------------------------------------------------------------------------- */
+int fb_decode_attention_noalloc(const void* q, const void* k, const void* v,
+                                const int64_t* position, int per_row, void* out, int batch,
+                                int q_heads, int kv_heads, int head_dim, int capacity, float scale,
+                                void* stream);
 
 /* ------------------------------------------------------------------------------------
  * Fused per-head Q/K RMSNorm + rotate-half RoPE + KV-cache append.
