@@ -38,6 +38,10 @@ _SIGNATURES = {
                                              _c_int, _c_float, _vp]),
     "fb_decode_attention_combine": (_c_int, [_vp, _c_int, _vp, _vp, _c_size,
                                              _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _vp]),
+    "fb_verify_attention_splits": (_c_int, [_c_int, _c_int, _c_int, _c_int]),
+    "fb_verify_attention_workspace": (_c_size, [_c_int, _c_int, _c_int, _c_int, _c_int]),
+    "fb_verify_attention": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_size, _c_int, _c_int, _c_int, _c_int,
+                                     _c_int, _c_int, _c_float, _c_int, _vp]),
     "fb_qk_norm_rope_append": (_c_int, [_vp, _c_int, _vp, _vp, _c_float, _c_float, _vp, _vp, _vp, _vp,
                                         _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
                                         _c_int, _c_int, _vp]),

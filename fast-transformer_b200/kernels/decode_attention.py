@@ -75,3 +75,44 @@ def decode_attention(query, key, value, position, scale):
     assert position.is_contiguous()
     _native.require_cuda(query, key, value, position)
     return attend(query, key, value, position, scale)
+
+
+_BLOCK_SPLITS = {}
+
+
+def block_attention(query, key, value, position, scale, chain, splits=None):
+    """Verify blocks: token-major Q [B,T,Hq,D], KV [B,Hkv,C,D], position [B] -> [B,T,Hq,D].
+
+    Token t of row b occupies slot ``position[b] + t``. The first ``chain[b]`` tokens attend
+    causally; the rest are alternatives to token 1 and attend to the prefix through token 0
+    plus themselves. The block's own keys must already be in the cache. The kernel is
+    fb_verify_attention (tcgen05 UMMA, TMEM accumulators), plus its split merge.
+    """
+    batch, tokens, query_heads, dim = query.shape
+    kv_heads, capacity = key.shape[1:3]
+    assert key.shape[0] == batch and query_heads % kv_heads == 0
+    assert query.dtype == key.dtype == value.dtype == torch.bfloat16
+    assert query.is_contiguous() and key.is_contiguous() and value.is_contiguous()
+    assert value.shape == key.shape and key.shape[3] == dim and dim in (64, 128)
+    assert position.shape == (batch,) and position.dtype == torch.int64
+    assert chain.shape == (batch,) and chain.dtype == torch.int64
+    if dim != 128:
+        raise ValueError("the tcgen05 verify kernel takes head_dim 128")
+    _native.require_cuda(query, key, value, position, chain)
+    shape = (query.device, batch, tokens, query_heads, kv_heads, capacity, dim)
+    if splits is None:
+        if shape not in _BLOCK_SPLITS:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("attention layout selection must finish during eager warmup")
+            _BLOCK_SPLITS[shape] = int(lib.fb_verify_attention_splits(batch, tokens, kv_heads, capacity))
+        splits = _BLOCK_SPLITS[shape]
+    out = torch.empty((batch, tokens, query_heads, dim), device=query.device, dtype=query.dtype)
+    need = int(lib.fb_verify_attention_workspace(batch, tokens, query_heads, kv_heads, splits))
+    workspace = torch.empty(need if splits > 1 else 0, dtype=torch.uint8, device=query.device)
+    check(lib.fb_verify_attention(ptr(query), ptr(key), ptr(value), ptr(position), ptr(chain), ptr(out),
+                                  ptr(workspace) if splits > 1 else None, workspace.numel(), batch, tokens,
+                                  query_heads, kv_heads, dim, capacity, float(scale), splits, stream()),
+          "fb_verify_attention")
+    if splits > 1:
+        _native.launches += 1  # the split merge
+    return out

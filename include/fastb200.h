@@ -104,6 +104,26 @@ int fb_decode_attention_noalloc(const void* q, const void* k, const void* v,
                                 void* stream);
 
 /* ------------------------------------------------------------------------------------
+ * Speculative-verify attention, T > 1 tokens per row, on tcgen05 tensor cores.
+ * Replaces engine/kernels/decode_attention.py:637-680 `block_attention` (kernels
+ * `_block_partials` :260-350 and `_block_merge` :455-478).
+ *   q        bf16 [B, T, Hq, D] token-major; token t of row b sits at slot position[b] + t
+ *   k, v     bf16 [B, Hkv, C, D] with the block's own K/V already appended
+ *   position int64 [B]; chain int64 [B]: tokens t < chain[b] see slots [0, position[b] + t];
+ *            later tokens see [0, position[b]] plus their own slot
+ *   out      bf16 [B, T, Hq, D]
+ *   D = 128; T * (Hq / Hkv) <= 2048. `splits` KV splits per (row, KV head):
+ *   fb_verify_attention_splits() gives the default; with splits > 1 the workspace must hold
+ *   fb_verify_attention_workspace() bytes (partials merged by a second launch).
+ * ---------------------------------------------------------------------------------- */
+int fb_verify_attention_splits(int batch, int tokens, int kv_heads, int capacity);
+size_t fb_verify_attention_workspace(int batch, int tokens, int q_heads, int kv_heads, int splits);
+int fb_verify_attention(const void* q, const void* k, const void* v, const int64_t* position,
+                        const int64_t* chain, void* out, void* workspace, size_t workspace_bytes,
+                        int batch, int tokens, int q_heads, int kv_heads, int head_dim, int capacity,
+                        float scale, int splits, void* stream);
+
+/* ------------------------------------------------------------------------------------
  * Fused per-head Q/K RMSNorm + rotate-half RoPE + KV-cache append.
  * Replaces engine/kernels/qk_rope.py:87-129 `qk_rope_cache` (kernel `_qk_rope_cache`
  * :13-84), same cast points: bf16(x * rsqrt(mean(x^2) + eps)) -> bf16(* gain) ->
