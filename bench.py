@@ -256,6 +256,42 @@ def attention_sweep(peak):
     return results
 
 
+def verify_config5(peak):
+    """verify attention, B=8, T=5 (causal chain of 5), 32/8 heads, D=128,
+    4096-slot prefix + 5 new slots, N(0,1) bf16 (seed 0); graph-timed over L2-cold copies."""
+    from kernels.decode_attention import block_attention
+    g = torch.Generator(device="cuda").manual_seed(0)
+    b, t, hq, hkv, d, cap = 8, 5, 32, 8, 128, 4101
+    sets = [(torch.randn(b, t, hq, d, device="cuda", generator=g).to(torch.bfloat16),
+             torch.randn(b, hkv, cap, d, device="cuda", generator=g).to(torch.bfloat16),
+             torch.randn(b, hkv, cap, d, device="cuda", generator=g).to(torch.bfloat16)) for _ in range(3)]
+    position = torch.full((b,), cap - t, dtype=torch.int64, device="cuda")
+    chain = torch.full((b,), t, dtype=torch.int64, device="cuda")
+
+    def run():
+        for q, k, v in sets:
+            block_attention(q, k, v, position, 1 / math.sqrt(d), chain)
+
+    run()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        run()
+    times = []
+    for _ in range(5):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        graph.replay()
+        end.record()
+        end.synchronize()
+        times.append(start.elapsed_time(end) / len(sets))
+    ms = statistics.median(times)
+    nbytes = 2 * b * hkv * cap * d * 2 + 2 * b * t * hq * d * 2
+    flops = 4 * b * hq * t * cap * d
+    return {"us": ms * 1e3, "GB/s": nbytes / ms / 1e6, "frac": nbytes / ms / 1e6 / peak,
+            "useful_TFLOP/s": flops / ms / 1e9, "kernel": "fb_verify_attention (tcgen05)"}
+
+
 def main():
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--gpus", type=int, default=1)
@@ -293,7 +329,7 @@ def main():
     total_steps = args.warmup + args.steps
     # capacity: the prompt, the warm-up and timed steps of both timed loops, plus one spare slot
     state = fdecode.DecodeState(weights, BATCH, PROMPT, 2 * total_steps + 2,
-                                comm=fdecode.Communicator(group, world), device=device)
+                                comm=fdecode.Communicator(group, world, rank), device=device)
     with torch.inference_mode():
         state.prefill(prompt)
     state.capture()
@@ -388,8 +424,12 @@ def main():
             "gpu_launches": per_step_launches * args.steps}
     if clock:
         line["clocks"] = clock
+    if world > 1:
+        line["allreduce"] = "fused: projection epilogue pushes fp32 tiles to peers over NVLink (symmetric memory, no multicast); consumer sums ranks in order + add/RMSNorm"
+
     if world == 1 and not args.no_sweep:
         line["attention_sweep"] = attention_sweep(peak)
+        line["verify_attention_config5"] = verify_config5(peak)
     if world == 1 and not args.no_cpu:
         torch.set_num_threads(os.cpu_count() or 1)
         step_s, threads, sample = cpu_decode_sample()

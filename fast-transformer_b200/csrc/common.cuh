@@ -10,7 +10,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include "../../include/fastb200.h"
+#include "fastb200.h"  // include/ is on the include path (build.py)
 
 namespace fb {
 

@@ -1,16 +1,26 @@
 // Skinny bf16 projection y[M, N] = x[M, K] @ W[N, K]^T for decode (M <= 64), sm_100a.
 //
 // Same contract as the reference's skinny kinds (engine/kernels/linear.py:27-93,
-// gemm.py:51-425): fp32 accumulation, one rounding to bf16, optional split-K fp32
-// partials [S, M, N] that a consumer sums in split order (merged.py:13-45).
+// gemm.py:51-425): fp32 accumulation and one rounding to bf16 per output; split-K fp32
+// partials may be handed to a consumer that sums them in split order (merged.py:13-45).
 //
-// The weight stream is the whole cost (HBM-bound: every weight byte is read once per
-// step), so the kernel is a TMA pipeline: one producer lane loads 128x64 weight tiles
-// and the matching Mx64 slab of x (rows past M are zero-filled by the tensor map) into
-// an NS-stage ring of 128-byte-swizzled buffers; four consumer warps each own 32 output
-// features and run mma.sync m16n8k16 with x as the 16-row A operand and W rows as B.
-// Grid = (N / 128 tiles) x (K splits); the split count is chosen on the host so that the
-// grid fills whole waves of the machine.
+// The weight stream is the whole cost (HBM-bound: every weight byte is read once per step):
+//  * Grid = (N / 128 tiles) x S K-splits, two CTAs per SM; S (fb_linear_splits) fills whole
+//    waves of the machine. One producer lane TMA-loads 128x64 weight tiles (L2 evict-first)
+//    and the matching M x 64 slab of x (rows past M zero-filled by the tensor map) into a
+//    6-stage mbarrier ring of 128-byte-swizzled buffers; four consumer warps each own 32 output
+//    features and run mma.sync m16n8k16 with x as the 16-row A operand.
+//  * Launched with programmatic stream serialization: the producer issues the weight stages
+//    before griddepcontrol.wait, so the stream overlaps the previous kernel's tail; nothing an
+//    earlier kernel wrote is read before the wait.
+//  * Epilogues: fp32 split partials [S, M, N]; or a finished tile - bf16, fp32, SwiGLU on
+//    weights packed as 64-row gate/up blocks, or (tensor parallelism) the fp32 tile pushed into
+//    every peer's receive buffer over NVLink followed by a release-increment of each peer's
+//    arrival counter. With S > 1 (S <= 8) the S CTAs of a tile form a thread-block cluster:
+//    each parks its fp32 partial tile in its own shared memory, and after a cluster barrier
+//    every CTA sums its share of the tile's columns over the cluster's CTAs in rank order
+//    through distributed shared memory (deterministic, no global round trip, no atomics),
+//    then runs the epilogue for that share. No workspace.
 #include "common.cuh"
 
 namespace fb {
@@ -21,40 +31,145 @@ constexpr int kTileK = 64;
 constexpr int kConsumerWarps = 4;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kStages = 6;
+constexpr int kMaxPeers = 8;
+constexpr int kMaxTiles = 65535;       // grid x
+constexpr int kMaxClusterSplits = 8;  // portable cluster size: K-splits of one finished tile
+
+enum Epilogue : int { kBf16 = 0, kFp32 = 1, kSwiGLU = 2, kSplits = 3, kPush = 4 };
 
 struct Params {
   void* out;
-  int m, n, k, splits, out_fp32;
+  int m, n, k, splits, epilogue;
+  // kPush: fp32 tile into recv[use][rank][m][n] of every peer, then counter[use] += 1 there
+  int world, rank, use;
+  float* peer_recv[kMaxPeers];
+  unsigned* peer_counter[kMaxPeers];
   unsigned* err;
 };
 
 template <int MT>
 struct Smem {
+  static constexpr int MP = MT * 16;
   static constexpr int kWBytes = kTileN * 128;
-  static constexpr int kXBytes = MT * 16 * 128;
+  static constexpr int kXBytes = MP * 128;
   static constexpr int kStageBytes = kWBytes + kXBytes;
-  static constexpr int kTotal = 1024 + kStages * kStageBytes + 2 * kStages * 8 + 16;
+  static constexpr int kTileVals = MP * kTileN * 4;  // staged in the drained stage buffers
+  static_assert(kTileVals <= kStages * kStageBytes, "tile values must fit the stage ring");
+  static constexpr int kTotal = 1024 + kStages * kStageBytes + 2 * kStages * 8 + 64;
 };
+
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address of the same shared-memory offset in the cluster CTA of rank `rank`.
+__device__ __forceinline__ uint32_t map_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ float silu_bf16(float g) {
+  // engine/kernels/swiglu.py:21: SiLU computed in fp32 and rounded to bf16
+  return bf16_round(g / (1.0f + expf(-g)));
+}
+
+// Column groups (4 fp32 columns) of a tile owned by cluster rank r of S: group cg, or for
+// SwiGLU the feature group cg % 16 (gate columns and the matching up columns together).
+__device__ __forceinline__ bool owned(int cg, int epi, int r, int S) {
+  return ((epi == kSwiGLU ? (cg & 15) : cg) % S) == r;
+}
+
+// Epilogue over a finished tile held in shared memory (vals[MP][128], fp32), for the column
+// groups this CTA owns (all of them when the tile was not split).
+template <int MT>
+__device__ void epilogue(const Params& p, const float* vals, int tile, int tid, int r, int S) {
+  constexpr int MP = MT * 16;
+  const int n0 = tile * kTileN;
+  if (p.epilogue == kSwiGLU) {
+    // Tile rows [0, 64) are gate features f0..f0+63 and rows [64, 128) the up features of the
+    // same f: out[m][f] = bf16(bf16(silu(bf16(g))) * bf16(u)).
+    const int f0 = tile * (kTileN / 2);
+    const int width = p.n / 2;
+    for (int e = tid; e < p.m * (kTileN / 2); e += kConsumerWarps * 32) {
+      const int m = e / (kTileN / 2), j = e % (kTileN / 2);
+      if (f0 + j >= width || !owned(j >> 2, kSwiGLU, r, S)) continue;
+      const float g = bf16_round(vals[m * kTileN + j]);
+      const float u = bf16_round(vals[m * kTileN + 64 + j]);
+      static_cast<__nv_bfloat16*>(p.out)[static_cast<size_t>(m) * width + f0 + j] =
+          __float2bfloat16_rn(silu_bf16(g) * u);
+    }
+    return;
+  }
+  if (p.epilogue == kPush) {
+    const size_t slab = static_cast<size_t>(p.m) * p.n;
+    for (int e = tid; e < p.m * (kTileN / 4); e += kConsumerWarps * 32) {
+      const int m = e / (kTileN / 4), c4 = e % (kTileN / 4);
+      if (n0 + c4 * 4 >= p.n || !owned(c4, kPush, r, S)) continue;
+      const float4 v = *reinterpret_cast<const float4*>(vals + m * kTileN + c4 * 4);
+      const size_t off = (static_cast<size_t>(p.use) * p.world + p.rank) * slab + static_cast<size_t>(m) * p.n +
+                         n0 + c4 * 4;
+      for (int r = 0; r < p.world; ++r) *reinterpret_cast<float4*>(p.peer_recv[r] + off) = v;
+    }
+    return;
+  }
+  for (int e = tid; e < p.m * (kTileN / 4); e += kConsumerWarps * 32) {
+    const int m = e / (kTileN / 4), c4 = e % (kTileN / 4);
+    const int col = n0 + c4 * 4;
+    if (col >= p.n || !owned(c4, p.epilogue, r, S)) continue;
+    const float4 v = *reinterpret_cast<const float4*>(vals + m * kTileN + c4 * 4);
+    if (p.epilogue == kFp32) {
+      *reinterpret_cast<float4*>(static_cast<float*>(p.out) + static_cast<size_t>(m) * p.n + col) = v;
+    } else {
+      uint2 w;
+      w.x = pack_bf16x2(v.x, v.y);
+      w.y = pack_bf16x2(v.z, v.w);
+      *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(m) * p.n + col) = w;
+    }
+  }
+  (void)MP;
+}
 
 template <int MT>
 __global__ void __launch_bounds__(kThreads)
     linear_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
-                  const Params p) {
+                  const __grid_constant__ Params p) {
   using S = Smem<MT>;
+  constexpr int MP = S::MP;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
+  float* vals = reinterpret_cast<float*>(base);  // reused once the ring has drained
   uint64_t* full = reinterpret_cast<uint64_t*>(base + kStages * S::kStageBytes);
   uint64_t* empty = full + kStages;
-  volatile int* abort_flag = reinterpret_cast<int*>(empty + kStages);
+  volatile int* flags = reinterpret_cast<volatile int*>(empty + kStages);  // [0] abort, [1] last
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * kTileN;
-  const int split = blockIdx.y;
+  const int tile = blockIdx.x, split = blockIdx.y;
+  const int n0 = tile * kTileN;
   const int chunks = (p.k + kTileK - 1) / kTileK;
   const int c0 = static_cast<int>((static_cast<long long>(chunks) * split) / p.splits);
   const int c1 = static_cast<int>((static_cast<long long>(chunks) * (split + 1)) / p.splits);
   const int count = c1 - c0;
+  // finished-tile epilogues reduce the K-splits of a tile across its cluster (dims 1 x S)
+  const bool clustered = p.epilogue != kSplits && p.splits > 1;
 
   if (warp == kConsumerWarps && lane == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -64,56 +179,68 @@ __global__ void __launch_bounds__(kThreads)
     fence_barrier_init();
     prefetch_tensormap(&xmap);
     prefetch_tensormap(&wmap);
-    *abort_flag = 0;
+    flags[0] = 0;
   }
   __syncthreads();
+  grid_launch_dependents();
 
   if (warp == kConsumerWarps) {
     if (lane == 0) {
       const uint64_t evict_first = l2_evict_first_policy();
-      for (int i = 0; i < count; ++i) {
+      // Weights do not depend on the previous kernel: fill the ring before waiting on it.
+      const int pre = count < kStages ? count : kStages;
+      for (int i = 0; i < pre; ++i) {
+        mbar_arrive_expect_tx(&full[i], S::kStageBytes);
+        tma_load_2d_hint(base + i * S::kStageBytes, &wmap, &full[i], (c0 + i) * kTileK, n0, evict_first);
+      }
+      grid_dependency_wait();
+      for (int i = 0; i < pre; ++i)
+        tma_load_2d(base + i * S::kStageBytes + S::kWBytes, &xmap, &full[i], (c0 + i) * kTileK, 0);
+      for (int i = pre; i < count; ++i) {
         const int s = i % kStages;
-        if (*abort_flag) break;
-        if (i >= kStages && !mbar_wait_bounded(&empty[s], ((i / kStages) - 1) & 1)) {
+        if (flags[0]) break;
+        if (!mbar_wait_bounded(&empty[s], ((i / kStages) - 1) & 1)) {
           raise_error(p.err, kErrTimeoutEmpty);
-          *abort_flag = 1;
+          flags[0] = 1;
           break;
         }
         uint8_t* wt = base + s * S::kStageBytes;
-        uint8_t* xt = wt + S::kWBytes;
         mbar_arrive_expect_tx(&full[s], S::kStageBytes);
-        const int kx = (c0 + i) * kTileK;
-        tma_load_2d_hint(wt, &wmap, &full[s], kx, n0, evict_first);
-        tma_load_2d(xt, &xmap, &full[s], kx, 0);
+        tma_load_2d_hint(wt, &wmap, &full[s], (c0 + i) * kTileK, n0, evict_first);
+        tma_load_2d(wt + S::kWBytes, &xmap, &full[s], (c0 + i) * kTileK, 0);
       }
+    }
+    __syncwarp();
+    if (clustered) {
+      // every thread of every CTA in the cluster takes the same two cluster barriers
+      cluster_sync();
+      cluster_sync();
     }
     return;
   }
 
-  const int g = lane >> 2, c = lane & 3;
+  grid_dependency_wait();  // outputs may be read by the previous kernel
+  const int g = lane >> 2, c4 = lane & 3;
+  const int tid = threadIdx.x;
+  const int q = lane >> 3;
+  const int a_row = (lane & 7) + (q & 1) * 8, a_kc = q >> 1;
+  const int b_row = (lane & 7) + (q >> 1) * 8, b_kc = q & 1;
   float acc[MT][4][4];
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt) acc[mt][nt][0] = acc[mt][nt][1] = acc[mt][nt][2] = acc[mt][nt][3] = 0.f;
-
-  // ldmatrix lane roles
-  const int q = lane >> 3;  // matrix index within an x4 load
-  // A (x): matrices (rows 0-7,k0-7) (rows 8-15,k0-7) (rows 0-7,k8-15) (rows 8-15,k8-15)
-  const int a_row = (lane & 7) + (q & 1) * 8;
-  const int a_kc = q >> 1;
-  // B (W): matrices (n 0-7,k0-7) (n 0-7,k8-15) (n 8-15,k0-7) (n 8-15,k8-15)
-  const int b_row = (lane & 7) + (q >> 1) * 8;
-  const int b_kc = q & 1;
-
+  bool aborted = false;
   for (int i = 0; i < count; ++i) {
     const int s = i % kStages;
     if (!mbar_wait_bounded(&full[s], (i / kStages) & 1)) {
       raise_error(p.err, kErrTimeoutFull);
-      *abort_flag = 1;
+      flags[0] = 1;
+    }
+    if (flags[0]) {
+      aborted = true;  // still takes the cluster barriers below
       break;
     }
-    if (*abort_flag) break;
     const uint32_t wt = smem_u32(base + s * S::kStageBytes);
     const uint32_t xt = wt + S::kWBytes;
 #pragma unroll
@@ -121,8 +248,7 @@ __global__ void __launch_bounds__(kThreads)
       uint32_t a[MT][4];
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt)
-        ldmatrix_x4(xt + sw128(mt * 16 + a_row, ks * 2 + a_kc), a[mt][0], a[mt][1], a[mt][2],
-                    a[mt][3]);
+        ldmatrix_x4(xt + sw128(mt * 16 + a_row, ks * 2 + a_kc), a[mt][0], a[mt][1], a[mt][2], a[mt][3]);
 #pragma unroll
       for (int np = 0; np < 2; ++np) {
         uint32_t b0, b1, b2, b3;
@@ -137,30 +263,83 @@ __global__ void __launch_bounds__(kThreads)
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
   }
+  if (aborted && !clustered) return;
 
-  // Epilogue: C fragment rows (g, g+8) x cols (2c, 2c+1) of each 16x8 tile.
+  if (p.epilogue == kSplits) {
+    // fp32 partials [S, M, N]: C fragment rows (g, g+8), columns (2c, 2c+1) of each 16x8 tile
 #pragma unroll
-  for (int mt = 0; mt < MT; ++mt) {
+    for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
-      const int col = n0 + warp * 32 + nt * 8 + 2 * c;
-      if (col >= p.n) continue;
+      for (int nt = 0; nt < 4; ++nt) {
+        const int col = n0 + warp * 32 + nt * 8 + 2 * c4;
+        if (col >= p.n) continue;
 #pragma unroll
-      for (int hlf = 0; hlf < 2; ++hlf) {
-        const int row = mt * 16 + g + hlf * 8;
-        if (row >= p.m) continue;
-        const float v0 = acc[mt][nt][hlf * 2 + 0], v1 = acc[mt][nt][hlf * 2 + 1];
-        if (p.splits == 1 && !p.out_fp32) {
-          *reinterpret_cast<uint32_t*>(static_cast<__nv_bfloat16*>(p.out) +
-                                       static_cast<size_t>(row) * p.n + col) = pack_bf16x2(v0, v1);
-        } else {
-          float* dst = static_cast<float*>(p.out) +
-                       (static_cast<size_t>(split) * p.m + row) * p.n + col;
-          *reinterpret_cast<float2*>(dst) = make_float2(v0, v1);
+        for (int hlf = 0; hlf < 2; ++hlf) {
+          const int row = mt * 16 + g + hlf * 8;
+          if (row >= p.m) continue;
+          float* dst = static_cast<float*>(p.out) + (static_cast<size_t>(split) * p.m + row) * p.n + col;
+          *reinterpret_cast<float2*>(dst) = make_float2(acc[mt][nt][hlf * 2], acc[mt][nt][hlf * 2 + 1]);
         }
       }
-    }
+    return;
   }
+
+  // ---- finished-tile epilogues: this split's sums -> shared tile (the ring has drained) ----
+  asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      const int col = warp * 32 + nt * 8 + 2 * c4;
+      *reinterpret_cast<float2*>(vals + (mt * 16 + g) * kTileN + col) = make_float2(acc[mt][nt][0], acc[mt][nt][1]);
+      *reinterpret_cast<float2*>(vals + (mt * 16 + g + 8) * kTileN + col) = make_float2(acc[mt][nt][2], acc[mt][nt][3]);
+    }
+  if (!clustered) {
+    asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+    epilogue<MT>(p, vals, tile, tid, 0, 1);
+    if (p.epilogue == kPush) {
+      // the pushed values must be visible on every peer before its counter moves
+      __threadfence_system();
+      asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+      if (tid < p.world)
+        asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(p.peer_counter[tid] + p.use) : "memory");
+    }
+    return;
+  }
+  // Split tile: sum the S partials through distributed shared memory. Rank r sums the column
+  // groups it owns over ranks 0..S-1 in order (deterministic) into its own tile, then runs
+  // the epilogue for those groups.
+  cluster_sync();  // every CTA's partial tile is complete and visible cluster-wide
+  const int r = static_cast<int>(cluster_rank());
+  const int nsplit = p.splits;
+  if (!aborted) {
+    const uint32_t local = smem_u32(vals);
+    for (int e = tid; e < p.m * (kTileN / 4); e += kConsumerWarps * 32) {
+      const int m = e / (kTileN / 4), cg = e % (kTileN / 4);
+      if (!owned(cg, p.epilogue, r, nsplit)) continue;
+      const uint32_t off = static_cast<uint32_t>((m * kTileN + cg * 4) * 4);
+      float4 parts[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        if (q < nsplit) parts[q] = ld_cluster_f4(map_shared(local + off, q));
+      float4 sum = parts[0];
+#pragma unroll
+      for (int q = 1; q < 8; ++q)
+        if (q < nsplit) {
+          sum.x += parts[q].x;
+          sum.y += parts[q].y;
+          sum.z += parts[q].z;
+          sum.w += parts[q].w;
+        }
+      *reinterpret_cast<float4*>(vals + m * kTileN + cg * 4) = sum;
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+    epilogue<MT>(p, vals, tile, tid, r, nsplit);
+    if (p.epilogue == kPush) __threadfence_system();
+  }
+  cluster_sync();  // no CTA leaves while another may still read its tile; pushes are done
+  if (p.epilogue == kPush && r == 0 && tid < p.world && !aborted)
+    asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(p.peer_counter[tid] + p.use) : "memory");
 }
 
 template <int MT>
@@ -170,14 +349,38 @@ int launch(const CUtensorMap& xm, const CUtensorMap& wm, const Params& p, cudaSt
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !configured[dev]) {
-    if (cudaFuncSetAttribute(linear_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             S::kTotal) != cudaSuccess)
+    if (cudaFuncSetAttribute(linear_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal) !=
+        cudaSuccess)
       return FB_ERR_LAUNCH;
     configured[dev] = true;
   }
-  dim3 grid((p.n + kTileN - 1) / kTileN, p.splits);
-  linear_kernel<MT><<<grid, kThreads, S::kTotal, stream>>>(xm, wm, p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((p.n + kTileN - 1) / kTileN, p.splits);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = S::kTotal;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (p.epilogue != kSplits && p.splits > 1) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = p.splits;
+    attr[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
+  }
+  if (cudaLaunchKernelEx(&cfg, linear_kernel<MT>, xm, wm, p) != cudaSuccess) return FB_ERR_LAUNCH;
   return check_launch();
+}
+
+int row_tiles(int m) { return m <= 16 ? 1 : m <= 32 ? 2 : 4; }
+
+int ctas_per_sm(int mt) {
+  const int total = mt == 1 ? Smem<1>::kTotal : mt == 2 ? Smem<2>::kTotal : Smem<4>::kTotal;
+  int per = (227 * 1024) / (total + 1024);
+  return per < 1 ? 1 : per;
 }
 
 }  // namespace lin
@@ -189,50 +392,68 @@ extern "C" int fb_linear_splits(int m, int n, int k) {
   if (m <= 0 || n <= 0 || k <= 0) return 1;
   const int tiles = (n + lin::kTileN - 1) / lin::kTileN;
   const int chunks = (k + lin::kTileK - 1) / lin::kTileK;
-  const int mt = m <= 16 ? 1 : m <= 32 ? 2 : 4;
-  const int stage = lin::kTileN * 128 + mt * 16 * 128;
-  const int per_sm = (227 * 1024) / (1024 + lin::kStages * stage + 128);
-  const int slots = sm_count() * (per_sm > 0 ? per_sm : 1);
-  // Modelled time ~ waves * (chunks per CTA + fixed ramp of ~2 chunks); pick the best S
-  // with at least 4 chunks per CTA so the pipeline fills.
-  int best = 1;
-  double best_cost = 1e30;
-  for (int s = 1; s <= 32; ++s) {
-    if (chunks / s < 4 && s > 1) break;
-    const int ctas = tiles * s;
-    const int waves = (ctas + slots - 1) / slots;
-    const double per_cta = static_cast<double>(chunks) / s + 2.0;
-    const double cost = waves * per_cta + (s > 1 ? 0.02 * s * m : 0.0);
-    if (cost < best_cost - 1e-9) {
-      best_cost = cost;
-      best = s;
-    }
-  }
-  return best;
+  const int slots = sm_count() * lin::ctas_per_sm(lin::row_tiles(m));
+  // One wave: the most splits whose CTAs are all resident at once (a second, partial wave
+  // costs more than the extra streams gain), keeping at least 4 chunks per CTA so each
+  // pipeline fills. Measured on B200 at M=16: N=4096/K=4096 -> 9 (7.3 us), N=6144 -> 6
+  // (9.3 us), N=24576 -> 1 (36 us); every other S was slower or within noise.
+  int best = tiles >= slots ? 1 : slots / tiles;
+  if (best > chunks / 4) best = chunks / 4;
+  return best < 1 ? 1 : best;
 }
 
-extern "C" int fb_linear(const void* x, const void* w, void* out, int m, int n, int k, int splits,
-                         int out_fp32, void* stream) {
+static int linear_impl(const void* x, const void* w, void* out, int m, int n, int k, int epilogue, int splits,
+                       void* stream, int world, int rank, int use, void* const* peer_recv,
+                       void* const* peer_counter) {
   if (!x || !w || !out || m <= 0 || n <= 0 || k <= 0 || splits <= 0) return FB_ERR_ARG;
   if (m > 64 || k % 8 != 0 || n % 8 != 0) return FB_ERR_SHAPE;
-  const int chunks = (k + lin::kTileK - 1) / lin::kTileK;
-  if (splits > chunks) return FB_ERR_SHAPE;
-  const int mt = m <= 16 ? 1 : m <= 32 ? 2 : 4;
+  if ((n + lin::kTileN - 1) / lin::kTileN > lin::kMaxTiles) return FB_ERR_SHAPE;
+  if (epilogue == lin::kSwiGLU && n % lin::kTileN != 0) return FB_ERR_SHAPE;
+  if (splits > (k + lin::kTileK - 1) / lin::kTileK || splits > 65535) return FB_ERR_SHAPE;
+  if (epilogue != lin::kSplits && splits > lin::kMaxClusterSplits) return FB_ERR_SHAPE;
+  const int mt = lin::row_tiles(m);
   CUtensorMap xm, wm;
   int st = encode_bf16_2d(&xm, x, m, k, k, 64, mt * 16, true);
   if (st != FB_OK) return st;
   st = encode_bf16_2d(&wm, w, n, k, k, 64, lin::kTileN, true);
   if (st != FB_OK) return st;
-  lin::Params p;
+  lin::Params p{};
   p.out = out;
   p.m = m;
   p.n = n;
   p.k = k;
   p.splits = splits;
-  p.out_fp32 = out_fp32;
+  p.epilogue = epilogue;
+  p.world = world;
+  p.rank = rank;
+  p.use = use;
+  if (epilogue == lin::kPush) {  // only the push form has peer buffers
+    for (int r = 0; r < world && r < lin::kMaxPeers; ++r) {
+      p.peer_recv[r] = static_cast<float*>(peer_recv[r]);
+      p.peer_counter[r] = static_cast<unsigned*>(peer_counter[r]);
+    }
+  }
   p.err = error_word();
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (mt == 1) return lin::launch<1>(xm, wm, p, s);
   if (mt == 2) return lin::launch<2>(xm, wm, p, s);
   return lin::launch<4>(xm, wm, p, s);
+}
+
+extern "C" int fb_linear(const void* x, const void* w, void* out, int m, int n, int k, int epilogue, int splits,
+                         void* stream) {
+  if (epilogue < lin::kBf16 || epilogue > lin::kSplits) return FB_ERR_ARG;
+  return linear_impl(x, w, out, m, n, k, epilogue, splits, stream, 1, 0, 0, nullptr, nullptr);
+}
+
+extern "C" int fb_linear_allreduce_push(const void* x, const void* w, int m, int n, int k, int splits, int world,
+                                        int rank, int use,
+                                        void* const* peer_recv, void* const* peer_counter, void* stream) {
+  if (world < 1 || world > lin::kMaxPeers || rank < 0 || rank >= world || use < 0) return FB_ERR_ARG;
+  if (!peer_recv || !peer_counter) return FB_ERR_ARG;
+  for (int r = 0; r < world; ++r)
+    if (!peer_recv[r] || !peer_counter[r] || (reinterpret_cast<uintptr_t>(peer_recv[r]) & 15u)) return FB_ERR_ARG;
+  // the kernel writes nothing through `out` in this mode; pass a valid dummy
+  return linear_impl(x, w, const_cast<void*>(x), m, n, k, lin::kPush, splits, stream, world, rank, use, peer_recv,
+                     peer_counter);
 }

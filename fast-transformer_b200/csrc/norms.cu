@@ -220,6 +220,95 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
+// Tensor-parallel all-reduce consumer fused with the residual add + RMSNorm. Every rank's
+// projection kernel pushed its fp32 [rows, W] partial into slab `rank` of this rank's
+// recv[use] and added one arrival per 128-column tile to arrivals[use]; once all
+// world * tiles arrivals are in, the slabs are summed in rank order (identical bits on every
+// rank), rounded to bf16 (the projection's output) and fed to add_rms_norm's arithmetic.
+// The last CTA to finish resets the use's arrival and completion counters for the next step.
+struct ReduceParams {
+  const float* recv;        // [uses, world, rows, W] on this rank
+  unsigned* arrivals;       // [uses] on this rank, bumped by every rank's producer
+  unsigned* done;           // [uses] on this rank
+  int use, world, expected;
+  const __nv_bfloat16* residual;
+  const __nv_bfloat16* w;
+  __nv_bfloat16* out;
+  __nv_bfloat16* sum;
+  int rows, width;
+  float eps;
+  unsigned* err;
+};
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__global__ void __launch_bounds__(kThreads) allreduce_add_rmsnorm_kernel(const ReduceParams p) {
+  __shared__ float scratch[kThreads / 32];
+  __shared__ int ok;
+  const int row = blockIdx.x;
+  if (threadIdx.x == 0) {
+    const unsigned long long start = globaltimer();
+    // After one wait has given up, fail fast instead of spending the budget again per use.
+    int good = p.err == nullptr || (*reinterpret_cast<volatile unsigned*>(p.err) & kErrTimeoutFull) == 0;
+    while (good && ld_acquire_sys(p.arrivals + p.use) < static_cast<unsigned>(p.expected)) {
+      if (globaltimer() - start > kWaitBudgetNs) {
+        raise_error(p.err, kErrTimeoutFull);
+        good = 0;
+        break;
+      }
+    }
+    ok = good;
+  }
+  __syncthreads();
+  const int chunks = p.width / 8;
+  const size_t slab = static_cast<size_t>(p.rows) * p.width;
+  const float* recv = p.recv + static_cast<size_t>(p.use) * p.world * slab + static_cast<size_t>(row) * p.width;
+  float v[kMaxChunks][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxChunks; ++i) {
+    const int ch = threadIdx.x + i * kThreads;
+    if (ch < chunks && ok) {
+      float x[8];
+      // rank-order fp32 sum of the partials, then the projection's bf16 rounding
+      load8(recv, p.world, slab, static_cast<size_t>(ch) * 8, x);
+      float r[8];
+      load8(p.residual, 0, 0, static_cast<size_t>(row) * p.width + ch * 8, r);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[i][e] = bf16_round(x[e] + r[e]);
+      store8(p.sum + static_cast<size_t>(row) * p.width + ch * 8, v[i]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += v[i][e] * v[i][e];
+    }
+  }
+  ss = block_sum(ss, scratch);
+  const float inv = 1.0f / sqrtf(ss / static_cast<float>(p.width) + p.eps);
+#pragma unroll
+  for (int i = 0; i < kMaxChunks; ++i) {
+    const int ch = threadIdx.x + i * kThreads;
+    if (ch < chunks && ok) {
+      float w[8], y[8];
+      load_w8(p.w, ch * 8, w);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) y[e] = bf16_round(v[i][e] * inv) * w[e];
+      store8(p.out + static_cast<size_t>(row) * p.width + ch * 8, y);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(p.done + p.use, 1u) == static_cast<unsigned>(gridDim.x) - 1) {
+      // every row has read this use's slabs: ready for the next step
+      p.done[p.use] = 0;
+      atomicExch(p.arrivals + p.use, 0u);
+    }
+  }
+}
+
 int check_width(int width) {
   if (width <= 0 || width % 8 != 0) return FB_ERR_SHAPE;
   if (width > 8 * kThreads * kMaxChunks) return FB_ERR_SHAPE;
@@ -312,5 +401,31 @@ extern "C" int fb_merge_splits(const void* partial, int splits, int64_t count, v
   const int blocks = static_cast<int>((threads + norm::kThreads - 1) / norm::kThreads);
   norm::merge_kernel<<<blocks, norm::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const float*>(partial), splits, count, out, out_fp32);
+  return check_launch();
+}
+
+extern "C" int fb_allreduce_add_rmsnorm(const void* recv, void* arrivals, void* done, int use, int world,
+                                        int expected, const void* residual, const void* w, void* out, void* sum,
+                                        int rows, int width, float eps, void* stream) {
+  if (!recv || !arrivals || !done || !residual || !w || !out || !sum) return FB_ERR_ARG;
+  if (use < 0 || world < 1 || expected < 1 || rows <= 0) return FB_ERR_ARG;
+  int st = norm::check_width(width);
+  if (st != FB_OK) return st;
+  norm::ReduceParams p;
+  p.recv = static_cast<const float*>(recv);
+  p.arrivals = static_cast<unsigned*>(arrivals);
+  p.done = static_cast<unsigned*>(done);
+  p.use = use;
+  p.world = world;
+  p.expected = expected;
+  p.residual = static_cast<const __nv_bfloat16*>(residual);
+  p.w = static_cast<const __nv_bfloat16*>(w);
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.sum = static_cast<__nv_bfloat16*>(sum);
+  p.rows = rows;
+  p.width = width;
+  p.eps = eps;
+  p.err = error_word();
+  norm::allreduce_add_rmsnorm_kernel<<<rows, norm::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
   return check_launch();
 }

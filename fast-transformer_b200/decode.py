@@ -9,10 +9,15 @@ then the final norm, LM head and argmax, and a device-side `position += 1`. Pref
 eagerly through cuBLAS and torch SDPA for the big GEMMs and prompt attention (as the
 reference's prefill does, engine/layers.py:69-74), with the fused kernel writing the cache.
 
-Tensor parallelism (by KV head, see qwen3.py): the o_proj and down_proj outputs are
-reduced across ranks with one NCCL all-reduce each (fp32, inside the captured graph); every
-rank then runs the same norms, LM head and argmax on identical data.
+Tensor parallelism (by KV head, see qwen3.py): o_proj and down_proj run as
+fb_linear_allreduce_push, which stores every finished fp32 output tile straight into each
+rank's receive buffer (torch symmetric memory, NVLink peer stores) and bumps that rank's
+arrival counter; fb_allreduce_add_rmsnorm then sums the ranks' slabs in rank order and applies
+the residual add + RMSNorm. Every rank therefore runs the same norms, LM head and argmax on
+bit-identical data. Prefill (eager, untimed) uses NCCL all-reduces.
 """
+
+import ctypes
 
 import math
 
@@ -22,12 +27,14 @@ import torch.nn.functional as F
 from kernels import _native
 from kernels.argmax import argmax
 from kernels.decode_attention import attend as attend_decode
-from kernels.linear import linear, merge, project, splits_for, supported
+from kernels import linear as klinear
+from kernels.linear import linear, swiglu_linear
 from kernels.merged import Split
 from kernels.qk_rope import qk_rope_cache
 from kernels.rmsnorm import add_rms_norm, embed_rms_norm
 from kernels.swiglu import swiglu
 from kernels._native import check, lib, ptr, stream
+import qwen3
 
 BF16 = torch.bfloat16
 
@@ -65,15 +72,57 @@ class _Norm:
 
 
 class Communicator:
-    """Sum-all-reduce over the tensor-parallel group (torch.distributed / NCCL); identity at TP 1."""
+    """The tensor-parallel group: identity at TP 1; NCCL all-reduce for prefill."""
 
-    def __init__(self, group=None, size=1):
-        self.group, self.size = group, size
+    def __init__(self, group=None, size=1, rank=0):
+        self.group, self.size, self.rank = group, size, rank
 
     def all_reduce(self, tensor):
         if self.size > 1:
             torch.distributed.all_reduce(tensor, group=self.group)
         return tensor
+
+
+class PeerBuffers:
+    """Receive slabs fp32 [uses, world, rows, width] + arrival/done counters uint32 [uses] in
+    torch symmetric memory, with every rank's base address for NVLink peer stores."""
+
+    def __init__(self, comm, uses, rows, width, device):
+        import os
+        # Plain peer mappings only: no NVLink multicast object behind these buffers.
+        os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
+        import torch.distributed._symmetric_memory as symm_mem
+        world = comm.size
+        self.uses, self.world, self.rows, self.width = uses, world, rows, width
+        recv = uses * world * rows * width * 4
+        self.recv_bytes = (recv + 255) // 256 * 256
+        total = self.recv_bytes + 2 * ((uses * 4 + 255) // 256 * 256)
+        group = comm.group if comm.group is not None else torch.distributed.group.WORLD
+        if hasattr(symm_mem, "enable_symm_mem_for_group"):
+            try:
+                symm_mem.enable_symm_mem_for_group(group.group_name)
+            except Exception:  # noqa: BLE001 - newer torch enables groups on demand
+                pass
+        self.buf = symm_mem.empty(total, dtype=torch.uint8, device=device)
+        self.buf.zero_()
+        torch.cuda.synchronize(device)
+        handle = symm_mem.rendezvous(self.buf, group)
+        bases = [int(b) for b in handle.buffer_ptrs]
+        self.handle = handle
+        self.multicast = bool(handle.has_multicast_support())
+        self.recv_ptrs = (ctypes.c_void_p * world)(*bases)
+        self.arrival_ptrs = (ctypes.c_void_p * world)(*[b + self.recv_bytes for b in bases])
+        local = self.buf.data_ptr()
+        self.recv_local = ctypes.c_void_p(local)
+        self.arrivals_local = ctypes.c_void_p(local + self.recv_bytes)
+        self.done_local = ctypes.c_void_p(local + self.recv_bytes + (uses * 4 + 255) // 256 * 256)
+        self.tiles = (width + 127) // 128
+        torch.distributed.barrier(group=group)
+
+    def reset(self):
+        """Zero every counter (between generations, with all ranks idle)."""
+        self.buf[self.recv_bytes:].zero_()
+        torch.cuda.synchronize()
 
 
 def _qk_rope_decode(packed, layer, eps, cos, sin, position, keys, values, q_heads):
@@ -90,16 +139,26 @@ def _qk_rope_decode(packed, layer, eps, cos, sin, position, keys, values, q_head
     return query.view(batch, q_heads, 1, dim)  # one token: token-major storage is [B, Hq, 1, D]
 
 
-def _project_reduced(x, weight, comm):
-    """x @ W^T summed over the TP group, as a one-slab FP32 ``Split`` for the next consumer."""
+def _push_projection(x, weight, comm, peers, use):
+    """This rank's fp32 partial of x @ W^T, pushed to every rank's recv[use] (fb_linear_allreduce_push)."""
     rows = x.numel() // x.shape[-1]
-    flat = x.reshape(rows, x.shape[-1])
+    flat = x.reshape(rows, x.shape[-1]).contiguous()
     n, k = weight.shape
-    splits = splits_for(rows, n, k, x.device)
-    part = project(flat, weight, splits, out_fp32=True)
-    total = part if splits == 1 else merge(part, out_fp32=True).view(1, rows, n)
-    comm.all_reduce(total)
-    return Split(total, (*x.shape[:-1], n))
+    splits = klinear.splits_for(rows, n, k, x.device, finished=True)
+    check(lib.fb_linear_allreduce_push(ptr(flat), ptr(weight), rows, n, k, splits, comm.size, comm.rank, use,
+                                       peers.recv_ptrs, peers.arrival_ptrs, stream()),
+          "fb_linear_allreduce_push")
+
+
+def _reduce_add_norm(peers, use, residual, weight, eps):
+    """(normalized, summed) = add_rms_norm(all-reduced recv[use], residual) (fb_allreduce_add_rmsnorm)."""
+    rows, width = residual.numel() // residual.shape[-1], residual.shape[-1]
+    out = torch.empty_like(residual)
+    summed = torch.empty_like(residual)
+    check(lib.fb_allreduce_add_rmsnorm(peers.recv_local, peers.arrivals_local, peers.done_local, use, peers.world,
+                                       peers.world * peers.tiles, ptr(residual), ptr(weight), ptr(out), ptr(summed),
+                                       rows, width, float(eps), stream()), "fb_allreduce_add_rmsnorm")
+    return out, summed
 
 
 class DecodeState:
@@ -130,17 +189,20 @@ class DecodeState:
             int(lib.fb_decode_attention_workspace(batch, weights.q_heads, weights.kv_heads, cfg.head_dim, self.ctas)),
             dtype=torch.uint8, device=self.device)
         self.attn_out = torch.empty((batch, 1, weights.q_heads, cfg.head_dim), dtype=BF16, device=self.device)
+        self.peers = None
+        if self.comm.size > 1:
+            self.peers = PeerBuffers(self.comm, 2 * cfg.num_hidden_layers, batch, cfg.hidden_size, self.device)
 
     # ------------------------------------------------------------------ decode step
     def decode(self):
         """One greedy step for every row (the captured body)."""
-        w, cfg, cache, comm = self.w, self.cfg, self.cache, self.comm
+        w, cfg, cache, comm, peers = self.w, self.cfg, self.cache, self.comm, self.peers
         eps = cfg.rms_norm_eps
-        tp = comm.size > 1
-        normalized, residual = embed_rms_norm(self.token_ids, w.embed, w.layers[0].ln1, eps)
+        layers = w.layers
+        normalized, residual = embed_rms_norm(self.token_ids, w.embed, layers[0].ln1, eps)
         hidden = None
-        for index, layer in enumerate(w.layers):
-            if index > 0:
+        for index, layer in enumerate(layers):
+            if index > 0 and peers is None:
                 normalized, residual = add_rms_norm(hidden, residual, layer.ln1, eps)
             packed = linear(normalized, layer.qkv, split_ok=True)
             query = _qk_rope_decode(packed, layer, eps, self.cos, self.sin, self.position,
@@ -148,18 +210,21 @@ class DecodeState:
             attention = attend_decode(query, cache.keys[index], cache.values[index], self.position, self.scale,
                                       out=self.attn_out, workspace=self.workspace, ctas=self.ctas)
             attention = attention.reshape(self.batch, 1, -1)
-            if tp:
-                out = _project_reduced(attention, layer.o, comm)
-            else:
+            if peers is None:
                 out = linear(attention, layer.o, split_ok=True)
-            normalized, residual = add_rms_norm(out, residual, layer.ln2, eps)
-            gate_up = linear(normalized, layer.gate_up, split_ok=True)
-            activated = swiglu(gate_up)
-            if tp:
-                hidden = _project_reduced(activated, layer.down, comm)
+                normalized, residual = add_rms_norm(out, residual, layer.ln2, eps)
             else:
+                _push_projection(attention, layer.o, comm, peers, 2 * index)
+                normalized, residual = _reduce_add_norm(peers, 2 * index, residual, layer.ln2, eps)
+            activated = swiglu_linear(normalized, layer.gate_up)
+            if peers is None:
                 hidden = linear(activated, layer.down, split_ok=True)
-        normalized, _ = add_rms_norm(hidden, residual, w.final_norm, eps)
+            else:
+                _push_projection(activated, layer.down, comm, peers, 2 * index + 1)
+                following = layers[index + 1].ln1 if index + 1 < len(layers) else w.final_norm
+                normalized, residual = _reduce_add_norm(peers, 2 * index + 1, residual, following, eps)
+        if peers is None:
+            normalized, _ = add_rms_norm(hidden, residual, w.final_norm, eps)
         logits = linear(normalized, w.lm_head)
         self.logits = logits
         self.token_ids.copy_(argmax(logits[:, 0, :]).unsqueeze(-1))
@@ -227,7 +292,9 @@ class DecodeState:
                 attention = attention.transpose(1, 2).reshape(1, length, -1)
                 out = comm.all_reduce(F.linear(attention, layer.o))
                 normalized, residual = add_rms_norm(out, residual, layer.ln2, eps)
-                hidden = comm.all_reduce(F.linear(swiglu(F.linear(normalized, layer.gate_up)), layer.down))
+                gate, up = qwen3.split_gate_up(layer.gate_up)
+                hidden = comm.all_reduce(F.linear(swiglu(torch.cat((F.linear(normalized, gate),
+                                                                      F.linear(normalized, up)), -1)), layer.down))
             last[row] = hidden[0, -1:]
             last_residual[row] = residual[0, -1:]
         normalized, _ = add_rms_norm(last, last_residual, w.final_norm, eps)

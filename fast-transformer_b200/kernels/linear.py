@@ -2,9 +2,12 @@
 
 Drop-in for engine/kernels/linear.py:489-523 ``linear(x, weight, split_ok)``: all products
 accumulate in FP32 and round once to BF16. Decode-sized inputs (<= MAX_ROWS rows, aligned
-K/N) run the TMA + mma.sync kernel fb_linear; with ``split_ok`` a split-K result comes
-back as a ``Split`` for a consumer kernel to sum (merged.py). Larger row counts (prefill)
-stay on cuBLAS through ``F.linear``, exactly as the reference routes them (linear.py:492).
+K/N) run the TMA + mma.sync kernel fb_linear over (N/128 tiles) x (K splits); with
+``split_ok`` a split-K result comes back as a ``Split`` of FP32 partials for a consumer kernel
+to sum (merged.py), otherwise the splits of a tile (at most 8, one thread-block cluster) sum
+their partials through distributed shared memory and write BF16. Larger
+row counts (prefill) stay on cuBLAS through ``F.linear``, exactly as the reference routes them
+(linear.py:492).
 """
 
 import torch
@@ -16,16 +19,20 @@ from kernels.merged import Split
 
 #: Rows the skinny kernel takes (x is staged as 16/32/64-row slabs).
 MAX_ROWS = 64
+BF16_OUT, FP32_OUT, SWIGLU_OUT, SPLITS_OUT = 0, 1, 2, 3
+#: K-splits of one finished tile form a thread-block cluster (portable size limit).
+MAX_CLUSTER_SPLITS = 8
 _SPLITS = {}
 
 
-def splits_for(rows, n, k, device):
+def splits_for(rows, n, k, device, finished=False):
+    """fb_linear_splits' choice; capped at MAX_CLUSTER_SPLITS for finished-tile epilogues."""
     key = (device, rows, n, k)
     if key not in _SPLITS:
         if torch.cuda.is_current_stream_capturing():
             raise RuntimeError("projection selection must finish during eager warmup")
         _SPLITS[key] = int(lib.fb_linear_splits(rows, n, k))
-    return _SPLITS[key]
+    return min(_SPLITS[key], MAX_CLUSTER_SPLITS) if finished else _SPLITS[key]
 
 
 def supported(rows, weight):
@@ -33,25 +40,20 @@ def supported(rows, weight):
     return 0 < rows <= MAX_ROWS and k % 8 == 0 and n % 8 == 0 and weight.dtype == torch.bfloat16
 
 
-def project(flat, weight, splits, out_fp32=False):
-    """fb_linear on [M,K] x [N,K]: BF16 [M,N] (one split) or FP32 partials [S,M,N]."""
+def project(flat, weight, epilogue=BF16_OUT, splits=None):
+    """fb_linear on [M,K] x [N,K]: BF16 [M,N], FP32 [M,N], SwiGLU BF16 [M,N/2] or FP32 split
+    partials [S,M,N]."""
     m, k = flat.shape
     n = weight.shape[0]
-    if splits == 1 and not out_fp32:
-        out = torch.empty((m, n), device=flat.device, dtype=torch.bfloat16)
-    else:
+    if splits is None:
+        splits = splits_for(m, n, k, flat.device, finished=epilogue != SPLITS_OUT)
+    if epilogue == SWIGLU_OUT:
+        out = torch.empty((m, n // 2), device=flat.device, dtype=torch.bfloat16)
+    elif epilogue == SPLITS_OUT:
         out = torch.empty((splits, m, n), device=flat.device, dtype=torch.float32)
-    check(lib.fb_linear(ptr(flat), ptr(weight), ptr(out), m, n, k, splits, 1 if out_fp32 else 0, stream()),
-          "fb_linear")
-    return out
-
-
-def merge(partial, out_fp32=False):
-    """Sum FP32 partials [S,M,N] in split order into BF16 (or FP32) [M,N]."""
-    splits, m, n = partial.shape
-    out = torch.empty((m, n), device=partial.device, dtype=torch.float32 if out_fp32 else torch.bfloat16)
-    check(lib.fb_merge_splits(ptr(partial), splits, m * n, ptr(out), 1 if out_fp32 else 0, stream()),
-          "fb_merge_splits")
+    else:
+        out = torch.empty((m, n), device=flat.device, dtype=torch.float32 if epilogue == FP32_OUT else torch.bfloat16)
+    check(lib.fb_linear(ptr(flat), ptr(weight), ptr(out), m, n, k, epilogue, splits, stream()), "fb_linear")
     return out
 
 
@@ -62,10 +64,16 @@ def linear(x, weight, split_ok=False):
         return F.linear(x, weight)
     _native.require_cuda(x, weight)
     flat = x.reshape(rows, x.shape[-1]).contiguous()
-    splits = splits_for(rows, weight.shape[0], weight.shape[1], x.device)
-    result = project(flat, weight, splits)
-    if splits > 1 and split_ok:
-        return Split(result, (*x.shape[:-1], weight.shape[0]))
-    if splits > 1:
-        result = merge(result)
-    return result.reshape(*x.shape[:-1], weight.shape[0])
+    n, k = weight.shape
+    splits = splits_for(rows, n, k, x.device)
+    if split_ok and splits > 1:
+        return Split(project(flat, weight, SPLITS_OUT, splits), (*x.shape[:-1], n))
+    return project(flat, weight, BF16_OUT, min(splits, MAX_CLUSTER_SPLITS)).reshape(*x.shape[:-1], n)
+
+
+def swiglu_linear(x, gate_up_blocked):
+    """SwiGLU(x @ W^T) in one launch, W's rows being [gate; up] interleaved in 64-row blocks:
+    bf16(bf16(silu(gate)) * up) per feature, the reference's projection + swiglu arithmetic."""
+    rows = x.numel() // x.shape[-1]
+    flat = x.reshape(rows, x.shape[-1]).contiguous()
+    return project(flat, gate_up_blocked, SWIGLU_OUT).reshape(*x.shape[:-1], gate_up_blocked.shape[0] // 2)

@@ -2,6 +2,7 @@
 
     python fast-transformer_b200/profile_kernels.py attention --batch 16 --length 8320
     python fast-transformer_b200/profile_kernels.py linear --m 16 --n 24576 --k 4096
+    python fast-transformer_b200/profile_kernels.py verify --batch 8 --tokens 5 --length 4101
     python fast-transformer_b200/profile_kernels.py step --preset qwen3-8b --batch 16 --length 8192
 
 Each mode warms up, then runs the measured launches inside the NVTX range "profiled", so
@@ -85,6 +86,32 @@ def linear(args):
     torch.cuda.synchronize()
 
 
+def verify(args):
+    """B=8, T=5 (chain 5), 32/8 heads, D=128, 4096-slot prefix + 5 new slots."""
+    from kernels.decode_attention import block_attention
+    b, t, hq, hkv, d, cap = args.batch, args.tokens, args.q_heads, args.kv_heads, 128, args.length
+    sets = [(torch.randn(b, t, hq, d, device="cuda").bfloat16(), torch.randn(b, hkv, cap, d, device="cuda").bfloat16(),
+             torch.randn(b, hkv, cap, d, device="cuda").bfloat16()) for _ in range(args.copies)]
+    position = torch.full((b,), cap - t, dtype=torch.int64, device="cuda")
+    chain = torch.full((b,), t, dtype=torch.int64, device="cuda")
+
+    def run():
+        for q, k, v in sets:
+            block_attention(q, k, v, position, 1 / math.sqrt(d), chain)
+
+    ms = graph_time(run) / len(sets)
+    nbytes = 2 * b * hkv * cap * d * 2 + 2 * b * t * hq * d * 2
+    flops = 4 * b * hq * t * cap * d
+    print(f"verify B={b} T={t} Hq={hq} Hkv={hkv} L={cap}: {ms * 1e3:.2f} us, {nbytes / ms / 1e6:.0f} GB/s, "
+          f"{flops / ms / 1e9:.1f} TFLOP/s useful")
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("profiled")
+    for _ in range(args.launches):
+        block_attention(*sets[0], position, 1 / math.sqrt(d), chain)
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+
+
 def step(args):
     import decode as fdecode
     import qwen3
@@ -107,11 +134,12 @@ def step(args):
 
 def main():
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    parser.add_argument("mode", choices=("attention", "linear", "step"))
+    parser.add_argument("mode", choices=("attention", "linear", "verify", "step"))
     parser.add_argument("--batch", type=int, default=16)
     parser.add_argument("--q-heads", type=int, default=32)
     parser.add_argument("--kv-heads", type=int, default=8)
     parser.add_argument("--length", type=int, default=8320)
+    parser.add_argument("--tokens", type=int, default=5)
     parser.add_argument("--m", type=int, default=16)
     parser.add_argument("--n", type=int, default=24576)
     parser.add_argument("--k", type=int, default=4096)
@@ -119,7 +147,7 @@ def main():
     parser.add_argument("--copies", type=int, default=2)
     parser.add_argument("--launches", type=int, default=2)
     args = parser.parse_args()
-    {"attention": attention, "linear": linear, "step": step}[args.mode](args)
+    {"attention": attention, "linear": linear, "verify": verify, "step": step}[args.mode](args)
 
 
 if __name__ == "__main__":

@@ -3,7 +3,9 @@ tensor-parallel sharding by KV head.
 
 Packing follows the reference's module swaps (engine/layers.py:23-26 QKV rows [q; k; v],
 engine/layers.py:92-95 MLP rows [gate; up]), so one projection feeds the fused QK-norm/RoPE
-kernel and one feeds SwiGLU. Under tensor parallelism rank r of R owns KV heads
+kernel and one feeds SwiGLU; the gate/up rows are interleaved in 64-row blocks (gate block i,
+then up block i) so that every 128-row tile of the fused projection+SwiGLU kernel holds the
+gate and up rows of the same 64 features. Under tensor parallelism rank r of R owns KV heads
 [r*Hkv/R, (r+1)*Hkv/R) and their whole GQA query groups, the matching rows of q/k/v and
 gate/up, and the matching input columns of o_proj and down_proj; embeddings, norms and the
 (tied) LM head are replicated.
@@ -56,7 +58,7 @@ class Layer:
     q_norm: torch.Tensor    # [D]
     k_norm: torch.Tensor    # [D]
     o: torch.Tensor         # [H, q_local * D]
-    gate_up: torch.Tensor   # [2 I_local, H]
+    gate_up: torch.Tensor   # [2 I_local, H]: 64-row gate/up blocks interleaved
     down: torch.Tensor      # [H, I_local]
 
 
@@ -78,6 +80,24 @@ class Weights:
         per_layer = sum(t.numel() for t in (self.layers[0].qkv, self.layers[0].o, self.layers[0].gate_up,
                                               self.layers[0].down)) * 2
         return per_layer * len(self.layers) + self.lm_head.numel() * 2
+
+
+BLOCK = 64
+
+
+def interleave_gate_up(gate, up):
+    """[gate; up] rows -> 64-row blocks gate_0, up_0, gate_1, up_1, ... (I % 64 == 0)."""
+    rows, cols = gate.shape
+    if rows % BLOCK:
+        raise ValueError(f"MLP width {rows} per rank must be a multiple of {BLOCK}")
+    return torch.stack((gate.view(-1, BLOCK, cols), up.view(-1, BLOCK, cols)), dim=1).reshape(2 * rows, cols)
+
+
+def split_gate_up(blocked):
+    """Inverse of interleave_gate_up: (gate, up)."""
+    rows, cols = blocked.shape
+    view = blocked.view(-1, 2, BLOCK, cols)
+    return view[:, 0].reshape(rows // 2, cols), view[:, 1].reshape(rows // 2, cols)
 
 
 def _slices(cfg, tp_rank, tp_size):
@@ -102,7 +122,7 @@ def from_state_dict(cfg, state, device, tp_rank=0, tp_size=1):
         p = f"model.layers.{i}."
         qkv = torch.cat((get(p + "self_attn.q_proj.weight")[q], get(p + "self_attn.k_proj.weight")[kv],
                          get(p + "self_attn.v_proj.weight")[kv]), dim=0).contiguous()
-        gate_up = torch.cat((get(p + "mlp.gate_proj.weight")[mlp], get(p + "mlp.up_proj.weight")[mlp]), dim=0).contiguous()
+        gate_up = interleave_gate_up(get(p + "mlp.gate_proj.weight")[mlp], get(p + "mlp.up_proj.weight")[mlp]).contiguous()
         layers.append(Layer(
             ln1=get(p + "input_layernorm.weight"), ln2=get(p + "post_attention_layernorm.weight"), qkv=qkv,
             q_norm=get(p + "self_attn.q_norm.weight"), k_norm=get(p + "self_attn.k_norm.weight"),
@@ -138,7 +158,7 @@ def random_init(cfg, device, seed=0, tp_rank=0, tp_size=1, std=0.02):
         qkv = torch.cat((linear(p + "q", hq * d, h)[q], linear(p + "k", hkv * d, h)[kv],
                          linear(p + "v", hkv * d, h)[kv]), dim=0).contiguous()
         o = linear(p + "o", h, hq * d)[:, q].contiguous()
-        gate_up = torch.cat((linear(p + "gate", i, h)[mlp], linear(p + "up", i, h)[mlp]), dim=0).contiguous()
+        gate_up = interleave_gate_up(linear(p + "gate", i, h)[mlp], linear(p + "up", i, h)[mlp]).contiguous()
         down = linear(p + "down", h, i)[:, mlp].contiguous()
         layers.append(Layer(ln1=ones_h, ln2=ones_h, qkv=qkv, q_norm=ones_d, k_norm=ones_d, o=o,
                             gate_up=gate_up, down=down))
@@ -158,7 +178,7 @@ def to_state_dict(weights, device="cpu"):
     for i, layer in enumerate(weights.layers):
         p = f"model.layers.{i}."
         q, k, v = layer.qkv.to(device).split((hq * d, hkv * d, hkv * d), dim=0)
-        gate, up = layer.gate_up.to(device).split((inter, inter), dim=0)
+        gate, up = split_gate_up(layer.gate_up.to(device))
         out.update({
             p + "input_layernorm.weight": layer.ln1.to(device), p + "post_attention_layernorm.weight": layer.ln2.to(device),
             p + "self_attn.q_proj.weight": q, p + "self_attn.k_proj.weight": k, p + "self_attn.v_proj.weight": v,

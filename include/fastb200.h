@@ -179,20 +179,51 @@ int fb_embed_rmsnorm(const int64_t* ids, const void* table, int64_t vocab, const
 int fb_swiglu(const void* packed, int splits, void* out, int rows, int width, void* stream);
 
 /* ------------------------------------------------------------------------------------
- * Skinny bf16 projection y = x @ W^T with fp32 accumulation.
+ * Skinny bf16 projection y = x @ W^T with fp32 accumulation and one rounding.
  * Replaces engine/kernels/linear.py:489-523 `linear` for rows <= 64 (the reference's
- * Triton kinds, linear.py:27-93 and gemm.py:51-425); larger row counts stay on cuBLAS
- * exactly as the reference does (linear.py:492-493).
- *   x   bf16 [M, K], W bf16 [N, K] (both contiguous, K % 64 == 0, N % 8 == 0), M <= 64
- *   out: splits == 1 and out_fp32 == 0 -> bf16 [M, N] (one rounding)
- *        otherwise fp32 partials [splits, M, N] (split s covers K range
- *        [s*K/splits, (s+1)*K/splits) in 64-wide chunks; consumers sum then round,
- *        engine/kernels/merged.py:13-45)
- * fb_linear_splits() is the default split count for a shape on the current device.
+ * Triton kinds, linear.py:27-93 and gemm.py:51-425; larger row counts stay on cuBLAS
+ * exactly as the reference routes them, linear.py:492-493).
+ *   x   bf16 [M, K], W bf16 [N, K] (contiguous; K % 8 == 0, N % 8 == 0), M <= 64
+ *   epilogue 0: out bf16 [M, N]
+ *            1: out fp32 [M, N]
+ *            2: SwiGLU: W's rows are [gate; up] interleaved in 64-row blocks (block 2i =
+ *               gate rows 64i..64i+63, block 2i+1 = the matching up rows); out bf16 [M, N/2]
+ *               = bf16(bf16(silu(bf16(gate))) * bf16(up)) (engine/kernels/swiglu.py:13-24);
+ *               N % 128 == 0
+ *            3: out fp32 split-K partials [splits, M, N] (split s covers K range
+ *               [s*K/splits, (s+1)*K/splits) in 64-wide chunks); consumers sum them in split
+ *               order, then round (engine/kernels/merged.py:13-45). No workspace needed.
+ * Grid = ceil(N/128) tiles x `splits` K-splits (fb_linear_splits() picks a default; for
+ * epilogues 0-2 use min(that, 8)). For epilogues 0-2 with splits > 1 (at most 8) the splits
+ * of a tile run as one thread-block cluster and sum their partials in split order through
+ * distributed shared memory (deterministic). No workspace. Launched with programmatic
+ * stream serialization (weights are prefetched before the previous kernel completes).
  * ---------------------------------------------------------------------------------- */
 int fb_linear_splits(int m, int n, int k);
-int fb_linear(const void* x, const void* w, void* out, int m, int n, int k, int splits,
-              int out_fp32, void* stream);
+int fb_linear(const void* x, const void* w, void* out, int m, int n, int k, int epilogue, int splits,
+              void* stream);
+
+/* ------------------------------------------------------------------------------------
+ * Tensor-parallel projection + all-reduce over NVLink peer memory (no counterpart in the
+ * reference, which is single-GPU; this replaces an NCCL all-reduce after o_proj/down_proj).
+ * Producer: fb_linear_allreduce_push computes this rank's fp32 partial of y = x @ W^T and
+ *   stores every finished 128-column tile into slab `rank` of recv[use] on every rank
+ *   (peer_recv[r] = rank r's recv base, fp32 [uses, world, M, N]), then adds 1 to
+ *   arrivals[use] on every rank (peer_counter[r] = rank r's arrivals, uint32 [uses]) with a
+ *   system-scope release.
+ * Consumer: fb_allreduce_add_rmsnorm waits (bounded, 2 s) until this rank's arrivals[use]
+ *   reaches `expected` (= world * ceil(N / 128)), sums the world slabs in rank order (the same
+ *   bits on every rank), rounds to bf16 and applies add_rms_norm (fb_add_rmsnorm's
+ *   arithmetic) with `residual`/`w`; the last CTA resets arrivals[use] and done[use]
+ *   (uint32 [uses], local) for the next use. One call per use per step, in the same order
+ *   on every rank.
+ * ---------------------------------------------------------------------------------- */
+int fb_linear_allreduce_push(const void* x, const void* w, int m, int n, int k, int splits, int world,
+                             int rank, int use,
+                             void* const* peer_recv, void* const* peer_counter, void* stream);
+int fb_allreduce_add_rmsnorm(const void* recv, void* arrivals, void* done, int use, int world,
+                             int expected, const void* residual, const void* w, void* out,
+                             void* sum, int rows, int width, float eps, void* stream);
 
 /* Sums fp32 split partials [splits, count] into bf16 [count] (or fp32 when out_fp32):
  * the reference's `_merge_projection` (linear.py:81-93). */

@@ -46,8 +46,11 @@ def test_host_validation_without_gpu():
     assert lib.fb_argmax(null, 1, 100, null, null, null, 0, null) == -1
     p = ctypes.c_void_p(16)  # never dereferenced: shape checks fail first
     # unsupported shapes -> FB_ERR_SHAPE
-    assert lib.fb_linear(p, p, p, 65, 128, 128, 1, 0, null) == -2        # > 64 rows
-    assert lib.fb_linear(p, p, p, 4, 128, 100, 1, 0, null) == -2         # K not a multiple of 8
+    assert lib.fb_linear(p, p, p, 65, 128, 128, 0, 1, null) == -2     # > 64 rows
+    assert lib.fb_linear(p, p, p, 4, 128, 100, 0, 1, null) == -2      # K not a multiple of 8
+    assert lib.fb_linear(p, p, p, 4, 128, 128, 7, 1, null) == -1      # unknown epilogue
+    assert lib.fb_linear(p, p, p, 4, 128, 128, 0, 3, null) == -2      # more splits than K chunks
+    assert lib.fb_linear(p, p, p, 4, 128, 4096, 0, 9, null) == -2     # finished tile: cluster of <= 8 splits
     assert lib.fb_swiglu(p, 1, p, 4, 12, null) == -2                     # width % 8
     assert lib.fb_add_rmsnorm(p, 1, p, p, p, p, 4, 20000, 1e-6, null) == -2  # row too wide
     assert lib.fb_decode_attention(p, p, p, p, 0, p, p, 1 << 20, 1, 16, 8, 96, 2048, 0.1, 148, null) == -2  # D=96

@@ -203,18 +203,37 @@ def test_swiglu_matches_reference():
 
 
 def test_linear_matches_reference():
-    from kernels.linear import linear, merge, project
+    """Every epilogue against the reference's projection contract (F.linear, verify_gpu.py:175-185)
+    for several split counts: bf16 and fp32 finished tiles (cluster sum of the splits), fp32
+    split partials; deterministic; finished tiles equal the split-order sum of the partials."""
+    from kernels import linear as klin
+    from kernels._native import lib, ptr, stream, check
     fx = load("pointwise")
     for case in cases.LINEAR_CASES:
         x, weight = cases.linear_inputs(case)
-        got = linear(x.to(DEV), weight.to(DEV)).cpu()
+        xd, wd = x.to(DEV), weight.to(DEV)
+        got = klin.linear(xd, wd).cpu()
         torch.testing.assert_close(got.float(), fx[case[0]]["out"].float(), atol=1e-3, rtol=0.016)
-        # every split count gives the same sums up to fp32 reassociation
-        if x.shape[0] <= 64:
-            chunks = (x.shape[1] + 63) // 64
-            for splits in sorted({1, 2, min(5, chunks), chunks}):
-                part = project(x.to(DEV), weight.to(DEV), splits, out_fp32=True)
-                torch.testing.assert_close(merge(part).cpu().float(), fx[case[0]]["out"].float(), atol=1e-3, rtol=0.016)
+        assert torch.equal(got, klin.linear(xd, wd).cpu())
+        m, k = x.shape
+        n = weight.shape[0]
+        exact = x.float() @ weight.float().T
+        chunks = (k + 63) // 64
+        for splits in sorted({1, 2, min(chunks, 7), min(chunks, 8), int(lib.fb_linear_splits(m, n, k)), chunks}):
+            part = torch.empty(splits, m, n, dtype=torch.float32, device=DEV)
+            check(lib.fb_linear(ptr(xd), ptr(wd), ptr(part), m, n, k, 3, splits, stream()), "fb_linear")
+            torch.cuda.synchronize()
+            torch.testing.assert_close(part.sum(0).cpu(), exact, atol=1e-4, rtol=1e-4)
+            if splits > klin.MAX_CLUSTER_SPLITS:
+                continue
+            out = torch.empty(m, n, dtype=torch.float32, device=DEV)
+            check(lib.fb_linear(ptr(xd), ptr(wd), ptr(out), m, n, k, 1, splits, stream()), "fb_linear")
+            torch.cuda.synchronize()
+            torch.testing.assert_close(out.cpu(), exact, atol=1e-4, rtol=1e-4)
+            ordered = part[0].clone()
+            for s in range(1, splits):
+                ordered += part[s]
+            assert torch.equal(out, ordered)  # rank-order cluster sum = split-order sum
 
 
 def test_linear_split_result_feeds_consumers():
@@ -224,11 +243,25 @@ def test_linear_split_result_feeds_consumers():
     w = (torch.randn(1024, 4096, device=DEV) * 0.02).bfloat16()
     res = linear(x, w, split_ok=True)
     expect = torch.nn.functional.linear(x.float(), w.float())
-    if isinstance(res, Split):
-        total = res.partial.sum(0).view(16, 1, 1024)
-    else:
-        total = res.float()
+    total = res.partial.sum(0).view(16, 1, 1024) if isinstance(res, Split) else res.float()
     torch.testing.assert_close(total, expect, atol=1e-3, rtol=0.016)
+
+
+def test_swiglu_linear_matches_oracle():
+    """Fused projection + SwiGLU (64-row gate/up blocks) equals projecting gate and up separately
+    and applying the reference's SwiGLU (swiglu.py:13-24)."""
+    import qwen3
+    from kernels.linear import swiglu_linear
+    g = torch.Generator().manual_seed(11)
+    for rows, width, hidden in ((1, 3072, 1024), (16, 1536, 4096), (5, 256, 256), (33, 512, 1024)):
+        x = torch.randn(rows, hidden, generator=g).bfloat16()
+        gate = (torch.randn(width, hidden, generator=g) * 0.05).bfloat16()
+        up = (torch.randn(width, hidden, generator=g) * 0.05).bfloat16()
+        blocked = qwen3.interleave_gate_up(gate, up).contiguous()
+        got = swiglu_linear(x.to(DEV), blocked.to(DEV)).cpu()
+        expect = opw.swiglu(torch.cat((opw.linear(x, gate), opw.linear(x, up)), -1))
+        assert (got == expect).float().mean() >= 0.99
+        torch.testing.assert_close(got.float(), expect.float(), atol=0.015625, rtol=0.016)
 
 
 def test_argmax_matches_reference():

@@ -52,7 +52,8 @@ def sharded_decode_step(w, token_ids, keys, values, position):
         out = attn.reshape(batch, 1, -1).to(F32) @ layer.o.to(F32).T  # partial sum over this rank's heads
         dist.all_reduce(out)
         normalized, residual = opw.add_rms_norm(out.to(BF16), residual, layer.ln2, eps)
-        act = opw.swiglu(opw.linear(normalized, layer.gate_up))
+        gate, up = qwen3.split_gate_up(layer.gate_up)
+        act = opw.swiglu(torch.cat((opw.linear(normalized, gate), opw.linear(normalized, up)), -1))
         down = act.to(F32) @ layer.down.to(F32).T
         dist.all_reduce(down)
         hidden = down.to(BF16)
@@ -87,7 +88,9 @@ def _worker(rank, world, port, queue, source):
         if rank == 0:
             model = omodel.Model(omodel.Config(**cfg.__dict__), qwen3.to_state_dict(full))
             expect = model.decode(tokens, position, (keys.clone(), values.clone()))
-            queue.put((logits, expect, gathered))
+            # numpy: pickled by value (a torch tensor would travel as a file descriptor that
+            # dies with this process)
+            queue.put((logits.float().numpy(), expect.float().numpy(), [t.float().numpy() for t in gathered]))
     finally:
         dist.destroy_process_group()
 
@@ -101,6 +104,8 @@ def test_tp2_decode_step_matches_unsharded_oracle(source):
     for p in procs:
         p.start()
     logits, expect, gathered = queue.get(timeout=300)
+    logits, expect = torch.from_numpy(logits), torch.from_numpy(expect)
+    gathered = [torch.from_numpy(t) for t in gathered]
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0

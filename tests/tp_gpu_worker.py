@@ -31,7 +31,7 @@ def main():
             prompt, steps = cases.model_prompt(case)
             batch, length = prompt.shape
             weights = qwen3.from_state_dict(cfg, state_dict, device, rank, world)
-            comm = fdecode.Communicator(dist.group.WORLD, world)
+            comm = fdecode.Communicator(dist.group.WORLD, world, rank)
             eager = fdecode.DecodeState(weights, batch, length, steps + 4, comm=comm, device=device)
             tokens, logits = fdecode.greedy(eager, prompt.to(device), steps)
             graph_state = fdecode.DecodeState(weights, batch, length, steps + 4, comm=comm, device=device)
@@ -55,6 +55,7 @@ def main():
                 "ranks agree": all(torch.equal(t, gathered[0]) for t in gathered),
                 "logits": bool(err <= 2e-2 * scale),
             }
+            checks["no multicast"] = not graph_state.peers.multicast
             if rank == 0:
                 print(case[0], checks, flush=True)
             ok = ok and all(checks.values())
