@@ -25,6 +25,8 @@ __global__ void __launch_bounds__(kThreads)
                         int* best_index) {
   __shared__ float sv[kThreads / 32];
   __shared__ int si[kThreads / 32];
+  pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.y;
   const int blk = blockIdx.x;
   const int64_t c0 = static_cast<int64_t>(blk) * kBlock;
@@ -73,6 +75,8 @@ __global__ void __launch_bounds__(kThreads)
 __global__ void __launch_bounds__(32)
     first_best_kernel(const float* best_value, const int* best_index, int blocks, int64_t* out,
                       float* top) {
+  pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.x;
   float v = -INFINITY;
   int idx = 0x7fffffff;
@@ -116,10 +120,8 @@ extern "C" int fb_argmax(const void* logits, int rows, int64_t vocab, int64_t* o
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool aligned_ptr = (reinterpret_cast<uintptr_t>(logits) & 15u) == 0;
   if (!aligned_ptr) return FB_ERR_ARG;
-  amax::block_argmax_kernel<<<dim3(blocks, rows), amax::kThreads, 0, s>>>(
-      static_cast<const __nv_bfloat16*>(logits), vocab, blocks, bv, bi);
-  int st = check_launch();
+  int st = launch_ex(amax::block_argmax_kernel, dim3(blocks, rows), dim3(amax::kThreads), 0, s, 1,
+                     static_cast<const __nv_bfloat16*>(logits), vocab, blocks, bv, bi);
   if (st != FB_OK) return st;
-  amax::first_best_kernel<<<rows, 32, 0, s>>>(bv, bi, blocks, out, top);
-  return check_launch();
+  return launch_ex(amax::first_best_kernel, dim3(rows), dim3(32), 0, s, 1, bv, bi, blocks, out, top);
 }

@@ -187,6 +187,46 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// ---------------------------------------------------------------------------------
+// Programmatic dependent launch. Every kernel of the decode step is launched with
+// programmatic stream serialization (launch_ex): it may start while its predecessor is
+// still running, reads only never-written inputs (weights, tables) before pdl_wait(), and
+// reads or writes nothing a predecessor touches until pdl_wait() has returned (the whole
+// predecessor grid has then completed and its writes are visible). pdl_trigger() lets
+// the successor start; it fires once every CTA has triggered or exited.
+// ---------------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------------
+// Thread-block clusters and distributed shared memory.
+// ---------------------------------------------------------------------------------
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address of the same shared-memory offset in the cluster CTA of rank `rank`.
+__device__ __forceinline__ uint32_t map_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
 }  // namespace fb
 
 // ---------------------------------------------------------------------------------
@@ -201,4 +241,30 @@ int sm_count();
 int check_launch();
 // Device address of the error word on the current device (kernels take it as a parameter).
 unsigned* error_word();
+
+// Launches `kernel` with programmatic stream serialization and, when cluster_x > 1, a
+// (cluster_x, 1, 1) thread-block cluster. Returns FB_OK or FB_ERR_LAUNCH.
+template <typename... Params, typename... Args>
+inline int launch_ex(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                     unsigned cluster_x, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.numAttrs = 1;
+  if (cluster_x > 1) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = cluster_x;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
+  }
+  cfg.attrs = attr;
+  if (cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...) != cudaSuccess) return FB_ERR_LAUNCH;
+  return check_launch();
+}
 }  // namespace fb

@@ -202,6 +202,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
 
   if (p.counters != nullptr && blockIdx.x == 0) {
+    pdl_wait();  // `out` may still be read by an earlier kernel
     // Rows with no valid slot get no run; the fused form writes their (empty) output.
     for (int b = 0; b < B; ++b)
       if (cum[b + 1] == cum[b])
@@ -245,8 +246,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int b = misc[0], h = misc[1], j = misc[2];
       int n = cum[b + 1] - cum[b];
+      // Cache rows below a row's position were written by earlier steps, so the ring is
+      // filled before the dependency wait; the tile holding the row's newest slot (the
+      // previous kernel appends it) waits for the previous kernel.
+      bool waited = false;
       for (int k = 0; k < count; ++k) {
         const int s = k % NS;
+        if (!waited && (k >= NS || j == n - 1)) {
+          pdl_wait();
+          waited = true;
+        }
         if (*abort_flag) break;
         if (k >= NS) {
           if (!mbar_wait_bounded(&empty[s], ((k / NS) - 1) & 1)) {
@@ -280,6 +289,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   // ========================== consumers: warps 0..3 ==========================
+  pdl_wait();  // the query rows come from the previous kernel
+  pdl_trigger();
   const int g = lane >> 2;  // fragment row group
   const int c = lane & 3;   // fragment column pair
   const int ctid = threadIdx.x;  // 0..127
@@ -518,6 +529,8 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const P
   __shared__ int s_before, s_total, s_n;
   __shared__ float s_w[kMaxCtas * kHeadsPad];
   __shared__ float s_den[kHeadsPad];
+  pdl_wait();
+  pdl_trigger();
   const int pair = blockIdx.x;
   const int b = pair / p.kv_heads, h = pair % p.kv_heads;
   const int G = p.groups;
@@ -566,8 +579,8 @@ int launch_partials(const CUtensorMap& km, const CUtensorMap& vm, const Params& 
       return FB_ERR_LAUNCH;
     configured[dev] = true;
   }
-  decode_partials_kernel<D, kStages><<<p.ctas, kThreads, S::kTotal, stream>>>(km, vm, p);
-  return check_launch();
+  return launch_ex(decode_partials_kernel<D, kStages>, dim3(p.ctas), dim3(kThreads), S::kTotal, stream, 1, km, vm,
+                   p);
 }
 
 int validate(int batch, int q_heads, int kv_heads, int head_dim, int capacity) {
@@ -683,11 +696,8 @@ extern "C" int fb_decode_attention_combine(const int64_t* position, int per_row,
   if (st != FB_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int pairs = batch * kv_heads;
-  if (head_dim == 128)
-    decode_combine_kernel<128><<<pairs, kCombineThreads, 0, s>>>(p);
-  else
-    decode_combine_kernel<64><<<pairs, kCombineThreads, 0, s>>>(p);
-  return check_launch();
+  if (head_dim == 128) return launch_ex(decode_combine_kernel<128>, dim3(pairs), dim3(kCombineThreads), 0, s, 1, p);
+  return launch_ex(decode_combine_kernel<64>, dim3(pairs), dim3(kCombineThreads), 0, s, 1, p);
 }
 
 // ---------------------------------------------------------------------------------------

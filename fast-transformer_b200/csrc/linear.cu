@@ -58,34 +58,6 @@ struct Smem {
   static constexpr int kTotal = 1024 + kStages * kStageBytes + 2 * kStages * 8 + 64;
 };
 
-__device__ __forceinline__ void grid_dependency_wait() {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-}
-__device__ __forceinline__ void grid_launch_dependents() {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-// Address of the same shared-memory offset in the cluster CTA of rank `rank`.
-__device__ __forceinline__ uint32_t map_shared(uint32_t addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
-  return r;
-}
-__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr)
-               : "memory");
-  return v;
-}
-
 __device__ __forceinline__ float silu_bf16(float g) {
   // engine/kernels/swiglu.py:21: SiLU computed in fp32 and rounded to bf16
   return bf16_round(g / (1.0f + expf(-g)));
@@ -182,7 +154,7 @@ __global__ void __launch_bounds__(kThreads)
     flags[0] = 0;
   }
   __syncthreads();
-  grid_launch_dependents();
+  pdl_trigger();
 
   if (warp == kConsumerWarps) {
     if (lane == 0) {
@@ -193,7 +165,7 @@ __global__ void __launch_bounds__(kThreads)
         mbar_arrive_expect_tx(&full[i], S::kStageBytes);
         tma_load_2d_hint(base + i * S::kStageBytes, &wmap, &full[i], (c0 + i) * kTileK, n0, evict_first);
       }
-      grid_dependency_wait();
+      pdl_wait();
       for (int i = 0; i < pre; ++i)
         tma_load_2d(base + i * S::kStageBytes + S::kWBytes, &xmap, &full[i], (c0 + i) * kTileK, 0);
       for (int i = pre; i < count; ++i) {
@@ -219,7 +191,7 @@ __global__ void __launch_bounds__(kThreads)
     return;
   }
 
-  grid_dependency_wait();  // outputs may be read by the previous kernel
+  pdl_wait();  // outputs may be read by the previous kernel
   const int g = lane >> 2, c4 = lane & 3;
   const int tid = threadIdx.x;
   const int q = lane >> 3;

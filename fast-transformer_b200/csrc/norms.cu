@@ -1,5 +1,5 @@
-// RMSNorm family, SwiGLU and the split-K merge (sm_100a). All HBM/latency bound; one
-// CTA per row with 16-byte vector accesses. Cast points follow the reference:
+// RMSNorm family, SwiGLU and the split-K merge (sm_100a). All HBM/latency bound, 16-byte
+// vector accesses; an RMSNorm row is spread over a thread-block cluster at decode sizes. Cast points follow the reference:
 //   rms_norm       engine/kernels/rmsnorm.py:21-46   y = bf16(bf16(x*inv) * w)
 //   add_rms_norm   engine/kernels/rmsnorm.py:75-95   s = bf16(x+r); y = bf16(bf16(s*inv) * w)
 //   embed_rms_norm engine/kernels/rmsnorm.py:128-142 h = table[id]; y = rms_norm(h)
@@ -12,11 +12,16 @@
 namespace fb {
 namespace norm {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 256;     // elementwise kernels (swiglu, merge)
+constexpr int kMaxThreads = 256;  // RMSNorm CTAs
+constexpr int kMaxPer = 4;        // 8-wide chunks per RMSNorm thread
+constexpr int kMaxCluster = 8;    // CTAs sharing one RMSNorm row
+constexpr int kSlabBatch = 8;     // split slabs whose loads are in flight together
 
 // 8 consecutive logical bf16 values starting at element `off` of a tensor that is either
-// bf16 (splits == 0) or fp32 split partials [splits, count] (splits >= 1).
-__device__ __forceinline__ void load8(const void* src, int splits, size_t count, size_t off,
+// bf16 (splits == 0) or fp32 split partials [splits, slab] (splits >= 1). Up to eight slabs
+// are loaded before they are added (in split order), so S <= 8 costs one memory round trip.
+__device__ __forceinline__ void load8(const void* src, int splits, size_t slab, size_t off,
                                       float (&x)[8]) {
   if (splits == 0) {
     const uint4 w = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(src) + off);
@@ -31,30 +36,27 @@ __device__ __forceinline__ void load8(const void* src, int splits, size_t count,
     return;
   }
   const float* f = static_cast<const float*>(src) + off;
-  const float4 a = *reinterpret_cast<const float4*>(f);
-  const float4 b = *reinterpret_cast<const float4*>(f + 4);
-  x[0] = a.x;
-  x[1] = a.y;
-  x[2] = a.z;
-  x[3] = a.w;
-  x[4] = b.x;
-  x[5] = b.y;
-  x[6] = b.z;
-  x[7] = b.w;
-  // Issue the loads of up to four slabs before adding them (in split order), so a
-  // multi-split input costs ceil((S-1)/4) memory round trips rather than S-1.
-  for (int s0 = 1; s0 < splits; s0 += 4) {
-    float4 c[4], d[4];
+  for (int s0 = 0; s0 < splits; s0 += kSlabBatch) {
+    float4 c[kSlabBatch], d[kSlabBatch];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < kSlabBatch; ++j) {
       if (s0 + j < splits) {
-        c[j] = __ldg(reinterpret_cast<const float4*>(f + (s0 + j) * count));
-        d[j] = __ldg(reinterpret_cast<const float4*>(f + (s0 + j) * count + 4));
+        c[j] = __ldcg(reinterpret_cast<const float4*>(f + (s0 + j) * slab));
+        d[j] = __ldcg(reinterpret_cast<const float4*>(f + (s0 + j) * slab + 4));
       }
     }
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      if (s0 + j < splits) {
+    for (int j = 0; j < kSlabBatch; ++j) {
+      if (s0 + j == 0) {
+        x[0] = c[0].x;
+        x[1] = c[0].y;
+        x[2] = c[0].z;
+        x[3] = c[0].w;
+        x[4] = d[0].x;
+        x[5] = d[0].y;
+        x[6] = d[0].z;
+        x[7] = d[0].w;
+      } else if (s0 + j < splits) {
         x[0] += c[j].x;
         x[1] += c[j].y;
         x[2] += c[j].z;
@@ -80,7 +82,7 @@ __device__ __forceinline__ void store8(__nv_bfloat16* dst, const float (&y)[8]) 
 }
 
 __device__ __forceinline__ void load_w8(const __nv_bfloat16* w, int col, float (&x)[8]) {
-  const uint4 v = *reinterpret_cast<const uint4*>(w + col);
+  const uint4 v = __ldg(reinterpret_cast<const uint4*>(w + col));
   x[0] = bf16_lo(v.x);
   x[1] = bf16_hi(v.x);
   x[2] = bf16_lo(v.y);
@@ -103,50 +105,102 @@ __device__ __forceinline__ float block_sum(float v, float* scratch) {
   return t;
 }
 
-// Per-thread register cache: up to kMaxChunks 8-wide chunks per thread (W <= 16384).
-constexpr int kMaxChunks = 8;
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 
-// mode 0: rms_norm(x)  mode 1: add_rms_norm(x, residual)  mode 2: embed + rms_norm
+// mode 0: rms_norm(x)          mode 1: add_rms_norm(x, residual)
+// mode 2: embed + rms_norm     mode 3: tensor-parallel all-reduce + add_rms_norm
+//
+// Mode 3: every rank's projection pushed its fp32 [rows, W] partial into slab `rank` of
+// this rank's receive buffer and added one arrival per 128-column tile to `arrivals`; once
+// all `expected` arrivals are in, the slabs are summed in rank order (identical bits on
+// every rank), rounded to bf16 (the projection's output) and fed to add_rms_norm's
+// arithmetic. The last CTA to finish resets the arrival and completion counters.
 struct Params {
-  const void* x;
-  int splits;
-  int64_t row_stride;
+  const void* x;          // mode 3: this use's receive slabs [world, rows, W]
+  int splits;             // fp32 slabs in x (0: x is bf16); mode 3: world
+  int64_t row_stride;     // mode 0
   const __nv_bfloat16* residual;
   const __nv_bfloat16* w;
   __nv_bfloat16* y;
   __nv_bfloat16* sum;
-  const int64_t* ids;
+  const int64_t* ids;     // mode 2
   int64_t vocab;
+  unsigned* arrivals;     // mode 3: this use's counters
+  unsigned* done;
+  unsigned expected;
   int rows, width;
   float eps;
   unsigned* err;
 };
 
+// Grid: rows * C CTAs, clusters of C (C = gridDim.x / rows) along x; CTA `rank` of a row's
+// cluster owns chunks [rank * per, (rank + 1) * per) of the row (8 values per chunk), each
+// thread up to kMaxPer of them. The row's sum of squares is reduced per CTA, then across
+// the cluster through distributed shared memory in rank order (the same order, hence the
+// same bits, in every CTA).
 template <int MODE>
-__global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const Params p) {
-  __shared__ float scratch[kThreads / 32];
-  const int row = blockIdx.x;
+__global__ void __launch_bounds__(kMaxThreads) rmsnorm_kernel(const Params p) {
+  __shared__ float scratch[kMaxThreads / 32];
+  __shared__ float cta_ss;
+  __shared__ int ok;
+  const int C = gridDim.x / p.rows;
+  const int row = blockIdx.x / C;
+  const int rank = blockIdx.x % C;
   const int chunks = p.width / 8;
-  float v[kMaxChunks][8];
+  const int per = (chunks + C - 1) / C;
+  const int c0 = rank * per;
+  const int c1 = min(chunks, c0 + per);
+  const int T = blockDim.x;
+  // the gains are never written while decoding: load them before the dependency wait
+  float wv[kMaxPer][8];
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    const int ch = c0 + threadIdx.x + i * T;
+    if (ch < c1) load_w8(p.w, ch * 8, wv[i]);
+  }
+  pdl_wait();
+  pdl_trigger();
+
   const void* src = p.x;
   size_t base = static_cast<size_t>(row) * p.width;
   if (MODE == 0) base = static_cast<size_t>(row) * p.row_stride;
   if (MODE == 2) {
     const long long id = p.ids[row];
-    if (id < 0 || id >= p.vocab) {
-      if (threadIdx.x == 0) raise_error(p.err, kErrBadShape);
+    if (id < 0 || id >= p.vocab) {  // the whole cluster (one row) leaves before any barrier
+      if (threadIdx.x == 0 && rank == 0) raise_error(p.err, kErrBadShape);
       return;
     }
     base = static_cast<size_t>(id) * p.width;
   }
-  const size_t count = static_cast<size_t>(p.rows) * p.width;
+  if (MODE == 3) {
+    if (threadIdx.x == 0) {
+      const unsigned long long start = globaltimer();
+      // after one wait has given up, fail fast instead of spending the budget again
+      int good = p.err == nullptr || (*reinterpret_cast<volatile unsigned*>(p.err) & kErrTimeoutFull) == 0;
+      while (good && ld_acquire_sys(p.arrivals) < p.expected) {
+        if (globaltimer() - start > kWaitBudgetNs) {
+          raise_error(p.err, kErrTimeoutFull);
+          good = 0;
+        }
+      }
+      ok = good;
+    }
+    __syncthreads();
+  }
+  const int split_count = (MODE == 1 || MODE == 3) ? p.splits : 0;
+  const size_t slab = static_cast<size_t>(p.rows) * p.width;
+  float v[kMaxPer][8];
   float ss = 0.f;
 #pragma unroll
-  for (int i = 0; i < kMaxChunks; ++i) {
-    const int ch = threadIdx.x + i * kThreads;
-    if (ch < chunks) {
-      load8(src, MODE == 1 ? p.splits : 0, count, base + ch * 8, v[i]);
-      if (MODE == 1) {
+  for (int i = 0; i < kMaxPer; ++i) {
+    const int ch = c0 + threadIdx.x + i * T;
+    if (ch < c1 && (MODE != 3 || ok)) {
+      load8(src, split_count, slab, base + ch * 8, v[i]);
+      if (MODE == 1 || MODE == 3) {
         float r[8];
         load8(p.residual, 0, 0, static_cast<size_t>(row) * p.width + ch * 8, r);
 #pragma unroll
@@ -159,25 +213,46 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const Params p) {
     }
   }
   ss = block_sum(ss, scratch);
+  if (C > 1) {
+    if (threadIdx.x == 0) cta_ss = ss;
+    cluster_sync();  // every CTA's sum is in its shared memory
+    const uint32_t local = smem_u32(&cta_ss);
+    float total = 0.f;
+    for (int q = 0; q < C; ++q) total += ld_cluster_f32(map_shared(local, q));
+    ss = total;
+  }
   const float inv = 1.0f / sqrtf(ss / static_cast<float>(p.width) + p.eps);
 #pragma unroll
-  for (int i = 0; i < kMaxChunks; ++i) {
-    const int ch = threadIdx.x + i * kThreads;
-    if (ch < chunks) {
-      float w[8], y[8];
-      load_w8(p.w, ch * 8, w);
+  for (int i = 0; i < kMaxPer; ++i) {
+    const int ch = c0 + threadIdx.x + i * T;
+    if (ch < c1 && (MODE != 3 || ok)) {
+      float y[8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) y[e] = bf16_round(v[i][e] * inv) * w[e];
+      for (int e = 0; e < 8; ++e) y[e] = bf16_round(v[i][e] * inv) * wv[i][e];
       const size_t out = (MODE == 0 ? static_cast<size_t>(row) * p.row_stride
                                     : static_cast<size_t>(row) * p.width) +
                          ch * 8;
       store8(p.y + out, y);
     }
   }
+  if (C > 1) cluster_sync();  // no CTA leaves while another may still read its sum
+  if (MODE == 3) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      if (atomicAdd(p.done, 1u) == gridDim.x - 1) {
+        // every CTA has read this use's slabs: ready for the next step
+        *p.done = 0;
+        atomicExch(p.arrivals, 0u);
+      }
+    }
+  }
 }
 
 __global__ void __launch_bounds__(kThreads)
     swiglu_kernel(const void* packed, int splits, __nv_bfloat16* out, int rows, int width) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t flat = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
   const int per_row = width / 8;
   if (flat >= static_cast<int64_t>(rows) * per_row) return;
@@ -198,6 +273,8 @@ __global__ void __launch_bounds__(kThreads)
 
 __global__ void __launch_bounds__(kThreads)
     merge_kernel(const float* partial, int splits, int64_t count, void* out, int out_fp32) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t i = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) * 4;
   if (i >= count) return;
   float x[4];
@@ -220,99 +297,43 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
-// Tensor-parallel all-reduce consumer fused with the residual add + RMSNorm. Every rank's
-// projection kernel pushed its fp32 [rows, W] partial into slab `rank` of this rank's
-// recv[use] and added one arrival per 128-column tile to arrivals[use]; once all
-// world * tiles arrivals are in, the slabs are summed in rank order (identical bits on every
-// rank), rounded to bf16 (the projection's output) and fed to add_rms_norm's arithmetic.
-// The last CTA to finish resets the use's arrival and completion counters for the next step.
-struct ReduceParams {
-  const float* recv;        // [uses, world, rows, W] on this rank
-  unsigned* arrivals;       // [uses] on this rank, bumped by every rank's producer
-  unsigned* done;           // [uses] on this rank
-  int use, world, expected;
-  const __nv_bfloat16* residual;
-  const __nv_bfloat16* w;
-  __nv_bfloat16* out;
-  __nv_bfloat16* sum;
-  int rows, width;
-  float eps;
-  unsigned* err;
+// Launch shape of the RMSNorm kernel: CTAs per row (cluster size) and threads per CTA.
+struct Shape {
+  int cluster, threads;
 };
 
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
+int shape_for(int rows, int width, Shape* out) {
+  if (width <= 0 || width % 8 != 0) return FB_ERR_SHAPE;
+  const int chunks = width / 8;
+  // Few rows (decode): spread each row over a cluster so its loads use many SMs. Many rows
+  // (prefill): one CTA per row unless the row does not fit one CTA.
+  int c = 1;
+  if (rows < 2 * sm_count()) c = chunks >= 512 ? 8 : chunks >= 256 ? 4 : chunks >= 128 ? 2 : 1;
+  while (c < kMaxCluster && (chunks + c - 1) / c > kMaxThreads * kMaxPer) c *= 2;
+  const int per = (chunks + c - 1) / c;
+  if (per > kMaxThreads * kMaxPer) return FB_ERR_SHAPE;
+  int t = per <= kMaxThreads ? per : (per + kMaxPer - 1) / kMaxPer;
+  t = (t + 31) / 32 * 32;
+  if (t > kMaxThreads) t = kMaxThreads;
+  out->cluster = c;
+  out->threads = t;
+  return FB_OK;
 }
 
-__global__ void __launch_bounds__(kThreads) allreduce_add_rmsnorm_kernel(const ReduceParams p) {
-  __shared__ float scratch[kThreads / 32];
-  __shared__ int ok;
-  const int row = blockIdx.x;
-  if (threadIdx.x == 0) {
-    const unsigned long long start = globaltimer();
-    // After one wait has given up, fail fast instead of spending the budget again per use.
-    int good = p.err == nullptr || (*reinterpret_cast<volatile unsigned*>(p.err) & kErrTimeoutFull) == 0;
-    while (good && ld_acquire_sys(p.arrivals + p.use) < static_cast<unsigned>(p.expected)) {
-      if (globaltimer() - start > kWaitBudgetNs) {
-        raise_error(p.err, kErrTimeoutFull);
-        good = 0;
-        break;
-      }
-    }
-    ok = good;
-  }
-  __syncthreads();
-  const int chunks = p.width / 8;
-  const size_t slab = static_cast<size_t>(p.rows) * p.width;
-  const float* recv = p.recv + static_cast<size_t>(p.use) * p.world * slab + static_cast<size_t>(row) * p.width;
-  float v[kMaxChunks][8];
-  float ss = 0.f;
-#pragma unroll
-  for (int i = 0; i < kMaxChunks; ++i) {
-    const int ch = threadIdx.x + i * kThreads;
-    if (ch < chunks && ok) {
-      float x[8];
-      // rank-order fp32 sum of the partials, then the projection's bf16 rounding
-      load8(recv, p.world, slab, static_cast<size_t>(ch) * 8, x);
-      float r[8];
-      load8(p.residual, 0, 0, static_cast<size_t>(row) * p.width + ch * 8, r);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) v[i][e] = bf16_round(x[e] + r[e]);
-      store8(p.sum + static_cast<size_t>(row) * p.width + ch * 8, v[i]);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) ss += v[i][e] * v[i][e];
-    }
-  }
-  ss = block_sum(ss, scratch);
-  const float inv = 1.0f / sqrtf(ss / static_cast<float>(p.width) + p.eps);
-#pragma unroll
-  for (int i = 0; i < kMaxChunks; ++i) {
-    const int ch = threadIdx.x + i * kThreads;
-    if (ch < chunks && ok) {
-      float w[8], y[8];
-      load_w8(p.w, ch * 8, w);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) y[e] = bf16_round(v[i][e] * inv) * w[e];
-      store8(p.out + static_cast<size_t>(row) * p.width + ch * 8, y);
-    }
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    if (atomicAdd(p.done + p.use, 1u) == static_cast<unsigned>(gridDim.x) - 1) {
-      // every row has read this use's slabs: ready for the next step
-      p.done[p.use] = 0;
-      atomicExch(p.arrivals + p.use, 0u);
-    }
-  }
+template <int MODE>
+int launch_rmsnorm(const Params& p, void* stream) {
+  Shape sh;
+  const int st = shape_for(p.rows, p.width, &sh);
+  if (st != FB_OK) return st;
+  const long long grid = static_cast<long long>(p.rows) * sh.cluster;
+  if (grid >= (1ll << 31)) return FB_ERR_SHAPE;
+  return launch_ex(rmsnorm_kernel<MODE>, dim3(static_cast<unsigned>(grid)), dim3(sh.threads), 0,
+                   static_cast<cudaStream_t>(stream), sh.cluster, p);
 }
 
 int check_width(int width) {
-  if (width <= 0 || width % 8 != 0) return FB_ERR_SHAPE;
-  if (width > 8 * kThreads * kMaxChunks) return FB_ERR_SHAPE;
-  return FB_OK;
+  Shape sh;
+  return shape_for(1, width, &sh);
 }
 
 }  // namespace norm
@@ -336,8 +357,7 @@ extern "C" int fb_rmsnorm(const void* x, int64_t row_stride, const void* w, void
   p.width = width;
   p.eps = eps;
   p.err = error_word();
-  norm::rmsnorm_kernel<0><<<rows, norm::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
-  return check_launch();
+  return norm::launch_rmsnorm<0>(p, stream);
 }
 
 extern "C" int fb_add_rmsnorm(const void* x, int x_splits, const void* residual, const void* w,
@@ -356,8 +376,7 @@ extern "C" int fb_add_rmsnorm(const void* x, int x_splits, const void* residual,
   p.width = width;
   p.eps = eps;
   p.err = error_word();
-  norm::rmsnorm_kernel<1><<<rows, norm::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
-  return check_launch();
+  return norm::launch_rmsnorm<1>(p, stream);
 }
 
 extern "C" int fb_embed_rmsnorm(const int64_t* ids, const void* table, int64_t vocab, const void* w,
@@ -378,8 +397,7 @@ extern "C" int fb_embed_rmsnorm(const int64_t* ids, const void* table, int64_t v
   p.width = width;
   p.eps = eps;
   p.err = error_word();
-  norm::rmsnorm_kernel<2><<<rows, norm::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
-  return check_launch();
+  return norm::launch_rmsnorm<2>(p, stream);
 }
 
 extern "C" int fb_swiglu(const void* packed, int splits, void* out, int rows, int width,
@@ -389,9 +407,9 @@ extern "C" int fb_swiglu(const void* packed, int splits, void* out, int rows, in
   const int64_t threads = static_cast<int64_t>(rows) * (width / 8);
   const int64_t blocks = (threads + norm::kThreads - 1) / norm::kThreads;
   if (blocks >= (1ll << 31)) return FB_ERR_SHAPE;
-  norm::swiglu_kernel<<<static_cast<unsigned>(blocks), norm::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      packed, splits, static_cast<__nv_bfloat16*>(out), rows, width);
-  return check_launch();
+  return launch_ex(norm::swiglu_kernel, dim3(static_cast<unsigned>(blocks)), dim3(norm::kThreads), 0,
+                   static_cast<cudaStream_t>(stream), 1, packed, splits, static_cast<__nv_bfloat16*>(out), rows,
+                   width);
 }
 
 extern "C" int fb_merge_splits(const void* partial, int splits, int64_t count, void* out,
@@ -399,9 +417,8 @@ extern "C" int fb_merge_splits(const void* partial, int splits, int64_t count, v
   if (!partial || !out || splits <= 0 || count <= 0) return FB_ERR_ARG;
   const int64_t threads = (count + 3) / 4;
   const int blocks = static_cast<int>((threads + norm::kThreads - 1) / norm::kThreads);
-  norm::merge_kernel<<<blocks, norm::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const float*>(partial), splits, count, out, out_fp32);
-  return check_launch();
+  return launch_ex(norm::merge_kernel, dim3(blocks), dim3(norm::kThreads), 0, static_cast<cudaStream_t>(stream), 1,
+                   static_cast<const float*>(partial), splits, count, out, out_fp32);
 }
 
 extern "C" int fb_allreduce_add_rmsnorm(const void* recv, void* arrivals, void* done, int use, int world,
@@ -411,21 +428,20 @@ extern "C" int fb_allreduce_add_rmsnorm(const void* recv, void* arrivals, void* 
   if (use < 0 || world < 1 || expected < 1 || rows <= 0) return FB_ERR_ARG;
   int st = norm::check_width(width);
   if (st != FB_OK) return st;
-  norm::ReduceParams p;
-  p.recv = static_cast<const float*>(recv);
-  p.arrivals = static_cast<unsigned*>(arrivals);
-  p.done = static_cast<unsigned*>(done);
-  p.use = use;
-  p.world = world;
-  p.expected = expected;
+  const size_t slab = static_cast<size_t>(rows) * width;
+  norm::Params p{};
+  p.x = static_cast<const float*>(recv) + static_cast<size_t>(use) * world * slab;
+  p.splits = world;
+  p.arrivals = static_cast<unsigned*>(arrivals) + use;
+  p.done = static_cast<unsigned*>(done) + use;
+  p.expected = static_cast<unsigned>(expected);
   p.residual = static_cast<const __nv_bfloat16*>(residual);
   p.w = static_cast<const __nv_bfloat16*>(w);
-  p.out = static_cast<__nv_bfloat16*>(out);
+  p.y = static_cast<__nv_bfloat16*>(out);
   p.sum = static_cast<__nv_bfloat16*>(sum);
   p.rows = rows;
   p.width = width;
   p.eps = eps;
   p.err = error_word();
-  norm::allreduce_add_rmsnorm_kernel<<<rows, norm::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
-  return check_launch();
+  return norm::launch_rmsnorm<3>(p, stream);
 }

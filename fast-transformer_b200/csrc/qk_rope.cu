@@ -53,39 +53,33 @@ __device__ __forceinline__ void load_packed(const Params& p, size_t off, size_t 
     }
   } else {
     const float* src = static_cast<const float*>(p.packed) + off;
-    const float4* src4 = reinterpret_cast<const float4*>(src);
-    float v0[E];
-    if constexpr (E == 4) {
-      const float4 a = __ldg(src4);
-      v0[0] = a.x; v0[1] = a.y; v0[2] = a.z; v0[3] = a.w;
-    } else {
-      const float2 a = __ldg(reinterpret_cast<const float2*>(src));
-      v0[0] = a.x; v0[1] = a.y;
-    }
+    // Loads of up to eight slabs in flight before their in-order adds (one round trip for
+    // S <= 8).
+    for (int s0 = 0; s0 < p.splits; s0 += 8) {
+      float y[8][E];
 #pragma unroll
-    for (int e = 0; e < E; ++e) x[e] = v0[e];
-    // Loads of up to four slabs in flight before their in-order adds.
-    for (int s0 = 1; s0 < p.splits; s0 += 4) {
-      float y[4][E];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
+      for (int j = 0; j < 8; ++j) {
         if (s0 + j < p.splits) {
           const float* q = src + (s0 + j) * split_stride;
           if constexpr (E == 4) {
-            const float4 a = __ldg(reinterpret_cast<const float4*>(q));
+            const float4 a = __ldcg(reinterpret_cast<const float4*>(q));
             y[j][0] = a.x; y[j][1] = a.y; y[j][2] = a.z; y[j][3] = a.w;
           } else {
-            const float2 a = __ldg(reinterpret_cast<const float2*>(q));
+            const float2 a = __ldcg(reinterpret_cast<const float2*>(q));
             y[j][0] = a.x; y[j][1] = a.y;
           }
         }
       }
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        if (s0 + j < p.splits) {
+      for (int j = 0; j < 8; ++j) {
+        if (s0 + j == 0) {
+#pragma unroll
+          for (int e = 0; e < E; ++e) x[e] = y[0][e];
+        } else if (s0 + j < p.splits) {
 #pragma unroll
           for (int e = 0; e < E; ++e) x[e] += y[j][e];
         }
+      }
     }
 #pragma unroll
     for (int e = 0; e < E; ++e) x[e] = bf16_round(x[e]);
@@ -99,7 +93,7 @@ __global__ void __launch_bounds__(128) qk_rope_kernel(const Params p) {
   const int lane = threadIdx.x & 31;
   const int heads = p.q_heads + p.kv_heads;
   const int rows = p.batch * p.tokens;
-  if (warp_global >= rows * heads) return;
+  if (warp_global >= rows * heads) return;  // a CTA's spare warps touch nothing
   const int row = warp_global / heads;
   const int head = warp_global % heads;
   const int b = row / p.tokens;
@@ -110,12 +104,7 @@ __global__ void __launch_bounds__(128) qk_rope_kernel(const Params p) {
 
   const bool is_q = head < p.q_heads;
   const int kvh = head - p.q_heads;
-  // Every global read is issued up front (the V head before any store that could alias it).
-  float x[E], v[E];
-  load_packed<E>(p, static_cast<size_t>(row) * width + head * D + d0, split_stride, x);
-  if (!is_q)
-    load_packed<E>(p, static_cast<size_t>(row) * width + (p.q_heads + p.kv_heads + kvh) * D + d0,
-                   split_stride, v);
+  // the norm gains are never written while decoding: load them before the dependency wait
   const __nv_bfloat16* gain = is_q ? p.q_weight : p.k_weight;
   float gw[E];
   if constexpr (E == 4) {
@@ -129,6 +118,15 @@ __global__ void __launch_bounds__(128) qk_rope_kernel(const Params p) {
     gw[0] = bf16_lo(gv);
     gw[1] = bf16_hi(gv);
   }
+  pdl_wait();
+  pdl_trigger();
+  // Every other global read is issued up front (the V head before any store that could
+  // alias it).
+  float x[E], v[E];
+  load_packed<E>(p, static_cast<size_t>(row) * width + head * D + d0, split_stride, x);
+  if (!is_q)
+    load_packed<E>(p, static_cast<size_t>(row) * width + (p.q_heads + p.kv_heads + kvh) * D + d0,
+                   split_stride, v);
   long long pos_base = 0;
   if (p.mode == 2)
     pos_base = __ldg(p.position + b);
@@ -238,9 +236,6 @@ extern "C" int fb_qk_norm_rope_append(const void* packed, int packed_splits, con
   const long long warps = static_cast<long long>(batch) * tokens * (q_heads + kv_heads);
   const int blocks = static_cast<int>((warps + 3) / 4);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (head_dim == 128)
-    rope::qk_rope_kernel<128><<<blocks, 128, 0, s>>>(p);
-  else
-    rope::qk_rope_kernel<64><<<blocks, 128, 0, s>>>(p);
-  return check_launch();
+  if (head_dim == 128) return launch_ex(rope::qk_rope_kernel<128>, dim3(blocks), dim3(128), 0, s, 1, p);
+  return launch_ex(rope::qk_rope_kernel<64>, dim3(blocks), dim3(128), 0, s, 1, p);
 }

@@ -132,6 +132,8 @@ struct Smem {
 __global__ void __launch_bounds__(kThreads, 1)
     verify_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                   const Params p) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = base;
@@ -384,6 +386,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // LSE merge over KV splits, token-major output (decode_attention.py:455-478). One CTA per
 // (row, token, query head); thread = dim.
 __global__ void __launch_bounds__(128) verify_merge_kernel(const Params p) {
+  pdl_wait();
+  pdl_trigger();
   const int index = blockIdx.x;  // (b, t, hq) in output order
   const int hq = index % p.q_heads;
   const int t = (index / p.q_heads) % p.tokens;
@@ -490,9 +494,7 @@ extern "C" int fb_verify_attention(const void* q, const void* k, const void* v, 
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   dim3 grid(batch * kv_heads, splits, member_groups);
-  verify::verify_kernel<<<grid, verify::kThreads, verify::Smem::kTotal, s>>>(km, vm, p);
-  st = check_launch();
+  st = launch_ex(verify::verify_kernel, grid, dim3(verify::kThreads), verify::Smem::kTotal, s, 1, km, vm, p);
   if (st != FB_OK || splits == 1) return st;
-  verify::verify_merge_kernel<<<batch * tokens * q_heads, 128, 0, s>>>(p);
-  return check_launch();
+  return launch_ex(verify::verify_merge_kernel, dim3(batch * tokens * q_heads), dim3(128), 0, s, 1, p);
 }

@@ -1,7 +1,7 @@
 """Run one decode-path kernel (or one eager decode step) at a chosen shape, for Nsight Compute.
 
     python fast-transformer_b200/profile_kernels.py attention --batch 16 --length 8320
-    python fast-transformer_b200/profile_kernels.py linear --m 16 --n 24576 --k 4096
+    python fast-transformer_b200/profile_kernels.py linear --m 16 --n 24576 --k 4096 --epilogue 2
     python fast-transformer_b200/profile_kernels.py verify --batch 8 --tokens 5 --length 4101
     python fast-transformer_b200/profile_kernels.py step --preset qwen3-8b --batch 16 --length 8192
 
@@ -66,22 +66,23 @@ def attention(args):
 
 
 def linear(args):
-    from kernels.linear import project, splits_for
+    from kernels.linear import SPLITS_OUT, project, splits_for
     x = torch.randn(args.m, args.k, device="cuda").bfloat16()
     weights = [(torch.randn(args.n, args.k, device="cuda") * 0.02).bfloat16() for _ in range(args.copies)]
-    splits = splits_for(args.m, args.n, args.k, x.device)
+    splits = splits_for(args.m, args.n, args.k, x.device, finished=args.epilogue != SPLITS_OUT)
 
     def run():
         for w in weights:
-            project(x, w, splits)
+            project(x, w, args.epilogue, splits)
 
     ms = graph_time(run) / len(weights)
     nbytes = args.n * args.k * 2
-    print(f"linear M={args.m} N={args.n} K={args.k} S={splits}: {ms * 1e3:.2f} us, {nbytes / ms / 1e6:.0f} GB/s")
+    print(f"linear M={args.m} N={args.n} K={args.k} epilogue={args.epilogue} S={splits}: {ms * 1e3:.2f} us, "
+          f"{nbytes / ms / 1e6:.0f} GB/s")
     torch.cuda.synchronize()
     torch.cuda.nvtx.range_push("profiled")
     for _ in range(args.launches):
-        project(x, weights[0], splits)
+        project(x, weights[0], args.epilogue, splits)
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
 
@@ -143,6 +144,7 @@ def main():
     parser.add_argument("--m", type=int, default=16)
     parser.add_argument("--n", type=int, default=24576)
     parser.add_argument("--k", type=int, default=4096)
+    parser.add_argument("--epilogue", type=int, default=3, help="0 bf16, 1 fp32, 2 SwiGLU, 3 split partials")
     parser.add_argument("--preset", default="qwen3-8b")
     parser.add_argument("--copies", type=int, default=2)
     parser.add_argument("--launches", type=int, default=2)

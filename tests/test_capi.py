@@ -52,7 +52,7 @@ def test_host_validation_without_gpu():
     assert lib.fb_linear(p, p, p, 4, 128, 128, 0, 3, null) == -2      # more splits than K chunks
     assert lib.fb_linear(p, p, p, 4, 128, 4096, 0, 9, null) == -2     # finished tile: cluster of <= 8 splits
     assert lib.fb_swiglu(p, 1, p, 4, 12, null) == -2                     # width % 8
-    assert lib.fb_add_rmsnorm(p, 1, p, p, p, p, 4, 20000, 1e-6, null) == -2  # row too wide
+    assert lib.fb_add_rmsnorm(p, 1, p, p, p, p, 4, 70000, 1e-6, null) == -2  # row too wide (> 65536)
     assert lib.fb_decode_attention(p, p, p, p, 0, p, p, 1 << 20, 1, 16, 8, 96, 2048, 0.1, 148, null) == -2  # D=96
     assert lib.fb_decode_attention(p, p, p, p, 0, p, p, 1 << 20, 1, 72, 8, 128, 2048, 0.1, 148, null) == -2  # G=9
     # workspace too small -> FB_ERR_WORKSPACE
