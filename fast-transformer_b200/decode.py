@@ -10,10 +10,11 @@ eagerly through cuBLAS and torch SDPA for the big GEMMs and prompt attention (as
 reference's prefill does, engine/layers.py:69-74), with the fused kernel writing the cache.
 
 Tensor parallelism (by KV head, see qwen3.py): o_proj and down_proj run as
-fb_linear_allreduce_push, which stores every finished fp32 output tile straight into each
-rank's receive buffer (torch symmetric memory, NVLink peer stores) and bumps that rank's
-arrival counter; fb_allreduce_add_rmsnorm then sums the ranks' slabs in rank order and applies
-the residual add + RMSNorm. Every rank therefore runs the same norms, LM head and argmax on
+fb_linear_allreduce_push, which stores every finished fp32 output value straight into each
+rank's receive buffer (torch symmetric memory, NVLink peer stores) as an 8-byte word carrying
+a flag (the decode position + 1); fb_allreduce_add_rmsnorm polls the flags, sums the ranks'
+slabs in rank order and applies the residual add + RMSNorm. No fence, counter or barrier
+sits on the step's path. Every rank therefore runs the same norms, LM head and argmax on
 bit-identical data. Prefill (eager, untimed) uses NCCL all-reduces.
 """
 
@@ -84,8 +85,9 @@ class Communicator:
 
 
 class PeerBuffers:
-    """Receive slabs fp32 [uses, world, rows, width] + arrival/done counters uint32 [uses] in
-    torch symmetric memory, with every rank's base address for NVLink peer stores."""
+    """Receive slabs in torch symmetric memory, uint64 words [uses, world, rows, width] (fp32
+    bits + a 32-bit flag per value: the low-latency push protocol), with every rank's base
+    address for NVLink peer stores."""
 
     def __init__(self, comm, uses, rows, width, device):
         import os
@@ -94,35 +96,30 @@ class PeerBuffers:
         import torch.distributed._symmetric_memory as symm_mem
         world = comm.size
         self.uses, self.world, self.rows, self.width = uses, world, rows, width
-        recv = uses * world * rows * width * 4
-        self.recv_bytes = (recv + 255) // 256 * 256
-        total = self.recv_bytes + 2 * ((uses * 4 + 255) // 256 * 256)
-        group = comm.group if comm.group is not None else torch.distributed.group.WORLD
+        total = uses * world * rows * width * 8
+        self.group = comm.group if comm.group is not None else torch.distributed.group.WORLD
         if hasattr(symm_mem, "enable_symm_mem_for_group"):
             try:
-                symm_mem.enable_symm_mem_for_group(group.group_name)
+                symm_mem.enable_symm_mem_for_group(self.group.group_name)
             except Exception:  # noqa: BLE001 - newer torch enables groups on demand
                 pass
         self.buf = symm_mem.empty(total, dtype=torch.uint8, device=device)
-        self.buf.zero_()
-        torch.cuda.synchronize(device)
-        handle = symm_mem.rendezvous(self.buf, group)
-        bases = [int(b) for b in handle.buffer_ptrs]
+        handle = symm_mem.rendezvous(self.buf, self.group)
         self.handle = handle
-        self.multicast = bool(handle.has_multicast_support())
-        self.recv_ptrs = (ctypes.c_void_p * world)(*bases)
-        self.arrival_ptrs = (ctypes.c_void_p * world)(*[b + self.recv_bytes for b in bases])
-        local = self.buf.data_ptr()
-        self.recv_local = ctypes.c_void_p(local)
-        self.arrivals_local = ctypes.c_void_p(local + self.recv_bytes)
-        self.done_local = ctypes.c_void_p(local + self.recv_bytes + (uses * 4 + 255) // 256 * 256)
-        self.tiles = (width + 127) // 128
-        torch.distributed.barrier(group=group)
+        # a multicast object would show as a non-zero multicast address
+        self.multicast = bool(int(getattr(handle, "multicast_ptr", 0) or 0))
+        self.recv_ptrs = (ctypes.c_void_p * world)(*[int(b) for b in handle.buffer_ptrs])
+        self.recv_local = ctypes.c_void_p(self.buf.data_ptr())
+        self.reset()
 
     def reset(self):
-        """Zero every counter (between generations, with all ranks idle)."""
-        self.buf[self.recv_bytes:].zero_()
-        torch.cuda.synchronize()
+        """Zero every slab with all ranks idle (before first use and whenever the epoch, the
+        decode position, may repeat a value: a new generation), then meet the other ranks so
+        no push of the next step can land before the zeroing."""
+        self.buf.zero_()
+        torch.cuda.synchronize(self.buf.device)
+        torch.distributed.barrier(group=self.group)
+        torch.cuda.synchronize(self.buf.device)
 
 
 def _qk_rope_decode(packed, layer, eps, cos, sin, position, keys, values, q_heads):
@@ -139,25 +136,26 @@ def _qk_rope_decode(packed, layer, eps, cos, sin, position, keys, values, q_head
     return query.view(batch, q_heads, 1, dim)  # one token: token-major storage is [B, Hq, 1, D]
 
 
-def _push_projection(x, weight, comm, peers, use):
-    """This rank's fp32 partial of x @ W^T, pushed to every rank's recv[use] (fb_linear_allreduce_push)."""
+def _push_projection(x, weight, comm, peers, use, epoch):
+    """This rank's fp32 partial of x @ W^T, pushed to every rank's recv[use] flagged with
+    epoch + 1 (fb_linear_allreduce_push)."""
     rows = x.numel() // x.shape[-1]
     flat = x.reshape(rows, x.shape[-1]).contiguous()
     n, k = weight.shape
     splits = klinear.splits_for(rows, n, k, x.device, finished=True)
     check(lib.fb_linear_allreduce_push(ptr(flat), ptr(weight), rows, n, k, splits, comm.size, comm.rank, use,
-                                       peers.recv_ptrs, peers.arrival_ptrs, stream()),
+                                       peers.recv_ptrs, ptr(epoch), stream()),
           "fb_linear_allreduce_push")
 
 
-def _reduce_add_norm(peers, use, residual, weight, eps):
+def _reduce_add_norm(peers, use, epoch, residual, weight, eps):
     """(normalized, summed) = add_rms_norm(all-reduced recv[use], residual) (fb_allreduce_add_rmsnorm)."""
     rows, width = residual.numel() // residual.shape[-1], residual.shape[-1]
     out = torch.empty_like(residual)
     summed = torch.empty_like(residual)
-    check(lib.fb_allreduce_add_rmsnorm(peers.recv_local, peers.arrivals_local, peers.done_local, use, peers.world,
-                                       peers.world * peers.tiles, ptr(residual), ptr(weight), ptr(out), ptr(summed),
-                                       rows, width, float(eps), stream()), "fb_allreduce_add_rmsnorm")
+    check(lib.fb_allreduce_add_rmsnorm(peers.recv_local, use, peers.world, ptr(epoch), ptr(residual), ptr(weight),
+                                       ptr(out), ptr(summed), rows, width, float(eps), stream()),
+          "fb_allreduce_add_rmsnorm")
     return out, summed
 
 
@@ -214,15 +212,15 @@ class DecodeState:
                 out = linear(attention, layer.o, split_ok=True)
                 normalized, residual = add_rms_norm(out, residual, layer.ln2, eps)
             else:
-                _push_projection(attention, layer.o, comm, peers, 2 * index)
-                normalized, residual = _reduce_add_norm(peers, 2 * index, residual, layer.ln2, eps)
+                _push_projection(attention, layer.o, comm, peers, 2 * index, self.position)
+                normalized, residual = _reduce_add_norm(peers, 2 * index, self.position, residual, layer.ln2, eps)
             activated = swiglu_linear(normalized, layer.gate_up)
             if peers is None:
                 hidden = linear(activated, layer.down, split_ok=True)
             else:
-                _push_projection(activated, layer.down, comm, peers, 2 * index + 1)
+                _push_projection(activated, layer.down, comm, peers, 2 * index + 1, self.position)
                 following = layers[index + 1].ln1 if index + 1 < len(layers) else w.final_norm
-                normalized, residual = _reduce_add_norm(peers, 2 * index + 1, residual, following, eps)
+                normalized, residual = _reduce_add_norm(peers, 2 * index + 1, self.position, residual, following, eps)
         if peers is None:
             normalized, _ = add_rms_norm(hidden, residual, w.final_norm, eps)
         logits = linear(normalized, w.lm_head)
@@ -247,6 +245,8 @@ class DecodeState:
         torch.cuda.synchronize(self.device)
         self.position.copy_(saved_position)
         self.token_ids.copy_(saved_tokens)
+        if self.peers is not None:
+            self.peers.reset()  # the warmup pushed words flagged with the position replayed next
         self.graph = torch.cuda.CUDAGraph()
         before = _native.launches
         with torch.cuda.graph(self.graph, stream=side):
@@ -270,6 +270,8 @@ class DecodeState:
         eps = cfg.rms_norm_eps
         batch, length = prompt.shape
         assert batch == self.batch and length == self.prompt_length
+        if self.peers is not None:
+            self.peers.reset()  # a new generation replays positions an earlier one flagged
         positions = torch.arange(length, device=self.device)
         cos, sin = self.cos[:length][None].contiguous(), self.sin[:length][None].contiguous()
         last = torch.empty((batch, 1, cfg.hidden_size), dtype=BF16, device=self.device)

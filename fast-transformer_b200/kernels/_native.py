@@ -53,8 +53,8 @@ _SIGNATURES = {
     "fb_linear": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _vp]),
     "fb_linear_allreduce_push": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _vp,
                                           _vp]),
-    "fb_allreduce_add_rmsnorm": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _vp, _vp, _vp, _vp, _c_int,
-                                          _c_int, _c_float, _vp]),
+    "fb_allreduce_add_rmsnorm": (_c_int, [_vp, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_float,
+                                          _vp]),
     "fb_merge_splits": (_c_int, [_vp, _c_int, _c_i64, _vp, _c_int, _vp]),
     "fb_argmax_workspace": (_c_size, [_c_int, _c_i64]),
     "fb_argmax": (_c_int, [_vp, _c_int, _c_i64, _vp, _vp, _vp, _c_size, _vp]),

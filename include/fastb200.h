@@ -206,24 +206,27 @@ int fb_linear(const void* x, const void* w, void* out, int m, int n, int k, int 
 /* ------------------------------------------------------------------------------------
  * Tensor-parallel projection + all-reduce over NVLink peer memory (no counterpart in the
  * reference, which is single-GPU; this replaces an NCCL all-reduce after o_proj/down_proj).
- * Producer: fb_linear_allreduce_push computes this rank's fp32 partial of y = x @ W^T and
- *   stores every finished 128-column tile into slab `rank` of recv[use] on every rank
- *   (peer_recv[r] = rank r's recv base, fp32 [uses, world, M, N]), then adds 1 to
- *   arrivals[use] on every rank (peer_counter[r] = rank r's arrivals, uint32 [uses]) with a
- *   system-scope release.
- * Consumer: fb_allreduce_add_rmsnorm waits (bounded, 2 s) until this rank's arrivals[use]
- *   reaches `expected` (= world * ceil(N / 128)), sums the world slabs in rank order (the same
+ * Low-latency protocol: every value travels as one 8-byte word, low half the fp32 bits,
+ * high half the flag (uint32)(*epoch) + 1, stored whole; a reader that sees the flag sees
+ * the value, so there is no fence, counter or reset. recv[r] is rank r's receive buffer,
+ * uint64 words [uses, world, M, N]; zero it before first use and again before `*epoch`
+ * (a device int64, the decode position) can repeat a value it had (a new generation).
+ * *epoch must differ between two calls with the same `use` and stay below 2^31.
+ * Producer: fb_linear_allreduce_push computes this rank's fp32 partial of y = x @ W^T
+ *   (splits <= 8 K-splits summed in one thread-block cluster) and stores every value into
+ *   slab `rank` of recv[use] on every rank (peer_recv[r] = rank r's recv base).
+ * Consumer: fb_allreduce_add_rmsnorm polls (bounded, 2 s) this rank's recv[use] until
+ *   every word of the world slabs carries the flag, sums the slabs in rank order (the same
  *   bits on every rank), rounds to bf16 and applies add_rms_norm (fb_add_rmsnorm's
- *   arithmetic) with `residual`/`w`; the last CTA resets arrivals[use] and done[use]
- *   (uint32 [uses], local) for the next use. One call per use per step, in the same order
- *   on every rank.
+ *   arithmetic) with `residual`/`w`. One call per use per step, in the same order on every
+ *   rank.
  * ---------------------------------------------------------------------------------- */
 int fb_linear_allreduce_push(const void* x, const void* w, int m, int n, int k, int splits, int world,
-                             int rank, int use,
-                             void* const* peer_recv, void* const* peer_counter, void* stream);
-int fb_allreduce_add_rmsnorm(const void* recv, void* arrivals, void* done, int use, int world,
-                             int expected, const void* residual, const void* w, void* out,
-                             void* sum, int rows, int width, float eps, void* stream);
+                             int rank, int use, void* const* peer_recv, const int64_t* epoch,
+                             void* stream);
+int fb_allreduce_add_rmsnorm(const void* recv, int use, int world, const int64_t* epoch,
+                             const void* residual, const void* w, void* out, void* sum, int rows,
+                             int width, float eps, void* stream);
 
 /* Sums fp32 split partials [splits, count] into bf16 [count] (or fp32 when out_fp32):
  * the reference's `_merge_projection` (linear.py:81-93). */
