@@ -96,6 +96,102 @@ __global__ void __launch_bounds__(32)
   }
 }
 
+// Per-row reduction of the fused projection's tile candidates (fb_linear_argmax), then, in
+// tensor parallelism, the exchange of every rank's best: each rank stores its (value, index)
+// as two flagged words (low half the payload, high half (uint32)(*epoch) + 1) into slot
+// [row][rank] of every rank's exchange buffer and reduces the world slots once their flags
+// match. Every rank applies the same rule to the same words, so all ranks pick the same id.
+constexpr int kCandThreads = 128;
+constexpr int kMaxWorld = 8;
+
+struct CandParams {
+  const uint64_t* cand;  // [rows, tiles]: index << 32 | value bits
+  int rows, tiles, world, rank;
+  uint64_t* peers[kMaxWorld];  // every rank's exchange buffer, uint64 [rows, world, 2]
+  const uint64_t* local;       // this rank's exchange buffer
+  const int64_t* epoch;
+  int64_t* out;
+  float* top;
+  unsigned* err;
+};
+
+__device__ __forceinline__ void unpack(uint64_t w, float& v, int& i) {
+  v = __uint_as_float(static_cast<uint32_t>(w));
+  i = static_cast<int>(static_cast<uint32_t>(w >> 32));
+}
+
+__global__ void __launch_bounds__(kCandThreads) candidates_kernel(const CandParams p) {
+  __shared__ float sv[kCandThreads / 32];
+  __shared__ int si[kCandThreads / 32];
+  pdl_wait();
+  pdl_trigger();
+  const int row = blockIdx.x;
+  float v = -INFINITY;
+  int idx = 0x7fffffff;
+  for (int t = threadIdx.x; t < p.tiles; t += kCandThreads) {
+    float ov;
+    int oi;
+    unpack(p.cand[static_cast<size_t>(row) * p.tiles + t], ov, oi);
+    better(v, idx, ov, oi);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    better(v, idx, ov, oi);
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    sv[warp] = v;
+    si[warp] = idx;
+  }
+  __syncthreads();
+  if (warp != 0) return;
+  v = sv[0];
+  idx = si[0];
+  for (int w = 1; w < kCandThreads / 32; ++w) better(v, idx, sv[w], si[w]);
+  if (p.world > 1) {
+    const uint64_t flag = static_cast<uint64_t>(static_cast<uint32_t>(*p.epoch) + 1u) << 32;
+    const size_t mine = (static_cast<size_t>(row) * p.world + p.rank) * 2;
+    if (lane < p.world) {
+      const uint64_t w0 = flag | __float_as_uint(v), w1 = flag | static_cast<uint32_t>(idx);
+      asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p.peers[lane] + mine), "l"(w0), "l"(w1)
+                   : "memory");
+    }
+    v = -INFINITY;
+    idx = 0x7fffffff;
+    if (lane < p.world) {
+      const uint64_t* slot = p.local + (static_cast<size_t>(row) * p.world + lane) * 2;
+      const unsigned long long start = globaltimer();
+      bool good = p.err == nullptr || (*reinterpret_cast<volatile unsigned*>(p.err) & kErrTimeoutFull) == 0;
+      while (good) {
+        uint64_t w0, w1;
+        asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(w0), "=l"(w1) : "l"(slot) : "memory");
+        if ((w0 >> 32) == (flag >> 32) && (w1 >> 32) == (flag >> 32)) {
+          v = __uint_as_float(static_cast<uint32_t>(w0));
+          idx = static_cast<int>(static_cast<uint32_t>(w1));
+          break;
+        }
+        if (globaltimer() - start > kWaitBudgetNs) {
+          raise_error(p.err, kErrTimeoutFull);
+          good = false;
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+      better(v, idx, ov, oi);
+    }
+  }
+  if (lane == 0) {
+    // All -inf (or NaN-only) rows keep index 0, like torch.argmax on an all -inf row.
+    p.out[row] = idx == 0x7fffffff ? 0 : idx;
+    if (p.top != nullptr) p.top[row] = v;
+  }
+}
+
 }  // namespace amax
 }  // namespace fb
 
@@ -124,4 +220,31 @@ extern "C" int fb_argmax(const void* logits, int rows, int64_t vocab, int64_t* o
                      static_cast<const __nv_bfloat16*>(logits), vocab, blocks, bv, bi);
   if (st != FB_OK) return st;
   return launch_ex(amax::first_best_kernel, dim3(rows), dim3(32), 0, s, 1, bv, bi, blocks, out, top);
+}
+
+extern "C" int fb_argmax_candidates(const void* cand, int rows, int tiles, int world, int rank,
+                                    void* const* peer_exchange, const void* exchange_local, const int64_t* epoch,
+                                    int64_t* out, float* top, void* stream) {
+  if (!cand || !out || rows <= 0 || tiles <= 0) return FB_ERR_ARG;
+  if (world < 1 || world > amax::kMaxWorld || rank < 0 || rank >= world) return FB_ERR_ARG;
+  amax::CandParams p{};
+  p.cand = static_cast<const uint64_t*>(cand);
+  p.rows = rows;
+  p.tiles = tiles;
+  p.world = world;
+  p.rank = rank;
+  if (world > 1) {
+    if (!peer_exchange || !exchange_local || !epoch) return FB_ERR_ARG;
+    for (int r = 0; r < world; ++r) {
+      if (!peer_exchange[r] || (reinterpret_cast<uintptr_t>(peer_exchange[r]) & 15u)) return FB_ERR_ARG;
+      p.peers[r] = static_cast<uint64_t*>(peer_exchange[r]);
+    }
+    p.local = static_cast<const uint64_t*>(exchange_local);
+    p.epoch = epoch;
+  }
+  p.out = out;
+  p.top = top;
+  p.err = error_word();
+  return launch_ex(amax::candidates_kernel, dim3(rows), dim3(amax::kCandThreads), 0, static_cast<cudaStream_t>(stream),
+                   1, p);
 }

@@ -35,13 +35,14 @@ constexpr int kMaxPeers = 8;
 constexpr int kMaxTiles = 65535;       // grid x
 constexpr int kMaxClusterSplits = 8;  // portable cluster size: K-splits of one finished tile
 
-enum Epilogue : int { kBf16 = 0, kFp32 = 1, kSwiGLU = 2, kSplits = 3, kPush = 4 };
+enum Epilogue : int { kBf16 = 0, kFp32 = 1, kSwiGLU = 2, kSplits = 3, kPush = 4, kArgmax = 5 };
 
 struct Params {
   void* out;
   int m, n, k, splits, epilogue;
   // kPush: every value of the tile as a flagged word into recv[use][rank][m][n] of every peer
   int world, rank, use;
+  long long index_base;  // kArgmax: vocabulary index of column 0
   uint64_t* peer_recv[kMaxPeers];
   const int64_t* epoch;  // the word's flag is (uint32)(*epoch) + 1
   unsigned* err;
@@ -75,6 +76,43 @@ template <int MT>
 __device__ void epilogue(const Params& p, const float* vals, int tile, int tid, int r, int S) {
   constexpr int MP = MT * 16;
   const int n0 = tile * kTileN;
+  if (p.epilogue == kArgmax) {
+    // Each row's (max, first index) over this tile's bf16-rounded logits (the values the
+    // projection would store), packed as index << 32 | value bits into cand[m][tile]. The
+    // tile's accumulation is one split over the whole of K, like the projection at S = 1.
+    const int warp = tid >> 5, lane = tid & 31;
+    for (int m = warp; m < p.m; m += kConsumerWarps) {
+      const float4 v4 = *reinterpret_cast<const float4*>(vals + m * kTileN + lane * 4);
+      const float vs[4] = {v4.x, v4.y, v4.z, v4.w};
+      float bv = -INFINITY;
+      int bi = 0x7fffffff;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int col = n0 + lane * 4 + e;
+        const float v = bf16_round(vs[e]);
+        if (col < p.n && (v > bv || (v == bv && col < bi))) {
+          bv = v;
+          bi = col;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) {
+          bv = ov;
+          bi = oi;
+        }
+      }
+      if (lane == 0) {
+        // no candidate (all -inf or NaN): index sentinel 0x7fffffff, never offset
+        const uint32_t index = bi == 0x7fffffff ? 0x7fffffffu : static_cast<uint32_t>(p.index_base + bi);
+        static_cast<uint64_t*>(p.out)[static_cast<size_t>(m) * gridDim.x + tile] =
+            (static_cast<uint64_t>(index) << 32) | __float_as_uint(bv);
+      }
+    }
+    return;
+  }
   if (p.epilogue == kSwiGLU) {
     // Tile rows [0, 64) are gate features f0..f0+63 and rows [64, 128) the up features of the
     // same f: out[m][f] = bf16(bf16(silu(bf16(g))) * bf16(u)).
@@ -375,11 +413,12 @@ extern "C" int fb_linear_splits(int m, int n, int k) {
 
 static int linear_impl(const void* x, const void* w, void* out, int m, int n, int k, int epilogue, int splits,
                        void* stream, int world, int rank, int use, void* const* peer_recv,
-                       const int64_t* epoch) {
+                       const int64_t* epoch, int64_t index_base = 0) {
   if (!x || !w || !out || m <= 0 || n <= 0 || k <= 0 || splits <= 0) return FB_ERR_ARG;
   if (m > 64 || k % 8 != 0 || n % 8 != 0) return FB_ERR_SHAPE;
   if ((n + lin::kTileN - 1) / lin::kTileN > lin::kMaxTiles) return FB_ERR_SHAPE;
   if (epilogue == lin::kSwiGLU && n % lin::kTileN != 0) return FB_ERR_SHAPE;
+  if (epilogue == lin::kArgmax && splits != 1) return FB_ERR_SHAPE;
   if (splits > (k + lin::kTileK - 1) / lin::kTileK || splits > 65535) return FB_ERR_SHAPE;
   if (epilogue != lin::kSplits && splits > lin::kMaxClusterSplits) return FB_ERR_SHAPE;
   const int mt = lin::row_tiles(m);
@@ -398,6 +437,7 @@ static int linear_impl(const void* x, const void* w, void* out, int m, int n, in
   p.world = world;
   p.rank = rank;
   p.use = use;
+  p.index_base = index_base;
   if (epilogue == lin::kPush) {  // only the push form has peer buffers
     for (int r = 0; r < world && r < lin::kMaxPeers; ++r) p.peer_recv[r] = static_cast<uint64_t*>(peer_recv[r]);
     p.epoch = epoch;
@@ -413,6 +453,17 @@ extern "C" int fb_linear(const void* x, const void* w, void* out, int m, int n, 
                          void* stream) {
   if (epilogue < lin::kBf16 || epilogue > lin::kSplits) return FB_ERR_ARG;
   return linear_impl(x, w, out, m, n, k, epilogue, splits, stream, 1, 0, 0, nullptr, nullptr);
+}
+
+extern "C" size_t fb_argmax_candidates_bytes(int m, int n) {
+  if (m <= 0 || n <= 0) return 0;
+  return static_cast<size_t>(m) * ((n + lin::kTileN - 1) / lin::kTileN) * sizeof(uint64_t);
+}
+
+extern "C" int fb_linear_argmax(const void* x, const void* w, int m, int n, int k, int64_t index_base, void* cand,
+                                void* stream) {
+  if (!cand || index_base < 0 || index_base + n > 0x7ffffffe) return FB_ERR_ARG;
+  return linear_impl(x, w, cand, m, n, k, lin::kArgmax, 1, stream, 1, 0, 0, nullptr, nullptr, index_base);
 }
 
 extern "C" int fb_linear_allreduce_push(const void* x, const void* w, int m, int n, int k, int splits, int world,

@@ -26,7 +26,7 @@ import torch
 import torch.nn.functional as F
 
 from kernels import _native
-from kernels.argmax import argmax
+from kernels.argmax import argmax, fused_argmax
 from kernels.decode_attention import attend as attend_decode
 from kernels import linear as klinear
 from kernels.linear import linear, swiglu_linear
@@ -96,7 +96,9 @@ class PeerBuffers:
         import torch.distributed._symmetric_memory as symm_mem
         world = comm.size
         self.uses, self.world, self.rows, self.width = uses, world, rows, width
-        total = uses * world * rows * width * 8
+        self.recv_bytes = uses * world * rows * width * 8
+        # argmax exchange slots after the slabs: uint64 [rows, world, 2]
+        total = self.recv_bytes + rows * world * 2 * 8
         self.group = comm.group if comm.group is not None else torch.distributed.group.WORLD
         if hasattr(symm_mem, "enable_symm_mem_for_group"):
             try:
@@ -110,6 +112,8 @@ class PeerBuffers:
         self.multicast = bool(int(getattr(handle, "multicast_ptr", 0) or 0))
         self.recv_ptrs = (ctypes.c_void_p * world)(*[int(b) for b in handle.buffer_ptrs])
         self.recv_local = ctypes.c_void_p(self.buf.data_ptr())
+        self.exchange_ptrs = (ctypes.c_void_p * world)(*[int(b) + self.recv_bytes for b in handle.buffer_ptrs])
+        self.exchange_local = ctypes.c_void_p(self.buf.data_ptr() + self.recv_bytes)
         self.reset()
 
     def reset(self):
@@ -192,8 +196,14 @@ class DecodeState:
             self.peers = PeerBuffers(self.comm, 2 * cfg.num_hidden_layers, batch, cfg.hidden_size, self.device)
 
     # ------------------------------------------------------------------ decode step
-    def decode(self):
-        """One greedy step for every row (the captured body)."""
+    def decode(self, keep_logits=False):
+        """One greedy step for every row (the captured body).
+
+        The greedy ids come from the fused LM-head argmax (no logits written; vocabulary-
+        parallel under tensor parallelism). With ``keep_logits`` the full logits are projected
+        (one K split, the fused kernel's arithmetic) into ``self.logits`` and reduced by
+        argmax instead - the same ids.
+        """
         w, cfg, cache, comm, peers = self.w, self.cfg, self.cache, self.comm, self.peers
         eps = cfg.rms_norm_eps
         layers = w.layers
@@ -223,9 +233,16 @@ class DecodeState:
                 normalized, residual = _reduce_add_norm(peers, 2 * index + 1, self.position, residual, following, eps)
         if peers is None:
             normalized, _ = add_rms_norm(hidden, residual, w.final_norm, eps)
-        logits = linear(normalized, w.lm_head)
-        self.logits = logits
-        self.token_ids.copy_(argmax(logits[:, 0, :]).unsqueeze(-1))
+        if keep_logits:
+            rows = normalized.numel() // normalized.shape[-1]
+            logits = klinear.project(normalized.reshape(rows, -1), w.lm_head, klinear.BF16_OUT, 1)
+            self.logits = logits.view(self.batch, 1, -1)
+            self.token_ids.copy_(argmax(logits).unsqueeze(-1))
+        elif peers is not None and w.lm_head_local is not w.lm_head:
+            fused_argmax(normalized, w.lm_head_local, out=self.token_ids.view(-1), index_base=w.vocab_base,
+                         exchange=(comm.size, comm.rank, peers.exchange_ptrs, peers.exchange_local, self.position))
+        else:
+            fused_argmax(normalized, w.lm_head, out=self.token_ids.view(-1))
         self.position.add_(1)
 
     def capture(self, warmup=3):
@@ -319,7 +336,7 @@ def greedy(state, prompt, steps):
     logits = state.prefill(prompt)
     tokens, all_logits = [state.token_ids[:, 0].clone()], [logits.float()]
     for _ in range(steps - 1):
-        state.decode()
+        state.decode(keep_logits=True)
         tokens.append(state.token_ids[:, 0].clone())
         all_logits.append(state.logits[:, 0, :].float())
     return torch.stack(tokens, 1), torch.stack(all_logits, 1)

@@ -117,7 +117,9 @@ def step(args):
     import decode as fdecode
     import qwen3
     cfg = qwen3.Config.make(**qwen3.PRESETS[args.preset])
-    weights = qwen3.random_init(cfg, "cuda", seed=0)
+    # --tp-size N: one rank's shard shapes (rank 0 of N), run alone, for per-kernel times at TP N
+    # (the all-reduce consumers then run as the single-rank add+norm)
+    weights = qwen3.random_init(cfg, "cuda", seed=0, tp_rank=0, tp_size=args.tp_size)
     state = fdecode.DecodeState(weights, args.batch, args.length, 8)
     # decode cost does not depend on cache contents: random K/V instead of a prefill
     state.cache.store.normal_()
@@ -126,11 +128,30 @@ def step(args):
         state.decode()
         state.position.fill_(args.length)
     torch.cuda.synchronize()
+    if args.timed:
+        # the captured step, replayed (PDL chains intact), CUDA events around 20 replays
+        state.capture()
+        for _ in range(3):
+            state.position.fill_(args.length)
+            state.step()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(20):
+            state.position.fill_(args.length)
+            state.step()
+        end.record()
+        end.synchronize()
+        ms = start.elapsed_time(end) / 20
+        print(f"step {args.preset} TP-shard 1/{args.tp_size} B={args.batch} L={args.length}: {ms * 1e3:.1f} us per "
+              f"captured step ({args.batch / ms * 1e3:.0f} tok/s for this shard alone)")
+        state.release()
+        return
     torch.cuda.nvtx.range_push("profiled")
     state.decode()
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
-    print(f"step {args.preset} B={args.batch} L={args.length}: one eager decode step profiled")
+    print(f"step {args.preset} TP-shard 1/{args.tp_size} B={args.batch} L={args.length}: one eager decode step profiled")
 
 
 def main():
@@ -146,6 +167,8 @@ def main():
     parser.add_argument("--k", type=int, default=4096)
     parser.add_argument("--epilogue", type=int, default=3, help="0 bf16, 1 fp32, 2 SwiGLU, 3 split partials")
     parser.add_argument("--preset", default="qwen3-8b")
+    parser.add_argument("--tp-size", type=int, default=1)
+    parser.add_argument("--timed", action="store_true", help="step: time the captured step instead of profiling")
     parser.add_argument("--copies", type=int, default=2)
     parser.add_argument("--launches", type=int, default=2)
     args = parser.parse_args()

@@ -74,12 +74,24 @@ class Weights:
         self.kv_heads = cfg.num_key_value_heads // tp_size
         self.q_heads = cfg.num_attention_heads // tp_size
         self.intermediate = cfg.intermediate_size // tp_size
+        # Vocabulary-parallel LM head: this rank's rows of the (replicated) LM head matrix when
+        # the vocabulary splits into whole 8-row groups, else the whole matrix on every rank.
+        vocab = lm_head.shape[0]
+        if tp_size > 1 and vocab % (8 * tp_size) == 0:
+            rows = vocab // tp_size
+            self.vocab_base = tp_rank * rows
+            self.lm_head_local = lm_head[self.vocab_base:self.vocab_base + rows]
+        else:
+            self.vocab_base = 0
+            self.lm_head_local = lm_head
 
-    def nbytes_per_step(self):
-        """Weight bytes one decode step reads on this rank (every projection once, the LM head once)."""
+    def nbytes_per_step(self, vocab_parallel=True):
+        """Weight bytes one decode step reads on this rank: every projection once and the LM
+        head rows this rank projects (its vocabulary slice, or all of it)."""
         per_layer = sum(t.numel() for t in (self.layers[0].qkv, self.layers[0].o, self.layers[0].gate_up,
                                               self.layers[0].down)) * 2
-        return per_layer * len(self.layers) + self.lm_head.numel() * 2
+        head = self.lm_head_local if vocab_parallel else self.lm_head
+        return per_layer * len(self.layers) + head.numel() * 2
 
 
 BLOCK = 64

@@ -204,6 +204,28 @@ int fb_linear(const void* x, const void* w, void* out, int m, int n, int k, int 
               void* stream);
 
 /* ------------------------------------------------------------------------------------
+ * Greedy ids without materialized logits: replaces engine/kernels/argmax.py:73-129
+ * (`_fused_block_argmax` + `_first_best`, `fused_argmax`) and, in tensor parallelism, the
+ * vocabulary-parallel LM head the reference does not have (its argmax is single-GPU).
+ * fb_linear_argmax: x bf16 [M, K] (M <= 64) times W bf16 [N, K] (one K split, fp32
+ *   accumulation), every logit rounded to bf16 as the projection would store it; each
+ *   128-column tile writes its per-row (max, first index) to cand uint64 [M, ceil(N/128)] as
+ *   (index_base + column) << 32 | value bits (fb_argmax_candidates_bytes() bytes).
+ * fb_argmax_candidates: per row the largest value, ties to the lowest index (torch.argmax's
+ *   rule, argmax.py:1-9), into out int64 [rows] (and the winning value into top when not
+ *   NULL). With world > 1 each rank holds a vocabulary slice (index_base = its offset) and
+ *   the ranks exchange their bests through peer_exchange[r] = rank r's exchange buffer,
+ *   uint64 [rows, world, 2], with the flagged-word protocol of fb_linear_allreduce_push
+ *   (same epoch rule; bounded 2 s wait): every rank writes the same ids.
+ * ---------------------------------------------------------------------------------- */
+size_t fb_argmax_candidates_bytes(int m, int n);
+int fb_linear_argmax(const void* x, const void* w, int m, int n, int k, int64_t index_base, void* cand,
+                     void* stream);
+int fb_argmax_candidates(const void* cand, int rows, int tiles, int world, int rank,
+                         void* const* peer_exchange, const void* exchange_local, const int64_t* epoch,
+                         int64_t* out, float* top, void* stream);
+
+/* ------------------------------------------------------------------------------------
  * Tensor-parallel projection + all-reduce over NVLink peer memory (no counterpart in the
  * reference, which is single-GPU; this replaces an NCCL all-reduce after o_proj/down_proj).
  * Low-latency protocol: every value travels as one 8-byte word, low half the fp32 bits,

@@ -275,6 +275,33 @@ def test_argmax_matches_reference():
         assert torch.equal(top.cpu(), fx[case[0]]["top"])
 
 
+def test_fused_argmax_equals_projection_then_argmax():
+    """fb_linear_argmax + fb_argmax_candidates (logits never written) give torch.argmax of the
+    bf16 logits the one-split projection stores, ties to the lowest index, for ragged vocab
+    tails, planted ties, -inf rows and a vocabulary offset (engine/kernels/argmax.py:73-129)."""
+    from kernels import linear as klin
+    from kernels.argmax import fused_argmax, greedy_tokens
+    g = torch.Generator().manual_seed(11)
+    for rows, n, k in ((1, 151936, 1024), (16, 18992, 4096), (5, 1000, 256), (33, 4104, 512), (64, 136, 64)):
+        x = torch.randn(rows, k, generator=g).bfloat16().to(DEV)
+        w = (torch.randn(n, k, generator=g) * 0.05).bfloat16().to(DEV)
+        if n == 136:
+            w[7] = w[130]  # identical rows: identical logits, the lower index must win
+        logits = klin.project(x, w, klin.BF16_OUT, 1)
+        expect = torch.argmax(logits.float(), dim=-1)
+        got = fused_argmax(x, w)
+        assert torch.equal(got, expect), (rows, n, k)
+        assert torch.equal(fused_argmax(x, w, index_base=1000), expect + 1000)
+        assert torch.equal(greedy_tokens(x, w, klin.linear), expect)
+        ids, full = greedy_tokens(x, w, klin.linear, top=torch.zeros(rows, device=DEV))
+        assert full.shape == (rows, n)
+    # a row whose logits are all -inf picks index 0, as torch.argmax does
+    x = torch.zeros(2, 64, device=DEV).bfloat16()
+    x[1, 0] = float("-inf")
+    w = torch.ones(256, 64, device=DEV).bfloat16()
+    assert fused_argmax(x, w).tolist() == torch.argmax(klin.project(x, w, klin.BF16_OUT, 1).float(), -1).tolist()
+
+
 def test_decode_attention_fused_equals_two_launch_and_counters_reset():
     """fb_decode_attention (last CTA merges) equals fb_decode_attention_partials +
     fb_decode_attention_combine bit for bit, and leaves its per-pair counters at zero."""
