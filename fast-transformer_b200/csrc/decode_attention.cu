@@ -130,6 +130,165 @@ __device__ void merge_pair(const Params& p, int pair, int lo, int hi, long long 
   }
 }
 
+// One consumer warp's running state on one (row, KV head) pair: Q^T fragments, O^T
+// accumulators and the online-softmax max/denominator of its two head columns.
+template <int D>
+struct WarpAcc {
+  uint32_t qb[D / 16][2];
+  float o[D / 16][4];
+  float m0, m1, l0, l1;
+};
+
+// Loads query heads h*G..h*G+G-1 of row b as the B operand (heads past G read as zero) and
+// clears the running state.
+template <int D>
+__device__ __forceinline__ void start_pair(WarpAcc<D>& a, const Params& p, int b, int h, int lane) {
+  const int g = lane >> 2, c = lane & 3, G = p.groups;
+  const bool live = g < G;
+  const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
+      p.q + (static_cast<size_t>(b) * p.q_heads + h * G + (live ? g : 0)) * D);
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) {
+    a.qb[kk][0] = live ? __ldg(qrow + (kk * 16 + 2 * c) / 2) : 0u;
+    a.qb[kk][1] = live ? __ldg(qrow + (kk * 16 + 8 + 2 * c) / 2) : 0u;
+  }
+#pragma unroll
+  for (int i = 0; i < D / 16; ++i) a.o[i][0] = a.o[i][1] = a.o[i][2] = a.o[i][3] = 0.f;
+  a.m0 = a.m1 = -INFINITY;
+  a.l0 = a.l1 = 0.f;
+}
+
+// One 64-token K/V tile (128-byte swizzled, D/64 boxes of 64 columns) starting at token
+// tile_start of a row with `len` valid tokens: this warp's 16 tokens, S^T = K * Q^T, the
+// online softmax over tokens, and O^T += V^T * P^T with P rounded to bf16.
+template <int D>
+__device__ __forceinline__ void attend_tile(WarpAcc<D>& a, uint8_t* kt, uint8_t* vt, int tile_start, int len,
+                                            int warp, int lane, float sl2) {
+  constexpr int kBoxes = D / 64;
+  constexpr int kKSteps = D / 16;
+  const int g = lane >> 2;
+  const int slice = tile_start + warp * 16;  // first token of this warp's slice
+  if (slice >= len) return;
+  if (slice + 16 > len) {
+    // Ragged end: zero this warp's V rows at or past the valid length so that whatever the
+    // cache holds there (stale values, NaN) never meets a zero weight.
+    for (int e = lane; e < 16 * 8 * kBoxes; e += 32) {
+      const int r = e / (8 * kBoxes);
+      const int rest = e % (8 * kBoxes);
+      const int bx = rest / 8, ch = rest % 8;
+      if (slice + r >= len)
+        *reinterpret_cast<uint4*>(vt + bx * kTile * 128 + (warp * 16 + r) * 128 + ch * 16) = make_uint4(0, 0, 0, 0);
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+  }
+  // ---- S^T = K * Q^T for this warp's 16 tokens ----
+  float sc[4] = {0.f, 0.f, 0.f, 0.f};
+  const uint32_t krow = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+  for (int kk = 0; kk < kKSteps; ++kk) {
+    const int chunk = (kk & 3) * 2 + (lane >> 4);
+    const uint32_t addr = smem_u32(kt + (kk >> 2) * kTile * 128) + sw128(krow, chunk);
+    uint32_t a0, a1, a2, a3;
+    ldmatrix_x4(addr, a0, a1, a2, a3);
+    mma_bf16_16816(sc, a0, a1, a2, a3, a.qb[kk][0], a.qb[kk][1]);
+  }
+  // ---- online softmax over tokens (rows g, g+8), heads (2c, 2c+1) ----
+  const int tok0 = slice + g, tok1 = slice + g + 8;
+  float s0 = tok0 < len ? sc[0] * sl2 : -INFINITY;
+  float s1 = tok0 < len ? sc[1] * sl2 : -INFINITY;
+  float s2 = tok1 < len ? sc[2] * sl2 : -INFINITY;
+  float s3 = tok1 < len ? sc[3] * sl2 : -INFINITY;
+  float mx0 = fmaxf(s0, s2), mx1 = fmaxf(s1, s3);
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+  }
+  const float n0 = fmaxf(a.m0, mx0), n1 = fmaxf(a.m1, mx1);
+  const float pv0 = n0 == -INFINITY ? 0.f : n0;  // never form -inf - -inf
+  const float pv1 = n1 == -INFINITY ? 0.f : n1;
+  const float corr0 = exp2f(a.m0 - pv0), corr1 = exp2f(a.m1 - pv1);
+  const float p0 = exp2f(s0 - pv0), p1 = exp2f(s1 - pv1);
+  const float p2 = exp2f(s2 - pv0), p3 = exp2f(s3 - pv1);
+  a.l0 = a.l0 * corr0 + (p0 + p2);
+  a.l1 = a.l1 * corr1 + (p1 + p3);
+  a.m0 = n0;
+  a.m1 = n1;
+#pragma unroll
+  for (int i = 0; i < kKSteps; ++i) {
+    a.o[i][0] *= corr0;
+    a.o[i][1] *= corr1;
+    a.o[i][2] *= corr0;
+    a.o[i][3] *= corr1;
+  }
+  // P^T fragments (bf16, as the reference's P cast) -> B operand of the PV product.
+  const uint32_t pb0 = movmatrix_trans(pack_bf16x2(p0, p1));
+  const uint32_t pb1 = movmatrix_trans(pack_bf16x2(p2, p3));
+  // ---- O^T += V^T * P^T ----
+  const uint32_t vrow = warp * 16 + (lane & 7) + ((lane >> 4) & 1) * 8;
+#pragma unroll
+  for (int i = 0; i < kKSteps; ++i) {
+    const int cg = 2 * i + ((lane >> 3) & 1);
+    const uint32_t addr = smem_u32(vt + (cg >> 3) * kTile * 128) + sw128(vrow, cg & 7);
+    uint32_t a0, a1, a2, a3;
+    ldmatrix_x4_trans(addr, a0, a1, a2, a3);
+    mma_bf16_16816(a.o[i], a0, a1, a2, a3, pb0, pb1);
+  }
+}
+
+// Parks this warp's state in shared memory for the cross-warp reduction: per-head (max,
+// denominator) pairs in red_ml[warp][head] and O^T columns in red_o[warp][d][head].
+template <int D>
+__device__ __forceinline__ void park_warp(WarpAcc<D>& a, float* red_o, float* red_ml, int warp, int lane, int G) {
+  const int g = lane >> 2, c = lane & 3;
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    a.l0 += __shfl_xor_sync(0xffffffffu, a.l0, off);
+    a.l1 += __shfl_xor_sync(0xffffffffu, a.l1, off);
+  }
+  if (g == 0) {
+    red_ml[(warp * kHeadsPad + 2 * c) * 2 + 0] = a.m0;
+    red_ml[(warp * kHeadsPad + 2 * c) * 2 + 1] = a.l0;
+    red_ml[(warp * kHeadsPad + 2 * c + 1) * 2 + 0] = a.m1;
+    red_ml[(warp * kHeadsPad + 2 * c + 1) * 2 + 1] = a.l1;
+  }
+  if (2 * c < G) {
+#pragma unroll
+    for (int i = 0; i < D / 16; ++i) {
+      float* r0 = red_o + ((warp * D) + 16 * i + g) * kHeadsPad + 2 * c;
+      float* r1 = red_o + ((warp * D) + 16 * i + g + 8) * kHeadsPad + 2 * c;
+      r0[0] = a.o[i][0];
+      r0[1] = a.o[i][1];
+      r1[0] = a.o[i][2];
+      r1[1] = a.o[i][3];
+    }
+  }
+}
+
+// The CTA's combined state for element e = (head gq, dim d) from the parked warp states:
+// M = max_w m_w, L = sum_w l_w 2^(m_w - M), O = sum_w o_w 2^(m_w - M), warps in order.
+template <int D>
+__device__ __forceinline__ void combine_warps(const float* red_o, const float* red_ml, int gq, int d, float& M,
+                                              float& L, float& O) {
+  float mw[kConsumerWarps];
+  M = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < kConsumerWarps; ++w) {
+    mw[w] = red_ml[(w * kHeadsPad + gq) * 2];
+    M = fmaxf(M, mw[w]);
+  }
+  const float piv = M == -INFINITY ? 0.f : M;
+  L = 0.f;
+  O = 0.f;
+#pragma unroll
+  for (int w = 0; w < kConsumerWarps; ++w) {
+    const float f = exp2f(mw[w] - piv);
+    L += red_ml[(w * kHeadsPad + gq) * 2 + 1] * f;
+    O += red_o[((w * D) + d) * kHeadsPad + gq] * f;
+  }
+}
+
 template <int D, int NS>
 struct Smem {
   static constexpr int kBoxes = D / 64;
@@ -153,7 +312,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                            const __grid_constant__ CUtensorMap vmap, const Params p) {
   using S = Smem<D, NS>;
   constexpr int kBoxes = S::kBoxes;
-  constexpr int kKSteps = D / 16;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -291,8 +449,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   // ========================== consumers: warps 0..3 ==========================
   pdl_wait();  // the query rows come from the previous kernel
   pdl_trigger();
-  const int g = lane >> 2;  // fragment row group
-  const int c = lane & 3;   // fragment column pair
   const int ctid = threadIdx.x;  // 0..127
 
   int b = misc[0], h = misc[1], j = misc[2];
@@ -300,25 +456,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   int len = row_length(p.position, p.per_row, b, p.capacity);
   int run_first = j;
 
-  uint32_t qb[kKSteps][2];
-  float o[kKSteps][4];
-  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-
-  auto load_q = [&](int bb, int hh) {
-    const bool live = g < G;
-    const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
-        p.q + (static_cast<size_t>(bb) * p.q_heads + hh * G + (live ? g : 0)) * D);
-#pragma unroll
-    for (int kk = 0; kk < kKSteps; ++kk) {
-      qb[kk][0] = live ? __ldg(qrow + (kk * 16 + 2 * c) / 2) : 0u;
-      qb[kk][1] = live ? __ldg(qrow + (kk * 16 + 8 + 2 * c) / 2) : 0u;
-    }
-#pragma unroll
-    for (int i = 0; i < kKSteps; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-    m0 = m1 = -INFINITY;
-    l0 = l1 = 0.f;
-  };
-  load_q(b, h);
+  WarpAcc<D> acc;
+  start_pair<D>(acc, p, b, h, lane);
 
   const float sl2 = p.scale_log2;
   bool aborted = false;
@@ -335,78 +474,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       break;
     }
     uint8_t* kt = stages + s * S::kStageBytes;
-    uint8_t* vt = kt + S::kTileBytes;
-    const int tile_start = j * kTile;
-    const int slice = tile_start + warp * 16;  // first token of this warp's slice
-    if (slice < len) {
-      if (slice + 16 > len) {
-        // Ragged end: zero this warp's V rows at or past the valid length so that
-        // whatever the cache holds there (stale values, NaN) never meets a zero weight.
-        for (int e = lane; e < 16 * 8 * kBoxes; e += 32) {
-          const int r = e / (8 * kBoxes);
-          const int rest = e % (8 * kBoxes);
-          const int bx = rest / 8, ch = rest % 8;
-          if (slice + r >= len)
-            *reinterpret_cast<uint4*>(vt + bx * kTile * 128 + (warp * 16 + r) * 128 + ch * 16) =
-                make_uint4(0, 0, 0, 0);
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-      }
-      // ---- S^T = K * Q^T for this warp's 16 tokens ----
-      float sc[4] = {0.f, 0.f, 0.f, 0.f};
-      const uint32_t krow = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-#pragma unroll
-      for (int kk = 0; kk < kKSteps; ++kk) {
-        const int chunk = (kk & 3) * 2 + (lane >> 4);
-        const uint32_t addr = smem_u32(kt + (kk >> 2) * kTile * 128) + sw128(krow, chunk);
-        uint32_t a0, a1, a2, a3;
-        ldmatrix_x4(addr, a0, a1, a2, a3);
-        mma_bf16_16816(sc, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
-      }
-      // ---- online softmax over tokens (rows g, g+8), heads (2c, 2c+1) ----
-      const int tok0 = slice + g, tok1 = slice + g + 8;
-      float s0 = tok0 < len ? sc[0] * sl2 : -INFINITY;
-      float s1 = tok0 < len ? sc[1] * sl2 : -INFINITY;
-      float s2 = tok1 < len ? sc[2] * sl2 : -INFINITY;
-      float s3 = tok1 < len ? sc[3] * sl2 : -INFINITY;
-      float mx0 = fmaxf(s0, s2), mx1 = fmaxf(s1, s3);
-#pragma unroll
-      for (int off = 4; off < 32; off <<= 1) {
-        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
-      }
-      const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
-      const float pv0 = n0 == -INFINITY ? 0.f : n0;  // never form -inf - -inf
-      const float pv1 = n1 == -INFINITY ? 0.f : n1;
-      const float corr0 = exp2f(m0 - pv0), corr1 = exp2f(m1 - pv1);
-      const float p0 = exp2f(s0 - pv0), p1 = exp2f(s1 - pv1);
-      const float p2 = exp2f(s2 - pv0), p3 = exp2f(s3 - pv1);
-      l0 = l0 * corr0 + (p0 + p2);
-      l1 = l1 * corr1 + (p1 + p3);
-      m0 = n0;
-      m1 = n1;
-#pragma unroll
-      for (int i = 0; i < kKSteps; ++i) {
-        o[i][0] *= corr0;
-        o[i][1] *= corr1;
-        o[i][2] *= corr0;
-        o[i][3] *= corr1;
-      }
-      // P^T fragments (bf16, as the reference's P cast) -> B operand of the PV product.
-      const uint32_t pb0 = movmatrix_trans(pack_bf16x2(p0, p1));
-      const uint32_t pb1 = movmatrix_trans(pack_bf16x2(p2, p3));
-      // ---- O^T += V^T * P^T ----
-      const uint32_t vrow = warp * 16 + (lane & 7) + ((lane >> 4) & 1) * 8;
-#pragma unroll
-      for (int i = 0; i < kKSteps; ++i) {
-        const int cg = 2 * i + ((lane >> 3) & 1);
-        const uint32_t addr = smem_u32(vt + (cg >> 3) * kTile * 128) + sw128(vrow, cg & 7);
-        uint32_t a0, a1, a2, a3;
-        ldmatrix_x4_trans(addr, a0, a1, a2, a3);
-        mma_bf16_16816(o[i], a0, a1, a2, a3, pb0, pb1);
-      }
-    }
+    attend_tile<D>(acc, kt, kt + S::kTileBytes, j * kTile, len, warp, lane, sl2);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
 
@@ -424,49 +492,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if (run_end) {
-      // Per-warp denominators: reduce the per-thread partial sums over the 8 rows.
-#pragma unroll
-      for (int off = 4; off < 32; off <<= 1) {
-        l0 += __shfl_xor_sync(0xffffffffu, l0, off);
-        l1 += __shfl_xor_sync(0xffffffffu, l1, off);
-      }
-      if (g == 0) {
-        red_ml[(warp * kHeadsPad + 2 * c) * 2 + 0] = m0;
-        red_ml[(warp * kHeadsPad + 2 * c) * 2 + 1] = l0;
-        red_ml[(warp * kHeadsPad + 2 * c + 1) * 2 + 0] = m1;
-        red_ml[(warp * kHeadsPad + 2 * c + 1) * 2 + 1] = l1;
-      }
-      if (2 * c < G) {
-#pragma unroll
-        for (int i = 0; i < kKSteps; ++i) {
-          float* r0 = red_o + ((warp * D) + 16 * i + g) * kHeadsPad + 2 * c;
-          float* r1 = red_o + ((warp * D) + 16 * i + g + 8) * kHeadsPad + 2 * c;
-          r0[0] = o[i][0];
-          r0[1] = o[i][1];
-          r1[0] = o[i][2];
-          r1[1] = o[i][3];
-        }
-      }
+      park_warp<D>(acc, red_o, red_ml, warp, lane, G);
       asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
       const bool whole = cur_first == 0 && cur_last == cur_n - 1;
       const int pair = cur_b * Hkv + cur_h;
       const int slot = blockIdx.x + pair;
       for (int e = ctid; e < G * D; e += kConsumerWarps * 32) {
         const int gq = e / D, d = e % D;
-        float mw[kConsumerWarps], M = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) {
-          mw[w] = red_ml[(w * kHeadsPad + gq) * 2];
-          M = fmaxf(M, mw[w]);
-        }
-        const float piv = M == -INFINITY ? 0.f : M;
-        float L = 0.f, O = 0.f;
-#pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) {
-          const float f = exp2f(mw[w] - piv);
-          L += red_ml[(w * kHeadsPad + gq) * 2 + 1] * f;
-          O += red_o[((w * D) + d) * kHeadsPad + gq] * f;
-        }
+        float M, L, O;
+        combine_warps<D>(red_o, red_ml, gq, d, M, L, O);
         if (whole) {
           p.out[(static_cast<size_t>(cur_b) * p.q_heads + cur_h * G + gq) * D + d] =
               __float2bfloat16_rn(O / L);
@@ -508,7 +542,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         n = cum[b + 1] - cum[b];
         len = row_length(p.position, p.per_row, b, p.capacity);
         run_first = j;
-        load_q(b, h);
+        start_pair<D>(acc, p, b, h, lane);
       }
     }
   }
@@ -564,7 +598,277 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const P
   merge_pair<D>(p, pair, lo, hi, T, threadIdx.x, kCombineThreads, s_w, s_den, [] { __syncthreads(); });
 }
 
+
+// ---------------------------------------------------------------------------------------
+// Cluster form, for a position shared by every row and few (row, KV head) pairs (tensor-
+// parallel shards, small batches): one thread-block cluster of C <= 8 CTAs per pair. CTA r
+// streams tiles [r*n/C, (r+1)*n/C) of the pair with the same per-tile arithmetic as the
+// persistent kernel, keeps its combined (max, denominator, O) in shared memory, and after one
+// cluster barrier every CTA merges its share of the pair's G*D outputs over the C partials
+// through distributed shared memory, in rank order: no global partials, fences, counters or
+// second pass.
+// ---------------------------------------------------------------------------------------
+constexpr int kMaxCluster = 8;
+
+template <int D, int NS>
+struct ClusterSmem {
+  static constexpr int kBoxes = D / 64;
+  static constexpr int kTileBytes = kBoxes * kTile * 128;
+  static constexpr int kStageBytes = 2 * kTileBytes;
+  static constexpr int kStagesBytes = NS * kStageBytes;
+  // the warps' O^T partials reuse the drained stage ring
+  static constexpr int kRedO = kConsumerWarps * D * kHeadsPad * 4;
+  static_assert(kRedO <= kStagesBytes, "the warp partials must fit the stage ring");
+  static constexpr int kRedML = kConsumerWarps * kHeadsPad * 2 * 4;
+  static constexpr int kPartO = kHeadsPad * D * 4;  // this CTA's O per (head, dim)
+  static constexpr int kPartML = kHeadsPad * 2 * 4;  // (max, denominator) per head
+  static constexpr int kWeights = kMaxCluster * kHeadsPad * 4 + kHeadsPad * 4;
+  static constexpr int kBars = 2 * NS * 8;
+  static constexpr int kTotal = 1024 + kStagesBytes + kRedML + kPartO + kPartML + kWeights + kBars + 16;
+  static_assert((kStagesBytes + kRedML + kPartO + kPartML + kWeights) % 16 == 0, "mbarrier alignment");
+};
+
+template <int D, int NS>
+__global__ void __launch_bounds__(kThreads, 1)
+    decode_cluster_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                          const Params p) {
+  using S = ClusterSmem<D, NS>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stages = base;
+  float* red_o = reinterpret_cast<float*>(base);  // used once the ring has drained
+  float* red_ml = reinterpret_cast<float*>(base + S::kStagesBytes);
+  float* part_o = red_ml + S::kRedML / 4;
+  float* part_ml = part_o + S::kPartO / 4;
+  float* wts = part_ml + S::kPartML / 4;  // [rank][head] merge weights
+  float* den = wts + kMaxCluster * kHeadsPad;
+  uint64_t* full = reinterpret_cast<uint64_t*>(den + kHeadsPad);
+  uint64_t* empty = full + NS;
+  int* abort_word = reinterpret_cast<int*>(empty + NS);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int C = gridDim.x;
+  const int rank = blockIdx.x;  // cluster dims (C, 1, 1): the CTA's rank in its cluster
+  const int pair = blockIdx.y;
+  const int Hkv = p.kv_heads, G = p.groups;
+  const int b = pair / Hkv, h = pair % Hkv;
+  // the shared position was written before this step: read before the dependency wait
+  const int len = row_length(p.position, 0, b, p.capacity);
+  const int n = tiles_of(len);
+  const int t0 = static_cast<int>(static_cast<long long>(n) * rank / C);
+  const int count = static_cast<int>(static_cast<long long>(n) * (rank + 1) / C) - t0;
+
+  if (warp == kConsumerWarps && lane == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    fence_barrier_init();
+    prefetch_tensormap(&kmap);
+    prefetch_tensormap(&vmap);
+    *abort_word = 0;
+  }
+  __syncthreads();
+  volatile int* abort_flag = abort_word;
+
+  if (warp == kConsumerWarps) {
+    // ===================== producer: one lane issues every TMA =====================
+    if (lane == 0) {
+      // Cache rows below the position were written by earlier steps: the ring is filled
+      // before the dependency wait; the row's last tile (the previous kernel appends its
+      // newest slot) waits for the previous kernel.
+      bool waited = false;
+      for (int k = 0; k < count; ++k) {
+        const int s = k % NS;
+        const int j = t0 + k;
+        if (!waited && (k >= NS || j == n - 1)) {
+          pdl_wait();
+          waited = true;
+        }
+        if (*abort_flag) break;
+        if (k >= NS && !mbar_wait_bounded(&empty[s], ((k / NS) - 1) & 1)) {
+          raise_error(p.err, kErrTimeoutEmpty);
+          *abort_flag = 1;
+          break;
+        }
+        uint8_t* kt = stages + s * S::kStageBytes;
+        uint8_t* vt = kt + S::kTileBytes;
+        const int row = (b * Hkv + h) * p.capacity + j * kTile;
+        mbar_arrive_expect_tx(&full[s], S::kStageBytes);
+#pragma unroll
+        for (int bx = 0; bx < S::kBoxes; ++bx) {
+          tma_load_2d(kt + bx * kTile * 128, &kmap, &full[s], bx * 64, row);
+          tma_load_2d(vt + bx * kTile * 128, &vmap, &full[s], bx * 64, row);
+        }
+      }
+    }
+    __syncwarp();
+    // every thread of every CTA in the cluster takes the same two cluster barriers
+    cluster_sync();
+    cluster_sync();
+    return;
+  }
+
+  // ========================== consumers: warps 0..3 ==========================
+  pdl_wait();  // the query rows come from the previous kernel
+  pdl_trigger();
+  const int ctid = threadIdx.x;  // 0..127
+  WarpAcc<D> acc;
+  start_pair<D>(acc, p, b, h, lane);
+  bool aborted = false;
+  for (int k = 0; k < count; ++k) {
+    const int s = k % NS;
+    if (!mbar_wait_bounded(&full[s], (k / NS) & 1)) {
+      raise_error(p.err, kErrTimeoutFull);
+      *abort_flag = 1;
+      aborted = true;
+    }
+    if (aborted || *abort_flag) {
+      aborted = true;  // still takes the cluster barriers below
+      break;
+    }
+    uint8_t* kt = stages + s * S::kStageBytes;
+    attend_tile<D>(acc, kt, kt + S::kTileBytes, (t0 + k) * kTile, len, warp, lane, p.scale_log2);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+  // this CTA's partial: (M, L) per head, O per (head, dim); an empty slice gives (-inf, 0, 0).
+  // Every warp is done with the stage ring (red_o overlays it) and no copy is in flight: the
+  // producer issued exactly `count` tiles and each was consumed, or the loop aborted.
+  asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+  park_warp<D>(acc, red_o, red_ml, warp, lane, G);
+  asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+  for (int e = ctid; e < G * D; e += kConsumerWarps * 32) {
+    const int gq = e / D, d = e % D;
+    float M, L, O;
+    combine_warps<D>(red_o, red_ml, gq, d, M, L, O);
+    part_o[e] = O;
+    if (d == 0) {
+      part_ml[gq * 2] = M;
+      part_ml[gq * 2 + 1] = L;
+    }
+  }
+  cluster_sync();  // every CTA's partial is complete and visible cluster-wide
+  if (ctid < G) {
+    const int gq = ctid;
+    float mq[kMaxCluster], lq[kMaxCluster];
+    float M = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < kMaxCluster; ++q)
+      if (q < C) {
+        mq[q] = ld_cluster_f32(map_shared(smem_u32(&part_ml[gq * 2]), q));
+        lq[q] = ld_cluster_f32(map_shared(smem_u32(&part_ml[gq * 2 + 1]), q));
+      }
+#pragma unroll
+    for (int q = 0; q < kMaxCluster; ++q)
+      if (q < C) M = fmaxf(M, mq[q]);
+    const float piv = M == -INFINITY ? 0.f : M;
+    float L = 0.f;
+#pragma unroll
+    for (int q = 0; q < kMaxCluster; ++q)
+      if (q < C) {
+        const float w = exp2f(mq[q] - piv);
+        L += lq[q] * w;
+        wts[q * kHeadsPad + gq] = w;
+      }
+    den[gq] = L;
+  }
+  asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+  // this CTA's share of the pair's G*D outputs, summed over the cluster in rank order
+  const int total = G * D, chunk = (total + C - 1) / C;
+  const int e0 = rank * chunk, e1 = min(total, e0 + chunk);
+  __nv_bfloat16* out = p.out + (static_cast<size_t>(b) * p.q_heads + h * G) * D;
+  for (int e = e0 + ctid; e < e1; e += kConsumerWarps * 32) {
+    const int gq = e / D;
+    float part[kMaxCluster];
+#pragma unroll
+    for (int q = 0; q < kMaxCluster; ++q)
+      if (q < C) part[q] = ld_cluster_f32(map_shared(smem_u32(&part_o[e]), q));
+    float O = 0.f;
+#pragma unroll
+    for (int q = 0; q < kMaxCluster; ++q)
+      if (q < C) O += part[q] * wts[q * kHeadsPad + gq];
+    const float L = den[gq];
+    out[e] = __float2bfloat16_rn(L > 0.f ? O / L : 0.f);  // a row with no valid slot writes zeros
+  }
+  cluster_sync();  // no CTA leaves while another may still read its partial
+}
+
 constexpr int kStages = 4;
+constexpr int kClusterStages = 2;  // the cluster form's small ring: three CTAs per SM
+
+template <int D, int NS>
+bool configure_cluster() {
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !configured[dev]) {
+    if (cudaFuncSetAttribute(decode_cluster_kernel<D, NS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             ClusterSmem<D, NS>::kTotal) != cudaSuccess)
+      return false;
+    configured[dev] = true;
+  }
+  return true;
+}
+
+// Clusters of `c` CTAs of the cluster kernel that the device holds at once (-1 if unknown),
+// cached per (device, head dim, stages, c).
+template <int D, int NS>
+int resident_clusters(int c) {
+  static int cache[64][kMaxCluster + 1] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && cache[dev][c] != 0) return cache[dev][c];
+  if (!configure_cluster<D, NS>()) return -1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(c, 1);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = ClusterSmem<D, NS>::kTotal;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = c;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, decode_cluster_kernel<D, NS>, &cfg) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    n = -1;  // unknown: never chosen
+  }
+  if (dev < 64) cache[dev][c] = n;
+  return n;
+}
+
+// The largest cluster size in {8, 4, 2} whose `pairs` clusters are all resident at once, or 0.
+template <int D, int NS>
+int cluster_size(int pairs) {
+  for (int c = kMaxCluster; c >= 2; c /= 2)
+    if (resident_clusters<D, NS>(c) >= pairs) return c;
+  return 0;
+}
+
+template <int D, int NS>
+int launch_cluster(const CUtensorMap& km, const CUtensorMap& vm, const Params& p, int cluster, cudaStream_t stream) {
+  if (!configure_cluster<D, NS>()) return FB_ERR_LAUNCH;
+  return launch_ex(decode_cluster_kernel<D, NS>, dim3(cluster, p.batch * p.kv_heads), dim3(kThreads),
+                   ClusterSmem<D, NS>::kTotal, stream, cluster, km, vm, p);
+}
+
+// Cluster form choice (measured on B200, 16 rows x 8193 tokens): the 4-stage ring (one CTA
+// per SM) while its clusters cover about two thirds of the SMs or more (32 pairs: 4 x 32
+// CTAs, 24.8 us against 26.7 us with 2 stages; 64 pairs: 2 x 64, 42.8 against 44.9); below
+// that the 2-stage ring (three CTAs per SM) fits larger clusters (16 pairs: 8 x 16 CTAs,
+// 19.2 us against 20.9 us for 4 x 16). Returns FB_ERR_SHAPE when neither fits in one wave.
+template <int D>
+int launch_cluster_form(const CUtensorMap& km, const CUtensorMap& vm, const Params& p, int pairs, cudaStream_t s) {
+  const int c4 = cluster_size<D, kStages>(pairs);
+  if (c4 >= 2 && 3 * pairs * c4 >= 2 * sm_count()) return launch_cluster<D, kStages>(km, vm, p, c4, s);
+  const int c2 = cluster_size<D, kClusterStages>(pairs);
+  if (c2 > c4) return launch_cluster<D, kClusterStages>(km, vm, p, c2, s);
+  if (c4 >= 2) return launch_cluster<D, kStages>(km, vm, p, c4, s);
+  return FB_ERR_SHAPE;
+}
 
 template <int D>
 int launch_partials(const CUtensorMap& km, const CUtensorMap& vm, const Params& p,
@@ -665,6 +969,13 @@ static int launch_decode(const void* q, const void* k, const void* v, const int6
   st = encode_bf16_2d(&vm, v, rows, head_dim, head_dim, 64, kTile, true);
   if (st != FB_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // A shared position and few pairs: one cluster per pair, merged through DSMEM, when the
+  // clusters all fit in one wave.
+  const int pairs = batch * kv_heads;
+  if (fused && !per_row && 2 * pairs <= sm_count()) {
+    st = head_dim == 128 ? launch_cluster_form<128>(km, vm, p, pairs, s) : launch_cluster_form<64>(km, vm, p, pairs, s);
+    if (st != FB_ERR_SHAPE) return st;
+  }
   return head_dim == 128 ? launch_partials<128>(km, vm, p, s) : launch_partials<64>(km, vm, p, s);
 }
 

@@ -268,26 +268,67 @@ __global__ void __launch_bounds__(kMaxThreads) rmsnorm_kernel(const Params p) {
   if (C > 1) cluster_sync();  // no CTA leaves while another may still read its sum
 }
 
-__global__ void __launch_bounds__(kThreads)
-    swiglu_kernel(const void* packed, int splits, __nv_bfloat16* out, int rows, int width) {
+constexpr int kSwigluThreads = 128;
+
+// Four output features per thread: the gate and up values of every split slab are loaded
+// together (up to 8 slabs in flight for each), summed in split order and rounded to bf16,
+// then bf16(bf16(silu(g)) * u) (engine/kernels/swiglu.py:13-24).
+__global__ void __launch_bounds__(kSwigluThreads)
+    swiglu_kernel(const void* packed, int splits, __nv_bfloat16* out, int rows, int width, int blocked) {
   pdl_wait();
   pdl_trigger();
-  const int64_t flat = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
-  const int per_row = width / 8;
+  const int64_t flat = static_cast<int64_t>(blockIdx.x) * kSwigluThreads + threadIdx.x;
+  const int per_row = width / 4;
   if (flat >= static_cast<int64_t>(rows) * per_row) return;
   const int row = static_cast<int>(flat / per_row);
-  const int ch = static_cast<int>(flat % per_row);
-  const size_t count = static_cast<size_t>(rows) * 2 * width;
-  const size_t base = static_cast<size_t>(row) * 2 * width + ch * 8;
-  float g[8], u[8], y[8];
-  load8(packed, splits, count, base, g);
-  load8(packed, splits, count, base + width, u);
+  const int f = static_cast<int>(flat % per_row) * 4;
+  // [gate | up] halves, or 64-column gate/up blocks interleaved (features 64i..64i+63 in
+  // columns 128i.. and their up halves in 128i+64..)
+  const size_t gate_col = blocked ? static_cast<size_t>(f / 64) * 128 + f % 64 : f;
+  const size_t up_col = blocked ? gate_col + 64 : static_cast<size_t>(f) + width;
+  const size_t base = static_cast<size_t>(row) * 2 * width;
+  float g[4], u[4];
+  if (splits == 0) {
+    const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(packed) + base;
+    const uint2 gw = *reinterpret_cast<const uint2*>(src + gate_col);
+    const uint2 uw = *reinterpret_cast<const uint2*>(src + up_col);
+    g[0] = bf16_lo(gw.x), g[1] = bf16_hi(gw.x), g[2] = bf16_lo(gw.y), g[3] = bf16_hi(gw.y);
+    u[0] = bf16_lo(uw.x), u[1] = bf16_hi(uw.x), u[2] = bf16_lo(uw.y), u[3] = bf16_hi(uw.y);
+  } else {
+    const float* src = static_cast<const float*>(packed) + base;
+    const size_t slab = static_cast<size_t>(rows) * 2 * width;
+    for (int s0 = 0; s0 < splits; s0 += kSlabBatch) {
+      float4 gs[kSlabBatch], us[kSlabBatch];
 #pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    const float act = bf16_round(g[e] / (1.0f + expf(-g[e])));
-    y[e] = act * u[e];
+      for (int j = 0; j < kSlabBatch; ++j)
+        if (s0 + j < splits) {
+          gs[j] = __ldcg(reinterpret_cast<const float4*>(src + (s0 + j) * slab + gate_col));
+          us[j] = __ldcg(reinterpret_cast<const float4*>(src + (s0 + j) * slab + up_col));
+        }
+#pragma unroll
+      for (int j = 0; j < kSlabBatch; ++j) {
+        if (s0 + j == 0) {
+          g[0] = gs[0].x, g[1] = gs[0].y, g[2] = gs[0].z, g[3] = gs[0].w;
+          u[0] = us[0].x, u[1] = us[0].y, u[2] = us[0].z, u[3] = us[0].w;
+        } else if (s0 + j < splits) {
+          g[0] += gs[j].x, g[1] += gs[j].y, g[2] += gs[j].z, g[3] += gs[j].w;
+          u[0] += us[j].x, u[1] += us[j].y, u[2] += us[j].z, u[3] += us[j].w;
+        }
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      g[e] = bf16_round(g[e]);
+      u[e] = bf16_round(u[e]);
+    }
   }
-  store8(out + static_cast<size_t>(row) * width + ch * 8, y);
+  float y[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) y[e] = bf16_round(g[e] / (1.0f + expf(-g[e]))) * u[e];
+  uint2 w;
+  w.x = pack_bf16x2(y[0], y[1]);
+  w.y = pack_bf16x2(y[2], y[3]);
+  *reinterpret_cast<uint2*>(out + static_cast<size_t>(row) * width + f) = w;
 }
 
 __global__ void __launch_bounds__(kThreads)
@@ -423,12 +464,23 @@ extern "C" int fb_swiglu(const void* packed, int splits, void* out, int rows, in
                          void* stream) {
   if (!packed || !out || rows <= 0 || splits < 0 || width <= 0) return FB_ERR_ARG;
   if (width % 8 != 0) return FB_ERR_SHAPE;
-  const int64_t threads = static_cast<int64_t>(rows) * (width / 8);
-  const int64_t blocks = (threads + norm::kThreads - 1) / norm::kThreads;
+  const int64_t threads = static_cast<int64_t>(rows) * (width / 4);
+  const int64_t blocks = (threads + norm::kSwigluThreads - 1) / norm::kSwigluThreads;
   if (blocks >= (1ll << 31)) return FB_ERR_SHAPE;
-  return launch_ex(norm::swiglu_kernel, dim3(static_cast<unsigned>(blocks)), dim3(norm::kThreads), 0,
+  return launch_ex(norm::swiglu_kernel, dim3(static_cast<unsigned>(blocks)), dim3(norm::kSwigluThreads), 0,
                    static_cast<cudaStream_t>(stream), 1, packed, splits, static_cast<__nv_bfloat16*>(out), rows,
-                   width);
+                   width, 0);
+}
+
+extern "C" int fb_swiglu_blocked(const void* packed, int splits, void* out, int rows, int width, void* stream) {
+  if (!packed || !out || rows <= 0 || splits < 0 || width <= 0) return FB_ERR_ARG;
+  if (width % 64 != 0) return FB_ERR_SHAPE;
+  const int64_t threads = static_cast<int64_t>(rows) * (width / 4);
+  const int64_t blocks = (threads + norm::kSwigluThreads - 1) / norm::kSwigluThreads;
+  if (blocks >= (1ll << 31)) return FB_ERR_SHAPE;
+  return launch_ex(norm::swiglu_kernel, dim3(static_cast<unsigned>(blocks)), dim3(norm::kSwigluThreads), 0,
+                   static_cast<cudaStream_t>(stream), 1, packed, splits, static_cast<__nv_bfloat16*>(out), rows,
+                   width, 1);
 }
 
 extern "C" int fb_merge_splits(const void* partial, int splits, int64_t count, void* out,

@@ -177,6 +177,10 @@ int fb_embed_rmsnorm(const int64_t* ids, const void* table, int64_t vocab, const
  *   out    bf16 [rows, I]; I % 8 == 0.
  * ---------------------------------------------------------------------------------- */
 int fb_swiglu(const void* packed, int splits, void* out, int rows, int width, void* stream);
+/* The same on the 64-column blocked layout of fb_linear's SwiGLU weights (block 2i = gate
+ * features 64i..64i+63, block 2i+1 = their up features): the split-K companion of epilogue 2
+ * (no counterpart in the reference, whose gate/up halves are contiguous). I % 64 == 0. */
+int fb_swiglu_blocked(const void* packed, int splits, void* out, int rows, int width, void* stream);
 
 /* ------------------------------------------------------------------------------------
  * Skinny bf16 projection y = x @ W^T with fp32 accumulation and one rounding.

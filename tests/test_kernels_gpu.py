@@ -113,6 +113,34 @@ def test_decode_attention_long_and_tiny_lengths():
                                    atol=2e-2, rtol=2e-2)
 
 
+@pytest.mark.parametrize("batch,q_heads,kv_heads,dim,length", [
+    (16, 4, 1, 128, 8193),    # a TP8 shard of config 4: clusters of 8
+    (16, 8, 2, 128, 4000),    # TP4: clusters of 4
+    (2, 8, 2, 64, 100),       # 2 tiles over 8 ranks: empty slices
+    (3, 32, 8, 128, 1),       # one valid slot
+    (4, 16, 1, 128, 65),      # G = 16 is not served (G <= 8): skipped below
+    (1, 8, 1, 128, 30000),
+])
+def test_decode_attention_cluster_form(batch, q_heads, kv_heads, dim, length):
+    """A shared position over few (row, KV head) pairs takes the cluster form (per-pair DSMEM
+    merge): it must match the fp32 reference like the persistent form, which the same lengths
+    given per row still take, and ignore NaN past the valid length."""
+    from kernels.decode_attention import decode_attention
+    if q_heads // kv_heads > 8:
+        pytest.skip("GQA groups above 8 are outside the kernel's contract")
+    lengths = [length] * batch
+    q, k, v, position = _ragged(batch, q_heads, kv_heads, dim, lengths, seed=batch * 7 + length)
+    shared = position[:1].contiguous()
+    cluster = decode_attention(q, k, v, shared, 1 / math.sqrt(dim))
+    persistent = decode_attention(q, k, v, position, 1 / math.sqrt(dim))
+    expect = torch_fp32_decode(q, k, v, lengths, 1 / math.sqrt(dim))
+    assert torch.isfinite(cluster.float()).all()
+    torch.testing.assert_close(cluster.float(), expect, atol=2e-2, rtol=2e-2)
+    torch.testing.assert_close(cluster.float(), persistent.float(), atol=2e-2, rtol=2e-2)
+    again = decode_attention(q, k, v, shared, 1 / math.sqrt(dim))
+    assert torch.equal(cluster, again)  # deterministic
+
+
 def test_decode_attention_graph_capture_and_determinism():
     from kernels.decode_attention import decode_attention
     q, k, v, position = _ragged(2, 32, 8, 128, [5000, 777], seed=5, poison=False)
@@ -248,20 +276,27 @@ def test_linear_split_result_feeds_consumers():
 
 
 def test_swiglu_linear_matches_oracle():
-    """Fused projection + SwiGLU (64-row gate/up blocks) equals projecting gate and up separately
-    and applying the reference's SwiGLU (swiglu.py:13-24)."""
+    """Projection + SwiGLU on 64-row gate/up blocks equals projecting gate and up separately and
+    applying the reference's SwiGLU (swiglu.py:13-24), in every form: the split-partials path
+    with fb_swiglu_blocked (what swiglu_linear picks when the shape needs K splits) and the
+    fused epilogue at one split and over a cluster of splits."""
     import qwen3
-    from kernels.linear import swiglu_linear
+    from kernels import linear as klin
     g = torch.Generator().manual_seed(11)
-    for rows, width, hidden in ((1, 3072, 1024), (16, 1536, 4096), (5, 256, 256), (33, 512, 1024)):
+    for rows, width, hidden in ((1, 3072, 1024), (16, 1536, 4096), (5, 256, 256), (33, 512, 1024), (16, 12288, 4096)):
         x = torch.randn(rows, hidden, generator=g).bfloat16()
         gate = (torch.randn(width, hidden, generator=g) * 0.05).bfloat16()
         up = (torch.randn(width, hidden, generator=g) * 0.05).bfloat16()
-        blocked = qwen3.interleave_gate_up(gate, up).contiguous()
-        got = swiglu_linear(x.to(DEV), blocked.to(DEV)).cpu()
+        blocked = qwen3.interleave_gate_up(gate, up).contiguous().to(DEV)
         expect = opw.swiglu(torch.cat((opw.linear(x, gate), opw.linear(x, up)), -1))
-        assert (got == expect).float().mean() >= 0.99
-        torch.testing.assert_close(got.float(), expect.float(), atol=0.015625, rtol=0.016)
+        xd = x.to(DEV)
+        forms = {"swiglu_linear": klin.swiglu_linear(xd, blocked)}
+        for splits in (1, 2):
+            forms[f"epilogue S={splits}"] = klin.project(xd, blocked, klin.SWIGLU_OUT, splits)
+        for name, got in forms.items():
+            got = got.cpu()
+            assert (got == expect).float().mean() >= 0.99, name
+            torch.testing.assert_close(got.float(), expect.float(), atol=0.015625, rtol=0.016, msg=name)
 
 
 def test_argmax_matches_reference():
@@ -303,10 +338,11 @@ def test_fused_argmax_equals_projection_then_argmax():
 
 
 def test_decode_attention_fused_equals_two_launch_and_counters_reset():
-    """fb_decode_attention (last CTA merges) equals fb_decode_attention_partials +
-    fb_decode_attention_combine bit for bit, and leaves its per-pair counters at zero."""
+    """fb_decode_attention (persistent form, last CTA merges) equals fb_decode_attention_partials
+    + fb_decode_attention_combine bit for bit, and leaves its per-pair counters at zero. Per-row
+    positions (two or more rows) keep every call on the persistent form."""
     from kernels.decode_attention import _ctas, attend, workspace_bytes
-    for lengths, q_heads in (([1, 700, 8192, 65], 32), ([30000], 16), ([300, 301, 302, 303, 1, 2, 3, 4], 16)):
+    for lengths, q_heads in (([1, 700, 8192, 65], 32), ([30000, 20001], 16), ([300, 301, 302, 303, 1, 2, 3, 4], 16)):
         q, k, v, position = _ragged(len(lengths), q_heads, 8, 128, lengths, seed=sum(lengths))
         ctas = _ctas((q.device, len(lengths), 8, k.shape[2], 128))
         ws = torch.zeros(workspace_bytes(len(lengths), q_heads, 8, 128, ctas), dtype=torch.uint8, device=DEV)
