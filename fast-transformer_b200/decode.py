@@ -140,16 +140,26 @@ def _qk_rope_decode(packed, layer, eps, cos, sin, position, keys, values, q_head
     return query.view(batch, q_heads, 1, dim)  # one token: token-major storage is [B, Hq, 1, D]
 
 
+#: K chunks (64 columns) up to which the push projection runs as one split with the push in
+#: its epilogue; longer K writes split partials that fb_reduce_push sums and pushes (on B200
+#: a cluster reduction of the splits inside the projection measured 3-5 us slower).
+PUSH_SINGLE_SPLIT_CHUNKS = 8
+
+
 def _push_projection(x, weight, comm, peers, use, epoch):
     """This rank's fp32 partial of x @ W^T, pushed to every rank's recv[use] flagged with
-    epoch + 1 (fb_linear_allreduce_push)."""
+    epoch + 1 (fb_linear_allreduce_push, or split partials + fb_reduce_push)."""
     rows = x.numel() // x.shape[-1]
     flat = x.reshape(rows, x.shape[-1]).contiguous()
     n, k = weight.shape
-    splits = klinear.splits_for(rows, n, k, x.device, finished=True)
-    check(lib.fb_linear_allreduce_push(ptr(flat), ptr(weight), rows, n, k, splits, comm.size, comm.rank, use,
-                                       peers.recv_ptrs, ptr(epoch), stream()),
-          "fb_linear_allreduce_push")
+    if (k + 63) // 64 <= PUSH_SINGLE_SPLIT_CHUNKS:
+        check(lib.fb_linear_allreduce_push(ptr(flat), ptr(weight), rows, n, k, 1, comm.size, comm.rank, use,
+                                           peers.recv_ptrs, ptr(epoch), stream()), "fb_linear_allreduce_push")
+        return
+    splits = min(klinear.splits_for(rows, n, k, x.device), klinear.MAX_CLUSTER_SPLITS)
+    partials = klinear.project(flat, weight, klinear.SPLITS_OUT, splits)
+    check(lib.fb_reduce_push(ptr(partials), splits, rows, n, comm.size, comm.rank, use, peers.recv_ptrs, ptr(epoch),
+                             stream()), "fb_reduce_push")
 
 
 def _reduce_add_norm(peers, use, epoch, residual, weight, eps):

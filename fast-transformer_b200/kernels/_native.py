@@ -57,6 +57,7 @@ _SIGNATURES = {
                                           _vp]),
     "fb_merge_splits": (_c_int, [_vp, _c_int, _c_i64, _vp, _c_int, _vp]),
     "fb_swiglu_blocked": (_c_int, [_vp, _c_int, _vp, _c_int, _c_int, _vp]),
+    "fb_reduce_push": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp]),
     "fb_argmax_candidates_bytes": (_c_size, [_c_int, _c_int]),
     "fb_linear_argmax": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _c_i64, _vp, _vp]),
     "fb_argmax_candidates": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp, _vp]),

@@ -250,6 +250,10 @@ int fb_argmax_candidates(const void* cand, int rows, int tiles, int world, int r
 int fb_linear_allreduce_push(const void* x, const void* w, int m, int n, int k, int splits, int world,
                              int rank, int use, void* const* peer_recv, const int64_t* epoch,
                              void* stream);
+/* The producer's split-K form: sums fp32 partials [splits, M, N] in split order and pushes
+ * every value like fb_linear_allreduce_push (same recv layout and flags); N % 4 == 0. */
+int fb_reduce_push(const void* partials, int splits, int m, int n, int world, int rank, int use,
+                   void* const* peer_recv, const int64_t* epoch, void* stream);
 int fb_allreduce_add_rmsnorm(const void* recv, int use, int world, const int64_t* epoch,
                              const void* residual, const void* w, void* out, void* sum, int rows,
                              int width, float eps, void* stream);

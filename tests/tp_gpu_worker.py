@@ -17,6 +17,34 @@ import decode as fdecode  # noqa: E402
 import qwen3  # noqa: E402
 
 
+def check_push_forms(comm, device, rank, world):
+    """Both all-reduce producers (one-split projection with the push epilogue; split partials +
+    fb_reduce_push) through fb_allreduce_add_rmsnorm: every rank gets the same bits, close to
+    an NCCL all-reduce of the fp32 partials followed by the same add + RMSNorm."""
+    from kernels.rmsnorm import add_rms_norm
+    peers = fdecode.PeerBuffers(comm, 2, 16, 4096, device)
+    epoch = torch.full((1,), 41, dtype=torch.int64, device=device)
+    g = torch.Generator(device=device).manual_seed(100 + rank)
+    residual = torch.randn(16, 4096, device=device, generator=torch.Generator(device=device).manual_seed(7)).bfloat16()
+    gain = torch.ones(4096, device=device).bfloat16()
+    checks = {}
+    for use, k in enumerate((512, 1536)):  # 8 chunks: one split; 24 chunks: split partials + reduce-push
+        x = torch.randn(16, k, device=device, generator=g).bfloat16()
+        weight = (torch.randn(4096, k, device=device, generator=g) * 0.05).bfloat16()
+        fdecode._push_projection(x, weight, comm, peers, use, epoch)
+        out, summed = fdecode._reduce_add_norm(peers, use, epoch, residual, gain, 1e-6)
+        partial = x.float() @ weight.float().T
+        dist.all_reduce(partial)
+        ref_out, ref_sum = add_rms_norm(partial.bfloat16(), residual, gain, 1e-6)
+        gathered = [torch.empty_like(out) for _ in range(world)]
+        dist.all_gather(gathered, out)
+        checks[f"K={k} ranks agree"] = all(torch.equal(t, gathered[0]) for t in gathered)
+        checks[f"K={k} vs NCCL"] = bool((out.float() - ref_out.float()).abs().max() <= 0.05) and \
+            bool((summed.float() - ref_sum.float()).abs().max() <= 0.05)
+    torch.cuda.synchronize()
+    return checks
+
+
 def main():
     rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
     torch.cuda.set_device(local)
@@ -24,6 +52,11 @@ def main():
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
     ok = True
     try:
+        comm0 = fdecode.Communicator(dist.group.WORLD, world, rank)
+        push_checks = check_push_forms(comm0, device, rank, world)
+        if rank == 0:
+            print("push forms", push_checks, flush=True)
+        ok = all(push_checks.values())
         fx = torch.load(os.path.join(HERE, "golden", "model.pt"), weights_only=False)
         cfg = qwen3.Config.make(**cases.TINY_QWEN3)
         state_dict = cases.tiny_qwen3_weights()
