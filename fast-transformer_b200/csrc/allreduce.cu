@@ -23,18 +23,20 @@ struct Params {
   const int64_t* epoch;
 };
 
+// Two values per thread, so one store instruction of a warp writes 512 contiguous bytes
+// (32 lanes x one 16-byte pair of flagged words) to each peer.
 __global__ void __launch_bounds__(kThreads) reduce_push_kernel(const __grid_constant__ Params p) {
   pdl_wait();
   pdl_trigger();
-  const int64_t i = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) * 4;
+  const int64_t i = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) * 2;
   const int64_t count = static_cast<int64_t>(p.m) * p.n;
   if (i >= count) return;
-  float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+  float2 x = make_float2(0.f, 0.f);
   for (int s0 = 0; s0 < p.splits; s0 += kBatch) {
-    float4 part[kBatch];
+    float2 part[kBatch];
 #pragma unroll
     for (int j = 0; j < kBatch; ++j)
-      if (s0 + j < p.splits) part[j] = __ldcg(reinterpret_cast<const float4*>(p.partials + (s0 + j) * count + i));
+      if (s0 + j < p.splits) part[j] = __ldcg(reinterpret_cast<const float2*>(p.partials + (s0 + j) * count + i));
 #pragma unroll
     for (int j = 0; j < kBatch; ++j) {
       if (s0 + j == 0) {
@@ -42,20 +44,15 @@ __global__ void __launch_bounds__(kThreads) reduce_push_kernel(const __grid_cons
       } else if (s0 + j < p.splits) {
         x.x += part[j].x;
         x.y += part[j].y;
-        x.z += part[j].z;
-        x.w += part[j].w;
       }
     }
   }
   const uint64_t flag = static_cast<uint64_t>(static_cast<uint32_t>(*p.epoch) + 1u) << 32;
   const uint64_t w0 = flag | __float_as_uint(x.x), w1 = flag | __float_as_uint(x.y);
-  const uint64_t w2 = flag | __float_as_uint(x.z), w3 = flag | __float_as_uint(x.w);
   const size_t off = (static_cast<size_t>(p.use) * p.world + p.rank) * count + i;
-  for (int q = 0; q < p.world; ++q) {
-    uint64_t* dst = p.peer_recv[q] + off;
-    asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(dst), "l"(w0), "l"(w1) : "memory");
-    asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(dst + 2), "l"(w2), "l"(w3) : "memory");
-  }
+  for (int q = 0; q < p.world; ++q)
+    asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p.peer_recv[q] + off), "l"(w0), "l"(w1)
+                 : "memory");
 }
 
 }  // namespace ar
@@ -67,7 +64,7 @@ extern "C" int fb_reduce_push(const void* partials, int splits, int m, int n, in
                               void* const* peer_recv, const int64_t* epoch, void* stream) {
   if (!partials || !peer_recv || !epoch || splits <= 0 || m <= 0 || n <= 0) return FB_ERR_ARG;
   if (world < 1 || world > ar::kMaxWorld || rank < 0 || rank >= world || use < 0) return FB_ERR_ARG;
-  if (n % 4 != 0) return FB_ERR_SHAPE;
+  if (n % 2 != 0) return FB_ERR_SHAPE;
   ar::Params p{};
   p.partials = static_cast<const float*>(partials);
   p.splits = splits;
@@ -81,7 +78,7 @@ extern "C" int fb_reduce_push(const void* partials, int splits, int m, int n, in
     if (!peer_recv[r] || (reinterpret_cast<uintptr_t>(peer_recv[r]) & 15u)) return FB_ERR_ARG;
     p.peer_recv[r] = static_cast<uint64_t*>(peer_recv[r]);
   }
-  const int64_t threads = (static_cast<int64_t>(m) * n + 3) / 4;
+  const int64_t threads = (static_cast<int64_t>(m) * n + 1) / 2;
   const int64_t blocks = (threads + ar::kThreads - 1) / ar::kThreads;
   if (blocks >= (1ll << 31)) return FB_ERR_SHAPE;
   return launch_ex(ar::reduce_push_kernel, dim3(static_cast<unsigned>(blocks)), dim3(ar::kThreads), 0,

@@ -131,21 +131,20 @@ __device__ void epilogue(const Params& p, const float* vals, int tile, int tid, 
   if (p.epilogue == kPush) {
     // Low-latency push: each fp32 value travels with its flag in one 8-byte word (stored
     // whole), so a reader that sees the flag sees the value; no fence or counter is needed.
+    // Two values per thread: consecutive lanes store consecutive 16-byte pairs of flagged
+    // words, so a warp's store instruction writes 512 contiguous bytes to each peer.
     const uint64_t flag = static_cast<uint64_t>(static_cast<uint32_t>(*p.epoch) + 1u) << 32;
     const size_t slab = static_cast<size_t>(p.m) * p.n;
-    for (int e = tid; e < p.m * (kTileN / 4); e += kConsumerWarps * 32) {
-      const int m = e / (kTileN / 4), c4 = e % (kTileN / 4);
-      if (n0 + c4 * 4 >= p.n || !owned(c4, kPush, r, S)) continue;
-      const float4 v = *reinterpret_cast<const float4*>(vals + m * kTileN + c4 * 4);
+    for (int e = tid; e < p.m * (kTileN / 2); e += kConsumerWarps * 32) {
+      const int m = e / (kTileN / 2), c2 = e % (kTileN / 2);
+      if (n0 + c2 * 2 >= p.n || !owned(c2 >> 1, kPush, r, S)) continue;
+      const float2 v = *reinterpret_cast<const float2*>(vals + m * kTileN + c2 * 2);
       const size_t off = (static_cast<size_t>(p.use) * p.world + p.rank) * slab + static_cast<size_t>(m) * p.n +
-                         n0 + c4 * 4;
+                         n0 + c2 * 2;
       const uint64_t w0 = flag | __float_as_uint(v.x), w1 = flag | __float_as_uint(v.y);
-      const uint64_t w2 = flag | __float_as_uint(v.z), w3 = flag | __float_as_uint(v.w);
-      for (int q = 0; q < p.world; ++q) {
-        uint64_t* dst = p.peer_recv[q] + off;
-        asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(dst), "l"(w0), "l"(w1) : "memory");
-        asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(dst + 2), "l"(w2), "l"(w3) : "memory");
-      }
+      for (int q = 0; q < p.world; ++q)
+        asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p.peer_recv[q] + off), "l"(w0), "l"(w1)
+                     : "memory");
     }
     return;
   }

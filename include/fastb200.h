@@ -251,7 +251,7 @@ int fb_linear_allreduce_push(const void* x, const void* w, int m, int n, int k, 
                              int rank, int use, void* const* peer_recv, const int64_t* epoch,
                              void* stream);
 /* The producer's split-K form: sums fp32 partials [splits, M, N] in split order and pushes
- * every value like fb_linear_allreduce_push (same recv layout and flags); N % 4 == 0. */
+ * every value like fb_linear_allreduce_push (same recv layout and flags); N % 2 == 0. */
 int fb_reduce_push(const void* partials, int splits, int m, int n, int world, int rank, int use,
                    void* const* peer_recv, const int64_t* epoch, void* stream);
 int fb_allreduce_add_rmsnorm(const void* recv, int use, int world, const int64_t* epoch,
