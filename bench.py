@@ -24,6 +24,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -57,8 +58,7 @@ class Clocks:
     def __init__(self, gpus):
         self.gpus = ",".join(str(g) for g in gpus)
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{os.getpid()}.csv") if os.path.isdir(
-            os.path.join(ROOT, "gpurun_out")) else f"/tmp/clocks_{os.getpid()}.csv"
+        self.path = os.path.join(tempfile.gettempdir(), f"clocks_{os.getpid()}.csv")
 
     def start(self):
         try:
@@ -399,8 +399,12 @@ def main():
     kv_bytes = 2 * BATCH * weights.kv_heads * valid * cfg.head_dim * 2
     qo_bytes = 2 * BATCH * weights.q_heads * cfg.head_dim * 2
     achieved = (kv_bytes + qo_bytes) / (attn_ms / 1e3) / 1e9
+    # DRAM traffic of one launch from an ncu capture of this kernel at 16 rows x 8 KV heads x
+    # 8320 slots (dram__bytes_read.sum 545.77 MB + dram__bytes_write.sum 4.09 MB), scaled to
+    # this launch's valid slots (traffic grows in proportion to the slots streamed)
+    traffic = (545.77e6 + 4.09e6) * (valid / 8320) if weights.kv_heads == 8 else None
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                "traffic": None, "kernel": "fb_decode_attention + combine (per layer)",
+                "traffic": traffic, "kernel": "fb_decode_attention (per layer)",
                 "algorithmic_bytes": kv_bytes + qo_bytes, "launch_us": attn_ms * 1e3,
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6.65 TB/s"}
     # per-rank algorithmic bytes of an average timed step: every weight once, K/V of the valid slots

@@ -1,6 +1,6 @@
 """Generate the golden fixtures by running the REFERENCE's own code on CPU.
 
-    python tests/golden/make_golden.py [--reference /path/to/fast-transformer]
+    python tests/golden/make_golden.py --reference /path/to/fast-transformer
 
 Runs john-jpet/fast-transformer's kernel wrappers (engine/kernels/*.py) with their kernel
 bodies replaced by the reference's own CPU restatements (agent/local_cpu/shim: the fake
@@ -64,7 +64,7 @@ def setup_reference(root):
 
 def main():
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference", default="/root/reference")
+    parser.add_argument("--reference", required=True, help="checkout of john-jpet/fast-transformer")
     parser.add_argument("--only", default="")
     args = parser.parse_args()
     cuda_shim = setup_reference(args.reference)
