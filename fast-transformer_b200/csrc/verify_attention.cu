@@ -29,10 +29,13 @@ namespace verify {
 
 constexpr int kTile = 128;          // tokens per K/V tile (UMMA M of the score product)
 constexpr int kMembers = 32;        // member columns per CTA (UMMA N)
-constexpr int kStages = 2;
-constexpr int kSoftmaxWarps = 4;    // 128 threads = 128 TMEM lanes
-constexpr int kThreads = (kSoftmaxWarps + 1) * 32;
-constexpr int kTmemCols = 64;       // S^T (32 columns) + O^T tile (32 columns)
+constexpr int kStages = 3;          // K/V ring depth (64 KB stages)
+constexpr int kSoftmaxWarps = 8;    // warp w: TMEM lanes 32*(w%4).., member columns 16*(w/4)..
+constexpr int kHalf = kMembers / 2; // member columns per softmax warp
+constexpr int kProducerWarp = kSoftmaxWarps;      // one lane issues every TMA
+constexpr int kMmaWarp = kSoftmaxWarps + 1;       // one lane issues every UMMA; the warp owns TMEM
+constexpr int kThreads = (kSoftmaxWarps + 2) * 32;
+constexpr int kTmemCols = 4 * kMembers;  // S^T double buffer + O^T tile double buffer
 
 struct Params {
   const __nv_bfloat16* q;  // [B, T, Hq, D] token-major
@@ -82,30 +85,35 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
+// 2^x with the PTX approximate base-2 exponential (what the reference's tl.exp2 lowers to);
+// -inf gives +0.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[kHalf]) {
+  uint32_t r[16];
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// Column-wise reduction of a 32x32 block held one row per lane: afterwards lane c holds the
-// reduction of column c (shuffle transpose-reduce, 31 shuffles).
+// Column-wise reduction of a 32x16 block held one row per lane: afterwards lanes c and c+16
+// hold the reduction of column c over all 32 rows (shuffle transpose-reduce, 16 shuffles).
 template <bool kMax>
-__device__ __forceinline__ float transpose_reduce(float (&v)[32], int lane) {
-  float a[32];
+__device__ __forceinline__ float transpose_reduce16(const float (&v)[kHalf], int lane) {
+  float a[kHalf];
 #pragma unroll
-  for (int i = 0; i < 32; ++i) a[i] = v[i];
+  for (int i = 0; i < kHalf; ++i) a[i] = v[i];
 #pragma unroll
-  for (int width = 16; width >= 1; width >>= 1) {
+  for (int width = kHalf / 2; width >= 1; width >>= 1) {
     const bool upper = (lane & width) != 0;
 #pragma unroll
     for (int i = 0; i < width; ++i) {
@@ -115,18 +123,21 @@ __device__ __forceinline__ float transpose_reduce(float (&v)[32], int lane) {
       a[i] = kMax ? fmaxf(mine, recv) : mine + recv;
     }
   }
-  return a[0];
+  const float recv = __shfl_xor_sync(0xffffffffu, a[0], 16);
+  return kMax ? fmaxf(a[0], recv) : a[0] + recv;
 }
 
 struct Smem {
   static constexpr int kTileBytes = 2 * kTile * 128;       // one of K or V: two 64-dim boxes
   static constexpr int kStageBytes = 2 * kTileBytes;       // K then V
   static constexpr int kQBytes = 2 * kMembers * 128;       // two 64-dim boxes of 32 rows
-  static constexpr int kPBytes = 2 * kMembers * 128;       // two 64-token boxes of 32 rows
-  static constexpr int kRed = kSoftmaxWarps * kMembers * 4;
-  static constexpr int kCol = 4 * kMembers * 4;            // run max, pivot, correction, mask data
-  static constexpr int kBars = (2 * kStages + 2) * 8;
-  static constexpr int kTotal = 1024 + kStages * kStageBytes + kQBytes + kPBytes + kRed + kCol + 2 * kMembers * 4 + kBars + 32;
+  static constexpr int kPBytes = 2 * kMembers * 128;       // one P tile: two 64-token boxes of 32 rows
+  static constexpr int kRed = 2 * 4 * kMembers * 4;       // per-quarter column maxima, by tile parity
+  static constexpr int kCol = 3 * kMembers * 4;            // run max, pivot, correction
+  static constexpr int kMask = 2 * kMembers * 4;           // visibility limits per member
+  static constexpr int kBars = (2 * kStages + 4 * 2) * 8;
+  static constexpr int kTotal = 1024 + kStages * kStageBytes + kQBytes + 2 * kPBytes + kRed + kCol + kMask + kBars + 32;
+  static_assert(kTotal <= 227 * 1024, "verify shared memory");
 };
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -138,17 +149,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = base;
   uint8_t* q_s = base + kStages * Smem::kStageBytes;
-  uint8_t* p_s = q_s + Smem::kQBytes;
-  float* red = reinterpret_cast<float*>(p_s + Smem::kPBytes);
-  float* col_max = red + kSoftmaxWarps * kMembers;   // running max per member
+  uint8_t* p_s = q_s + Smem::kQBytes;  // two P tiles
+  float* red = reinterpret_cast<float*>(p_s + 2 * Smem::kPBytes);
+  float* col_max = red + 2 * 4 * kMembers;   // running max per member (final, for split stats)
   float* col_piv = col_max + kMembers;
   float* col_corr = col_piv + kMembers;
   int* col_valid = reinterpret_cast<int*>(col_corr + kMembers);
   int* col_own = col_valid + kMembers;
-  uint64_t* full = reinterpret_cast<uint64_t*>(col_own + kMembers);
-  uint64_t* empty = full + kStages;
-  uint64_t* mma_bar = empty + kStages;  // [0] scores done, [1] values done
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_bar + 2);
+  uint64_t* full = reinterpret_cast<uint64_t*>(col_own + kMembers);  // TMA -> MMA, per stage
+  uint64_t* empty = full + kStages;                                   // MMA -> TMA, per stage
+  uint64_t* s_full = empty + kStages;   // MMA -> softmax: S^T[b] holds a tile's scores
+  uint64_t* s_free = s_full + 2;        // softmax -> MMA: S^T[b] has been read
+  uint64_t* p_full = s_free + 2;        // softmax -> MMA: P[b] written
+  uint64_t* o_full = p_full + 2;        // MMA -> softmax: O^T[b] holds a tile's product
+  uint64_t* o_free = o_full + 2;        // softmax -> MMA: O^T[b] has been read
+  uint64_t* done = o_free + 2;          // MMA lane: every issued UMMA has completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
@@ -164,19 +180,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tiles = stop > begin ? static_cast<int>((stop - begin + kTile - 1) / kTile) : 0;
 
   // ---- set-up: barriers, TMEM, Q tile, per-member visibility ----
-  if (warp == kSoftmaxWarps && lane == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+  if (warp == kProducerWarp && lane == 0) {
+    for (int st = 0; st < kStages; ++st) {
+      mbar_init(&full[st], 1);
+      mbar_init(&empty[st], 1);
     }
-    mbar_init(&mma_bar[0], 1);
-    mbar_init(&mma_bar[1], 1);
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(&s_full[x], 1);
+      mbar_init(&s_free[x], kSoftmaxWarps);
+      mbar_init(&p_full[x], kSoftmaxWarps);
+      mbar_init(&o_full[x], 1);
+      mbar_init(&o_free[x], kSoftmaxWarps);
+    }
+    mbar_init(done, 1);
     fence_barrier_init();
     prefetch_tensormap(&kmap);
     prefetch_tensormap(&vmap);
     *abort_flag = 0;
   }
-  if (warp == 0) {
+  if (warp == kMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -209,109 +231,183 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tmem_s = tmem;              // columns [0, 32): S^T
-  const uint32_t tmem_o = tmem + kMembers;   // columns [32, 64): O^T of the current tile
+  // S^T[x] = columns [32x, 32x + 32); O^T[x] = columns [64 + 32x, 96 + 32x)
 
-  if (warp == kSoftmaxWarps) {
+  if (warp == kProducerWarp) {
     // ============================ TMA producer ============================
     if (lane == 0) {
       const int row0 = pair * p.capacity + static_cast<int>(begin);
       for (int i = 0; i < tiles && !*abort_flag; ++i) {
-        const int s = i % kStages;
-        if (i >= kStages && !mbar_wait_bounded(&empty[s], ((i / kStages) - 1) & 1)) {
+        const int st = i % kStages;
+        if (i >= kStages && !mbar_wait_bounded(&empty[st], ((i / kStages) - 1) & 1)) {
           raise_error(p.err, kErrTimeoutEmpty);
           *abort_flag = 1;
           break;
         }
-        uint8_t* kt = stages + s * Smem::kStageBytes;
+        uint8_t* kt = stages + st * Smem::kStageBytes;
         uint8_t* vt = kt + Smem::kTileBytes;
-        mbar_arrive_expect_tx(&full[s], Smem::kStageBytes);
+        mbar_arrive_expect_tx(&full[st], Smem::kStageBytes);
         const int row = row0 + i * kTile;
-        tma_load_2d(kt, &kmap, &full[s], 0, row);
-        tma_load_2d(kt + kTile * 128, &kmap, &full[s], 64, row);
-        tma_load_2d(vt, &vmap, &full[s], 0, row);
-        tma_load_2d(vt + kTile * 128, &vmap, &full[s], 64, row);
+        tma_load_2d(kt, &kmap, &full[st], 0, row);
+        tma_load_2d(kt + kTile * 128, &kmap, &full[st], 64, row);
+        tma_load_2d(vt, &vmap, &full[st], 0, row);
+        tma_load_2d(vt + kTile * 128, &vmap, &full[st], 64, row);
       }
     }
-  } else {
-    // ======================= softmax / MMA warps (128 threads) =======================
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-    const uint32_t q_addr = smem_u32(q_s), p_addr = smem_u32(p_s);
-    const uint32_t idesc_s = idesc_bf16(false), idesc_o = idesc_bf16(true);
-    float o[kMembers], l[kMembers];
-#pragma unroll
-    for (int c = 0; c < kMembers; ++c) o[c] = l[c] = 0.f;
-    const float sl2 = p.scale_log2;
-    int mma_phase = 0;
-    for (int i = 0; i < tiles; ++i) {
-      const int s = i % kStages;
-      bool ok = mbar_wait_bounded(&full[s], (i / kStages) & 1);
-      if (!ok) {
-        raise_error(p.err, kErrTimeoutFull);
-        *abort_flag = 1;
-      }
-      if (*abort_flag) break;
-      uint8_t* kt = stages + s * Smem::kStageBytes;
-      uint8_t* vt = kt + Smem::kTileBytes;
-      const long long tile0 = begin + static_cast<long long>(i) * kTile;
-      // ---- S^T = K_tile * Q^T : 8 UMMAs over D = 128 ----
-      if (tid == 0) {
+  } else if (warp == kMmaWarp) {
+    // ============================ UMMA issuer ============================
+    // Order: S(i), then O(i-1) once P(i-1) is written - the tensor core computes O(i-1) and
+    // S(i+1) while the softmax warps work on tile i.
+    if (lane == 0) {
+      const uint32_t q_addr = smem_u32(q_s), p_addr = smem_u32(p_s);
+      const uint32_t idesc_s = idesc_bf16(false), idesc_o = idesc_bf16(true);
+      auto issue_o = [&](int j) -> bool {
+        const int x = j & 1;
+        if (!mbar_wait_bounded(&p_full[x], (j >> 1) & 1)) return false;
+        if (j >= 2 && !mbar_wait_bounded(&o_free[x], ((j - 2) >> 1) & 1)) return false;
         tc_fence_after();
-        const uint32_t k_addr = smem_u32(kt);
+        const uint32_t v_addr = smem_u32(stages + (j % kStages) * Smem::kStageBytes + Smem::kTileBytes);
+        const uint32_t pb = p_addr + x * Smem::kPBytes;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off_v = kk * 16 * 128;  // 16 tokens = two 8-row groups
+          const uint32_t off_p = (kk >> 2) * (kMembers * 128) + (kk & 3) * 32;
+          umma_bf16(tmem + 64 + 32 * x, umma_desc(v_addr + off_v, kTile * 128, 1024), umma_desc(pb + off_p, 16, 1024),
+                    idesc_o, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&o_full[x]);
+        umma_commit(&empty[j % kStages]);  // both products of tile j read their K/V stage
+        return true;
+      };
+      bool ok = true;
+      for (int i = 0; i < tiles && ok; ++i) {
+        const int st = i % kStages, x = i & 1;
+        ok = mbar_wait_bounded(&full[st], (i / kStages) & 1) &&
+             (i < 2 || mbar_wait_bounded(&s_free[x], ((i - 2) >> 1) & 1));
+        if (!ok || *abort_flag) break;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(stages + st * Smem::kStageBytes);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off_k = (kk >> 2) * (kTile * 128) + (kk & 3) * 32;
           const uint32_t off_q = (kk >> 2) * (kMembers * 128) + (kk & 3) * 32;
-          umma_bf16(tmem_s, umma_desc(k_addr + off_k, 16, 1024), umma_desc(q_addr + off_q, 16, 1024), idesc_s,
+          umma_bf16(tmem + 32 * x, umma_desc(k_addr + off_k, 16, 1024), umma_desc(q_addr + off_q, 16, 1024), idesc_s,
                     kk > 0 ? 1u : 0u);
         }
-        umma_commit(&mma_bar[0]);
+        umma_commit(&s_full[x]);
+        if (i >= 1) ok = issue_o(i - 1);
       }
-      if (!mbar_wait_bounded(&mma_bar[0], mma_phase)) {
+      if (ok && tiles >= 1 && !*abort_flag) ok = issue_o(tiles - 1);
+      if (!ok) {
         raise_error(p.err, kErrTimeoutMma);
         *abort_flag = 1;
+      }
+      // every UMMA issued above has completed before TMEM can be freed
+      umma_commit(done);
+      if (!mbar_wait_bounded(done, 0)) raise_error(p.err, kErrTimeoutDrain);
+    }
+    __syncwarp();
+  } else {
+    // ======================= softmax warps (256 threads) =======================
+    // Warp w reads TMEM lanes 32*(w%4).. (tokens of S^T, dims of O^T) and member columns
+    // [16*(w/4), 16*(w/4) + 16): two warps per scheduler, 16 columns per thread.
+    const int quarter = warp & 3, half = warp >> 2;
+    const int row = quarter * 32 + lane;  // token of the S^T tile, dim of the O^T tile
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const int col0 = half * kHalf;
+    float o[kHalf], l[kHalf], corr_prev[kHalf], run_max[kHalf];
+#pragma unroll
+    for (int c = 0; c < kHalf; ++c) {
+      o[c] = l[c] = corr_prev[c] = 0.f;
+      run_max[c] = -INFINITY;
+    }
+    const float sl2 = p.scale_log2;
+    // o <- o * corr(j) + O^T(j): the product of tile j, read from TMEM once it is complete
+    auto fold = [&](int j) -> bool {
+      const int x = j & 1;
+      if (!mbar_wait_bounded(&o_full[x], (j >> 1) & 1)) return false;
+      tc_fence_after();
+      float ot[kHalf];
+      tmem_ld16(tmem + 64 + 32 * x + col0 + lane_base, ot);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_free[x]);
+#pragma unroll
+      for (int c = 0; c < kHalf; ++c) o[c] = o[c] * corr_prev[c] + ot[c];
+      return true;
+    };
+    bool ok = true;
+    for (int i = 0; i < tiles; ++i) {
+      const int x = i & 1;
+      if (*abort_flag || !mbar_wait_bounded(&s_full[x], (i >> 1) & 1)) {
+        ok = false;
         break;
       }
       tc_fence_after();
-      float sc[kMembers];
-      tmem_ld32(tmem_s + lane_base, sc);
-      // ---- mask, scale, column max ----
-      const long long tok = tile0 + tid;
+      float sc[kHalf];
+      tmem_ld16(tmem + 32 * x + col0 + lane_base, sc);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[x]);
+      const long long tile0 = begin + static_cast<long long>(i) * kTile;
+      uint8_t* vt = stages + (i % kStages) * Smem::kStageBytes + Smem::kTileBytes;
+      // ---- mask, scale, column max. A tile wholly below the block's first slot is visible
+      // to every live member (dead members' columns only ever reach their own, unused,
+      // outputs), so only the block's own tile pays the per-member masks. ----
+      const long long tok = tile0 + row;
       const bool in_range = tok < stop;
+      if (tile0 + kTile <= first - 1 && tile0 + kTile <= stop) {
 #pragma unroll
-      for (int c = 0; c < kMembers; ++c) {
-        const bool visible = in_range && (tok < col_valid[c] || tok == col_own[c]);
-        sc[c] = visible ? sc[c] * sl2 : -INFINITY;
+        for (int c = 0; c < kHalf; ++c) sc[c] *= sl2;
+      } else {
+#pragma unroll
+        for (int c = 0; c < kHalf; ++c) {
+          const bool visible = in_range && (tok < col_valid[col0 + c] || tok == col_own[col0 + c]);
+          sc[c] = visible ? sc[c] * sl2 : -INFINITY;
+        }
       }
-      const float wmax = transpose_reduce<true>(sc, lane);
-      red[warp * kMembers + lane] = wmax;
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (tid < kMembers) {
-        float tmax = red[tid];
+      // Column maxima: each quarter's max over its 32 tokens goes to red[parity][quarter];
+      // after one barrier every thread folds the four quarters and its running max itself
+      // (all threads of a column half compute the same values). red is double-buffered by
+      // tile parity: the next write to this half happens after the next tile's barrier.
+      const float wmax = transpose_reduce16<true>(sc, lane);
+      float* rq = red + x * 4 * kMembers;
+      if (lane < kHalf) rq[quarter * kMembers + col0 + lane] = wmax;
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      float piv[kHalf], corr[kHalf];
 #pragma unroll
-        for (int w = 1; w < kSoftmaxWarps; ++w) tmax = fmaxf(tmax, red[w * kMembers + tid]);
-        const float old = col_max[tid];
-        const float nm = fmaxf(old, tmax);
-        const float piv = nm == -INFINITY ? 0.f : nm;
-        col_piv[tid] = piv;
-        col_corr[tid] = exp2f(old - piv);
-        col_max[tid] = nm;
+      for (int c4 = 0; c4 < kHalf / 4; ++c4) {
+        float4 t4 = *reinterpret_cast<const float4*>(rq + col0 + 4 * c4);
+#pragma unroll
+        for (int w = 1; w < 4; ++w) {
+          const float4 u4 = *reinterpret_cast<const float4*>(rq + w * kMembers + col0 + 4 * c4);
+          t4.x = fmaxf(t4.x, u4.x), t4.y = fmaxf(t4.y, u4.y), t4.z = fmaxf(t4.z, u4.z), t4.w = fmaxf(t4.w, u4.w);
+        }
+        const float tm[4] = {t4.x, t4.y, t4.z, t4.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int c = 4 * c4 + e;
+          const float nm = fmaxf(run_max[c], tm[e]);
+          piv[c] = nm == -INFINITY ? 0.f : nm;
+          // an unchanged max rescales by exactly 1 (and an all -inf column has l = o = 0)
+          corr[c] = nm == run_max[c] ? 1.f : ex2_approx(run_max[c] - piv[c]);
+          run_max[c] = nm;
+        }
       }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      // ---- P (bf16) into the K-major swizzled tile: row = member, column = token tid ----
-      float corr[kMembers];
+      // ---- P (bf16) into P[x], K-major swizzled: row = member, column = token. P[x] was
+      // last read by O(i-2), whose completion fold(i-2) already waited for. ----
+      uint8_t* pt = p_s + x * Smem::kPBytes;
+      const uint32_t pcol = (row >> 6) * (kMembers * 128) + (row & 7) * 2;
 #pragma unroll
-      for (int c = 0; c < kMembers; ++c) {
-        const float pv = exp2f(sc[c] - col_piv[c]);
-        corr[c] = col_corr[c];
+      for (int c = 0; c < kHalf; ++c) {
+        const float pv = ex2_approx(sc[c] - piv[c]);
         l[c] = l[c] * corr[c] + pv;
-        const uint32_t off = (tid >> 6) * (kMembers * 128) + sw128(c, (tid & 63) >> 3) + (tid & 7) * 2;
-        *reinterpret_cast<__nv_bfloat16*>(p_s + off) = __float2bfloat16_rn(pv);
+        *reinterpret_cast<__nv_bfloat16*>(pt + pcol + sw128(col0 + c, (row & 63) >> 3)) = __float2bfloat16_rn(pv);
       }
-      if (!in_range) {
+      if (!in_range && half == 0) {
         // V row past the visible range: zero it so stale values never meet a zero weight.
-        uint8_t* vrow0 = vt + tid * 128;
-        uint8_t* vrow1 = vt + kTile * 128 + tid * 128;
+        uint8_t* vrow0 = vt + row * 128;
+        uint8_t* vrow1 = vt + kTile * 128 + row * 128;
 #pragma unroll
         for (int c16 = 0; c16 < 8; ++c16) {
           *reinterpret_cast<uint4*>(vrow0 + c16 * 16) = make_uint4(0, 0, 0, 0);
@@ -319,49 +415,40 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       fence_proxy_async_smem();
-      tc_fence_before();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      // ---- O^T_tile = V^T * P^T : 8 UMMAs over the 128 tokens ----
-      if (tid == 0) {
-        tc_fence_after();
-        const uint32_t v_addr = smem_u32(vt);
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t off_v = kk * 16 * 128;  // 16 tokens = two 8-row groups
-          const uint32_t off_p = (kk >> 2) * (kMembers * 128) + (kk & 3) * 32;
-          umma_bf16(tmem_o, umma_desc(v_addr + off_v, kTile * 128, 1024), umma_desc(p_addr + off_p, 16, 1024),
-                    idesc_o, kk > 0 ? 1u : 0u);
-        }
-        umma_commit(&mma_bar[1]);
-      }
-      if (!mbar_wait_bounded(&mma_bar[1], mma_phase)) {
-        raise_error(p.err, kErrTimeoutMma);
-        *abort_flag = 1;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[x]);
+      // fold the previous tile's product (computed while this tile's softmax ran)
+      if (i >= 1 && !fold(i - 1)) {
+        ok = false;
         break;
       }
-      mma_phase ^= 1;
-      tc_fence_after();
-      float ot[kMembers];
-      tmem_ld32(tmem_o + lane_base, ot);
 #pragma unroll
-      for (int c = 0; c < kMembers; ++c) o[c] = o[c] * corr[c] + ot[c];
-      // Both products of this stage are complete: hand the K/V buffers back to the producer.
-      tc_fence_before();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (tid == 0) mbar_arrive(&empty[s]);
+      for (int c = 0; c < kHalf; ++c) corr_prev[c] = corr[c];
+    }
+    if (ok && tiles >= 1 && !*abort_flag) ok = fold(tiles - 1);
+    if (!ok) {
+      raise_error(p.err, kErrTimeoutMma);
+      *abort_flag = 1;
     }
     if (!*abort_flag) {
-      // ---- denominators: per-member sums over the 128 token-threads ----
-      const float wsum = transpose_reduce<false>(l, lane);
-      red[warp * kMembers + lane] = wsum;
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      // thread tid = dim d holds o[member] for this tile chunk; write partials or the output
-      const int d = tid;
+      // ---- denominators: per-member sums over the 128 token rows; the final maxima ----
+      if (quarter == 0) {
 #pragma unroll
-      for (int c = 0; c < kMembers; ++c) {
-        const int m = group0 + c;
+        for (int c = 0; c < kHalf; ++c)
+          if (lane == c) col_max[col0 + c] = run_max[c];
+      }
+      const float wsum = transpose_reduce16<false>(l, lane);
+      asm volatile("bar.sync 1, 256;" ::: "memory");  // every thread is past its last max read
+      if (lane < kHalf) red[quarter * kMembers + col0 + lane] = wsum;
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      // thread (dim d = row, members col0..col0+15) writes partials or the output
+      const int d = row;
+#pragma unroll
+      for (int c = 0; c < kHalf; ++c) {
+        const int m = group0 + col0 + c;
         if (m >= members) continue;
-        const float L = red[c] + red[kMembers + c] + red[2 * kMembers + c] + red[3 * kMembers + c];
+        const int mc = col0 + c;
+        const float L = red[mc] + red[kMembers + mc] + red[2 * kMembers + mc] + red[3 * kMembers + mc];
         const int t = m / G, g = m % G;
         if (p.splits == 1) {
           const size_t o_off = ((static_cast<size_t>(b) * T + t) * p.q_heads + h * G + g) * 128 + d;
@@ -369,15 +456,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
           const size_t slot = (static_cast<size_t>(pair) * p.splits + split) * p.members_pad + m;
           p.acc[slot * 128 + d] = o[c];
-          if (d == 0) p.stats[slot] = make_float2(col_max[c], L);
+          if (d == 0) p.stats[slot] = make_float2(col_max[mc], L);
         }
       }
     }
   }
-  // ---- teardown: every TMEM read and MMA has completed above; free the columns ----
+  // ---- teardown: the MMA lane saw every UMMA complete and every TMEM read has waited ----
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
   }
@@ -419,12 +506,23 @@ using namespace fb;
 
 extern "C" int fb_verify_attention_splits(int batch, int tokens, int kv_heads, int capacity) {
   if (batch <= 0 || kv_heads <= 0 || capacity <= 0) return 1;
+  // One CTA per SM (the 3-stage ring fills shared memory). Model the time as waves x (tiles
+  // per CTA + ~2 tiles of fixed cost: TMEM allocation, Q staging, the first TMA round trip)
+  // and take the cheapest split count (config 5, 64 pairs x 33 tiles: 2 splits, one wave).
   const int tiles = (capacity + verify::kTile - 1) / verify::kTile;
-  const int want = (2 * sm_count() + batch * kv_heads - 1) / (batch * kv_heads);
-  int s = want < 1 ? 1 : want;
-  if (s > tiles) s = tiles;
-  if (s > 64) s = 64;
-  return s;
+  const long long pairs = static_cast<long long>(batch) * kv_heads;
+  const int sms = sm_count();
+  int best = 1;
+  long long best_cost = -1;
+  for (int s = 1; s <= tiles && s <= 64; ++s) {
+    const long long waves = (pairs * s + sms - 1) / sms;
+    const long long cost = waves * ((tiles + s - 1) / s + 2);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = s;
+    }
+  }
+  return best;
 }
 
 extern "C" size_t fb_verify_attention_workspace(int batch, int tokens, int q_heads, int kv_heads, int splits) {
