@@ -58,6 +58,11 @@ _SIGNATURES = {
     "fb_merge_splits": (_c_int, [_vp, _c_int, _c_i64, _vp, _c_int, _vp]),
     "fb_swiglu_blocked": (_c_int, [_vp, _c_int, _vp, _c_int, _c_int, _vp]),
     "fb_reduce_push": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp]),
+    "fb_spec_propose": (_c_int, [_vp, _c_i64, _vp, _vp, _c_i64, _c_int, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int,
+                                 _c_int, _c_int, _c_int, _c_int, _vp]),
+    "fb_spec_within_margin": (_c_int, [_vp, _c_i64, _vp, _vp, _vp, _c_int, _c_int, _c_float, _vp]),
+    "fb_spec_settle": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _vp]),
+    "fb_spec_relocate": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp]),
     "fb_argmax_candidates_bytes": (_c_size, [_c_int, _c_int]),
     "fb_linear_argmax": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _c_i64, _vp, _vp]),
     "fb_argmax_candidates": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp, _vp]),

@@ -230,6 +230,38 @@ int fb_argmax_candidates(const void* cand, int rows, int tiles, int world, int r
                          int64_t* out, float* top, void* stream);
 
 /* ------------------------------------------------------------------------------------
+ * Speculation bookkeeping (exact speculative decoding): replaces engine/kernels/spec.py's
+ * fused programs with the same semantics. All int64 unless noted; one launch each.
+ * fb_spec_propose (spec.py:16-124 `_propose`, wrapper `propose` :106-124): per row of
+ *   history [B, size], with the newest token at position[b]: tokens [B, T] (trusted token,
+ *   chain drafts, alternatives to draft 1), chains [B] = 1 + chain drafts, phases [B, T].
+ *   d0..d3 = drafts by match length (<= 1, <= 3, <= 7, longer), each in [1, T - 1];
+ *   successor [vocab, top]; stale [B] (a hint, or -1); maxlen = 8 in the reference; T <= 64.
+ * fb_spec_within_margin (spec.py:127-166): logits bf16 [B*T, vocab], top fp32 [B*T] (each
+ *   row's winning logit): within [B, T] = 1 where draft `slot` >= 1 has a logit within
+ *   `margin` of the winning logit of row slot - 1; slot 0 is written 0.
+ * fb_spec_settle (spec.py:169-240): accepts, clamps at limit, writes result [B, T + 1]
+ *   (gained, then the emitted tokens), history[b, position+1 : position+1+T], move_from
+ *   (-1 = no KV move) / move_to, stale, and advances position in place. within may be NULL
+ *   (exact acceptance: draft == the model's choice).
+ * fb_spec_relocate (spec.py:243-270): store bf16 [planes = 2 x layers, B, Hkv, C, D]: copy
+ *   slot move_from[b] to move_to[b] for every head of row b where move_from[b] >= 0.
+ * Device-side indices out of range set the error word and skip the access.
+ * ---------------------------------------------------------------------------------- */
+int fb_spec_propose(const int64_t* history, int64_t size, const int64_t* position, const int64_t* successor,
+                    int64_t vocab, int top, const int64_t* stale, int64_t* tokens, int64_t* chains,
+                    int64_t* phases, int batch, int tokens_per_row, int d0, int d1, int d2, int d3,
+                    int maxlen, void* stream);
+int fb_spec_within_margin(const void* logits, int64_t vocab, const int64_t* tokens, const float* top,
+                          int64_t* within, int batch, int count, float margin, void* stream);
+int fb_spec_settle(const int64_t* tokens, const int64_t* greedy, const int64_t* within, int64_t* position,
+                   const int64_t* limit, int64_t* history, int64_t size, int64_t* result,
+                   int64_t* move_from, int64_t* move_to, const int64_t* chains, int64_t* stale, int batch,
+                   int count, void* stream);
+int fb_spec_relocate(void* store, int planes, int batch, int kv_heads, int capacity, int head_dim,
+                     const int64_t* move_from, const int64_t* move_to, void* stream);
+
+/* ------------------------------------------------------------------------------------
  * Tensor-parallel projection + all-reduce over NVLink peer memory (no counterpart in the
  * reference, which is single-GPU; this replaces an NCCL all-reduce after o_proj/down_proj).
  * Low-latency protocol: every value travels as one 8-byte word, low half the fp32 bits,

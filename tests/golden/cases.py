@@ -233,3 +233,79 @@ def tiny_qwen3_weights(seed=90):
 def model_prompt(case):
     name, batch, prompt, steps, seed = case
     return torch.randint(3, TINY_QWEN3["vocab_size"], (batch, prompt), generator=_gen(seed)), steps
+
+
+# ---------------------------------------------------------------- speculation bookkeeping
+# (name, batch, size, tokens per row, drafts by match length, successor width, vocab, seed)
+SPEC_CASES = [
+    ("p1", 4, 64, 8, (2, 4, 6, 7), 8, 5, 101),       # tiny vocabulary: long suffix matches
+    ("p2", 3, 200, 16, (5, 8, 13, 14), 8, 12, 102),
+    ("p3", 2, 40, 5, (2, 3, 4, 4), 4, 7, 103),
+    ("p4", 5, 300, 2, (1, 1, 1, 1), 8, 30, 104),     # no alternative lanes
+    ("p5", 2, 130, 16, (15, 15, 15, 15), 8, 9, 105),  # chain only, no alternatives
+    ("p6", 16, 2048, 16, (5, 8, 13, 14), 8, 50, 106),
+]
+
+
+def spec_inputs(case):
+    """History, position, successor table, stale hints and a greedy pass for one case.
+
+    Histories repeat short motifs so that suffix matches of every length occur; positions
+    leave room for a settle to write TOKENS slots; the greedy tokens agree with a random
+    number of chain drafts (planted after propose, see spec_greedy)."""
+    name, batch, size, tokens, drafts, top, vocab, seed = case
+    g = _gen(seed)
+    motif = torch.randint(0, vocab, (max(3, size // 7),), generator=g)
+    history = torch.empty(batch, size, dtype=torch.int64)
+    for b in range(batch):
+        pieces, n = [], 0
+        while n < size:
+            if torch.rand((), generator=g) < 0.5:
+                start = int(torch.randint(0, motif.numel(), (), generator=g))
+                piece = motif[start:start + int(torch.randint(1, 9, (), generator=g))]
+            else:
+                piece = torch.randint(0, vocab, (int(torch.randint(1, 5, (), generator=g)),), generator=g)
+            pieces.append(piece)
+            n += piece.numel()
+        history[b] = torch.cat(pieces)[:size]
+    position = torch.randint(0, size - tokens - 1, (batch,), generator=g)
+    position[0] = size - tokens - 1  # the latest possible place
+    successor = torch.randint(0, vocab, (vocab, top), generator=g)
+    stale = torch.randint(-1, vocab, (batch,), generator=g)
+    limit = position + torch.randint(0, tokens + 3, (batch,), generator=g)
+    return {"history": history, "position": position, "successor": successor, "stale": stale, "limit": limit,
+            "tokens": tokens, "drafts": drafts, "vocab": vocab, "seed": seed}
+
+
+def spec_greedy(proposed, chains, vocab, seed):
+    """A verify pass's greedy tokens for proposed rows: each row accepts a random number of
+    its chain drafts (greedy[slot] = draft[slot + 1]); some rows put an alternative lane's
+    token first (the branch path)."""
+    g = _gen(seed + 1000)
+    batch, tokens = proposed.shape
+    greedy = torch.randint(0, vocab, (batch, tokens), generator=g)
+    for b in range(batch):
+        chain = int(chains[b])
+        keep = int(torch.randint(0, chain, (), generator=g))
+        for slot in range(keep):
+            greedy[b, slot] = proposed[b, slot + 1]
+        if keep == 0 and chain < tokens and torch.rand((), generator=g) < 0.5:
+            greedy[b, 0] = proposed[b, int(torch.randint(chain, tokens, (), generator=g))]
+    return greedy
+
+
+def spec_margin_inputs(case, proposed):
+    """Logits [B*T, V] (bf16), their per-row maxima as fp32 and a margin for within_margin."""
+    name, batch, size, tokens, drafts, top, vocab, seed = case
+    g = _gen(seed + 2000)
+    logits = (torch.randn(batch * tokens, vocab, generator=g) * 2).bfloat16()
+    best = logits.float().max(-1).values
+    return logits, best, 0.75
+
+
+def relocate_inputs(seed=110):
+    g = _gen(seed)
+    store = torch.randn(2, 3, 4, 2, 40, 64, generator=g).bfloat16()
+    move_from = torch.tensor([5, -1, 39, 12], dtype=torch.int64)
+    move_to = torch.tensor([3, 7, 30, 13], dtype=torch.int64)
+    return store, move_from, move_to

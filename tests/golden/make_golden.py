@@ -174,6 +174,43 @@ def main():
             print("pointwise", flush=True)
             out["pointwise"] = fixtures
 
+        if want("spec"):
+            # The reference's speculation bookkeeping (engine/kernels/spec.py): propose,
+            # within_margin, settle (exact and relaxed) and relocate, through the shim's
+            # restatements (check_tree.py's emulation for _propose).
+            from kernels import spec as ref_spec
+            fixtures = {}
+            for case in cases.SPEC_CASES:
+                x = cases.spec_inputs(case)
+                batch, tokens_per_row = x["history"].shape[0], x["tokens"]
+                chains = torch.empty(batch, dtype=torch.int64)
+                phases = torch.empty(batch, tokens_per_row, dtype=torch.int64)
+                proposed = ref_spec.propose(x["history"], x["position"], tokens_per_row, x["drafts"], x["successor"],
+                                            x["stale"], chains, phases)
+                greedy = cases.spec_greedy(proposed, chains, x["vocab"], x["seed"])
+                logits, top, margin = cases.spec_margin_inputs(case, proposed)
+                within = ref_spec.within_margin(logits, proposed, top, margin)
+                entry = {"digest": cases.digest(x["history"], x["position"], x["successor"], x["stale"], x["limit"]),
+                         "tokens": proposed.clone(), "chains": chains.clone(), "phases": phases.clone(),
+                         "greedy": greedy.clone(), "within": within[:, 1:].clone()}
+                for relaxed in (False, True):
+                    history, position, stale = x["history"].clone(), x["position"].clone(), x["stale"].clone()
+                    result = torch.empty(batch, tokens_per_row + 1, dtype=torch.int64)
+                    move_from = torch.empty(batch, dtype=torch.int64)
+                    move_to = torch.empty(batch, dtype=torch.int64)
+                    ref_spec.settle(proposed, greedy, position, x["limit"], history, result, move_from, move_to, chains,
+                                    stale, within=within if relaxed else None)
+                    entry["settle_relaxed" if relaxed else "settle"] = {
+                        "result": result.clone(), "history": history.clone(), "move_from": move_from.clone(),
+                        "move_to": move_to.clone(), "position": position.clone(), "stale": stale.clone()}
+                fixtures[case[0]] = entry
+                print("spec", case[0], flush=True)
+            store, move_from, move_to = cases.relocate_inputs()
+            moved = store.clone()
+            ref_spec.relocate(moved, move_from, move_to)
+            fixtures["relocate"] = {"digest": cases.digest(store, move_from, move_to), "store": moved}
+            out["spec"] = fixtures
+
         if want("model"):
             from transformers import Qwen3Config, Qwen3ForCausalLM
             import decode as ref_decode
