@@ -22,7 +22,7 @@
 //    K = 128 tokens) with V read in place as an MN-major operand; each thread (one dim)
 //    folds the tile into its fp32 running output with the softmax correction.
 //  * Every mbarrier wait is bounded; TMEM is freed on every path.
-#include "common.cuh"
+#include "tcgen05.cuh"
 
 namespace fb {
 namespace verify {
@@ -49,61 +49,11 @@ struct Params {
   unsigned* err;
 };
 
-// ---- tcgen05 helpers --------------------------------------------------------------------
-__device__ __forceinline__ uint64_t umma_desc(uint32_t smem_addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
-  // sm_100 shared-memory matrix descriptor: start>>4 [0,14), LBO>>4 [16,30), SBO>>4 [32,46),
-  // version 1 [46,48), base offset 0, layout SWIZZLE_128B (2) [61,64).
-  uint64_t d = 0;
-  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
-  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
-  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
-  d |= static_cast<uint64_t>(1) << 46;
-  d |= static_cast<uint64_t>(2) << 61;
-  return d;
-}
-
-// kind::f16 instruction descriptor: bf16 x bf16 -> fp32, M = 128, N = kMembers.
-__host__ __device__ constexpr uint32_t idesc_bf16(bool a_mn_major) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn_major ? 1u : 0u) << 15) |
-         (static_cast<uint32_t>(kMembers >> 3) << 17) | (static_cast<uint32_t>(kTile >> 4) << 24);
-}
-
-__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                          uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   smem_u32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// 2^x with the PTX approximate base-2 exponential (what the reference's tl.exp2 lowers to);
-// -inf gives +0.
-__device__ __forceinline__ float ex2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[kHalf]) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
+// UMMA shapes: S^T = K * Q^T (M = 128 tokens, N = 32 members, A K-major) and
+// O^T = V^T * P^T (M = 128 dims, N = 32 members, A = V read MN-major).
+constexpr uint32_t kIdescS = tc::idesc_bf16(kTile, kMembers, false, false);
+constexpr uint32_t kIdescO = tc::idesc_bf16(kTile, kMembers, true, false);
+using tc::ex2_approx;
 
 // Column-wise reduction of a 32x16 block held one row per lane: afterwards lanes c and c+16
 // hold the reduction of column c over all 32 rows (shuffle transpose-reduce, 16 shuffles).
@@ -227,9 +177,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     col_max[tid] = -INFINITY;
   }
   fence_proxy_async_smem();
-  tc_fence_before();
+  tc::fence_before();
   __syncthreads();
-  tc_fence_after();
+  tc::fence_after();
   const uint32_t tmem = *tmem_slot;
   // S^T[x] = columns [32x, 32x + 32); O^T[x] = columns [64 + 32x, 96 + 32x)
 
@@ -260,23 +210,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     // S(i+1) while the softmax warps work on tile i.
     if (lane == 0) {
       const uint32_t q_addr = smem_u32(q_s), p_addr = smem_u32(p_s);
-      const uint32_t idesc_s = idesc_bf16(false), idesc_o = idesc_bf16(true);
+      const uint32_t idesc_s = kIdescS, idesc_o = kIdescO;
       auto issue_o = [&](int j) -> bool {
         const int x = j & 1;
         if (!mbar_wait_bounded(&p_full[x], (j >> 1) & 1)) return false;
         if (j >= 2 && !mbar_wait_bounded(&o_free[x], ((j - 2) >> 1) & 1)) return false;
-        tc_fence_after();
+        tc::fence_after();
         const uint32_t v_addr = smem_u32(stages + (j % kStages) * Smem::kStageBytes + Smem::kTileBytes);
         const uint32_t pb = p_addr + x * Smem::kPBytes;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off_v = kk * 16 * 128;  // 16 tokens = two 8-row groups
           const uint32_t off_p = (kk >> 2) * (kMembers * 128) + (kk & 3) * 32;
-          umma_bf16(tmem + 64 + 32 * x, umma_desc(v_addr + off_v, kTile * 128, 1024), umma_desc(pb + off_p, 16, 1024),
+          tc::mma_bf16(tmem + 64 + 32 * x, tc::desc_sw128(v_addr + off_v, kTile * 128, 1024), tc::desc_sw128(pb + off_p, 16, 1024),
                     idesc_o, kk > 0 ? 1u : 0u);
         }
-        umma_commit(&o_full[x]);
-        umma_commit(&empty[j % kStages]);  // both products of tile j read their K/V stage
+        tc::commit(&o_full[x]);
+        tc::commit(&empty[j % kStages]);  // both products of tile j read their K/V stage
         return true;
       };
       bool ok = true;
@@ -285,16 +235,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = mbar_wait_bounded(&full[st], (i / kStages) & 1) &&
              (i < 2 || mbar_wait_bounded(&s_free[x], ((i - 2) >> 1) & 1));
         if (!ok || *abort_flag) break;
-        tc_fence_after();
+        tc::fence_after();
         const uint32_t k_addr = smem_u32(stages + st * Smem::kStageBytes);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off_k = (kk >> 2) * (kTile * 128) + (kk & 3) * 32;
           const uint32_t off_q = (kk >> 2) * (kMembers * 128) + (kk & 3) * 32;
-          umma_bf16(tmem + 32 * x, umma_desc(k_addr + off_k, 16, 1024), umma_desc(q_addr + off_q, 16, 1024), idesc_s,
+          tc::mma_bf16(tmem + 32 * x, tc::desc_sw128(k_addr + off_k, 16, 1024), tc::desc_sw128(q_addr + off_q, 16, 1024), idesc_s,
                     kk > 0 ? 1u : 0u);
         }
-        umma_commit(&s_full[x]);
+        tc::commit(&s_full[x]);
         if (i >= 1) ok = issue_o(i - 1);
       }
       if (ok && tiles >= 1 && !*abort_flag) ok = issue_o(tiles - 1);
@@ -303,7 +253,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         *abort_flag = 1;
       }
       // every UMMA issued above has completed before TMEM can be freed
-      umma_commit(done);
+      tc::commit(done);
       if (!mbar_wait_bounded(done, 0)) raise_error(p.err, kErrTimeoutDrain);
     }
     __syncwarp();
@@ -326,10 +276,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto fold = [&](int j) -> bool {
       const int x = j & 1;
       if (!mbar_wait_bounded(&o_full[x], (j >> 1) & 1)) return false;
-      tc_fence_after();
+      tc::fence_after();
       float ot[kHalf];
-      tmem_ld16(tmem + 64 + 32 * x + col0 + lane_base, ot);
-      tc_fence_before();
+      tc::ld16(tmem + 64 + 32 * x + col0 + lane_base, ot);
+      tc::fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&o_free[x]);
 #pragma unroll
@@ -343,10 +293,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = false;
         break;
       }
-      tc_fence_after();
+      tc::fence_after();
       float sc[kHalf];
-      tmem_ld16(tmem + 32 * x + col0 + lane_base, sc);
-      tc_fence_before();
+      tc::ld16(tmem + 32 * x + col0 + lane_base, sc);
+      tc::fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[x]);
       const long long tile0 = begin + static_cast<long long>(i) * kTile;
@@ -462,10 +412,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   // ---- teardown: the MMA lane saw every UMMA complete and every TMEM read has waited ----
-  tc_fence_before();
+  tc::fence_before();
   __syncthreads();
   if (warp == kMmaWarp) {
-    tc_fence_after();
+    tc::fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
   }
 }

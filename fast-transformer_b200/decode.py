@@ -6,8 +6,9 @@ The structure follows the reference engine (engine/decode.py): one graph-stable 
 (:216-278) - embed+norm, per layer add+norm, packed QKV projection, fused QK-norm/RoPE/KV
 append, split-KV decode attention, o_proj, add+norm, packed gate/up, SwiGLU, down_proj -
 then the final norm, LM head and argmax, and a device-side `position += 1`. Prefill runs
-eagerly through cuBLAS and torch SDPA for the big GEMMs and prompt attention (as the
-reference's prefill does, engine/layers.py:69-74), with the fused kernel writing the cache.
+eagerly: cuBLAS for the big GEMMs (as the reference's prefill does, engine/layers.py:69-74),
+the tcgen05 causal flash kernel (fb_prefill_attention) for the prompt attention, and the
+fused kernel writing the cache.
 
 Tensor parallelism (by KV head, see qwen3.py): o_proj and down_proj run as
 fb_linear_allreduce_push, which stores every finished fp32 output value straight into each
@@ -27,6 +28,7 @@ import torch.nn.functional as F
 
 from kernels import _native
 from kernels.argmax import argmax, fused_argmax
+from kernels.prefill import prefill_attention
 from kernels.decode_attention import attend as attend_decode
 from kernels import linear as klinear
 from kernels.linear import linear, swiglu_linear
@@ -315,10 +317,8 @@ class DecodeState:
                 packed = F.linear(normalized, layer.qkv)
                 query = qk_rope_cache(packed, _Norm(layer.q_norm, eps), _Norm(layer.k_norm, eps), cos, sin,
                                       positions, keys, values, w.q_heads, prefill=True)
-                attention = F.scaled_dot_product_attention(
-                    query, keys[:, :, :length], values[:, :, :length], is_causal=True, scale=self.scale,
-                    enable_gqa=True)
-                attention = attention.transpose(1, 2).reshape(1, length, -1)
+                attention = prefill_attention(query, keys[:, :, :length], values[:, :, :length], self.scale)
+                attention = attention.reshape(1, length, -1)
                 out = comm.all_reduce(F.linear(attention, layer.o))
                 normalized, residual = add_rms_norm(out, residual, layer.ln2, eps)
                 gate, up = qwen3.split_gate_up(layer.gate_up)

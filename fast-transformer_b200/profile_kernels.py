@@ -3,6 +3,7 @@
     python fast-transformer_b200/profile_kernels.py attention --batch 16 --length 8320
     python fast-transformer_b200/profile_kernels.py linear --m 16 --n 24576 --k 4096 --epilogue 2
     python fast-transformer_b200/profile_kernels.py verify --batch 8 --tokens 5 --length 4101
+    python fast-transformer_b200/profile_kernels.py prefill --batch 1 --length 8192
     python fast-transformer_b200/profile_kernels.py step --preset qwen3-8b --batch 16 --length 8192
 
 Each mode warms up, then runs the measured launches inside the NVTX range "profiled", so
@@ -113,6 +114,29 @@ def verify(args):
     torch.cuda.synchronize()
 
 
+def prefill(args):
+    """One config-4 prompt row: causal GQA attention over --length tokens, ours vs torch SDPA
+    (the reference's own call, library Flash attention) for comparison."""
+    from kernels.prefill import prefill_attention
+    b, hq, hkv, d, n = args.batch, args.q_heads, args.kv_heads, 128, args.length
+    q = torch.randn(b, hq, n, d, device="cuda").bfloat16()
+    k = torch.randn(b, hkv, n, d, device="cuda").bfloat16()
+    v = torch.randn(b, hkv, n, d, device="cuda").bfloat16()
+    scale = 1 / math.sqrt(d)
+    flops = 4 * b * hq * d * n * (n + 1) / 2  # causal: QK^T and PV over the lower triangle
+    ms = graph_time(lambda: prefill_attention(q, k, v, scale))
+    ms_ref = graph_time(lambda: torch.nn.functional.scaled_dot_product_attention(
+        q, k, v, is_causal=True, scale=scale, enable_gqa=True))
+    print(f"prefill B={b} Hq={hq} Hkv={hkv} T={n}: {ms * 1e3:.1f} us, {flops / ms / 1e9:.1f} TFLOP/s "
+          f"(torch SDPA {ms_ref * 1e3:.1f} us, {flops / ms_ref / 1e9:.1f} TFLOP/s)")
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("profiled")
+    for _ in range(args.launches):
+        prefill_attention(q, k, v, scale)
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+
+
 def step(args):
     import decode as fdecode
     import qwen3
@@ -156,7 +180,7 @@ def step(args):
 
 def main():
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    parser.add_argument("mode", choices=("attention", "linear", "verify", "step"))
+    parser.add_argument("mode", choices=("attention", "linear", "verify", "prefill", "step"))
     parser.add_argument("--batch", type=int, default=16)
     parser.add_argument("--q-heads", type=int, default=32)
     parser.add_argument("--kv-heads", type=int, default=8)
@@ -172,7 +196,7 @@ def main():
     parser.add_argument("--copies", type=int, default=2)
     parser.add_argument("--launches", type=int, default=2)
     args = parser.parse_args()
-    {"attention": attention, "linear": linear, "verify": verify, "step": step}[args.mode](args)
+    {"attention": attention, "linear": linear, "verify": verify, "prefill": prefill, "step": step}[args.mode](args)
 
 
 if __name__ == "__main__":

@@ -230,6 +230,18 @@ int fb_argmax_candidates(const void* cand, int rows, int tiles, int world, int r
                          int64_t* out, float* top, void* stream);
 
 /* ------------------------------------------------------------------------------------
+ * Causal GQA prefill attention (flash attention forward, tcgen05): replaces the reference's
+ * prefill path engine/attention.py:8-21 (`grouped_sdpa` without a mask: torch SDPA Flash,
+ * is_causal, enable_gqa).
+ *   q   bf16 [B, Hq, T, D] contiguous (head-major), D = 64 or 128
+ *   k,v bf16 [B, Hkv, C, D] (the KV cache; slots [0, T) hold the prompt), C >= T
+ *   out bf16 [B, T, Hq, D]: token t of head hq attends keys [0, t] of KV head hq / (Hq/Hkv)
+ * fp32 scores and accumulation, P rounded to bf16 for the value product.
+ * ---------------------------------------------------------------------------------- */
+int fb_prefill_attention(const void* q, const void* k, const void* v, void* out, int batch, int tokens,
+                         int q_heads, int kv_heads, int head_dim, int capacity, float scale, void* stream);
+
+/* ------------------------------------------------------------------------------------
  * Speculation bookkeeping (exact speculative decoding): replaces engine/kernels/spec.py's
  * fused programs with the same semantics. All int64 unless noted; one launch each.
  * fb_spec_propose (spec.py:16-124 `_propose`, wrapper `propose` :106-124): per row of
