@@ -20,6 +20,7 @@ struct Params {
   const float* partials;  // [splits, m, n]
   int splits, m, n, world, rank, use;
   uint64_t* peer_recv[kMaxWorld];
+  uint64_t* mc_recv;  // multicast address of the receive buffers (NVSwitch), or null
   const int64_t* epoch;
 };
 
@@ -50,9 +51,15 @@ __global__ void __launch_bounds__(kThreads) reduce_push_kernel(const __grid_cons
   const uint64_t flag = static_cast<uint64_t>(static_cast<uint32_t>(*p.epoch) + 1u) << 32;
   const uint64_t w0 = flag | __float_as_uint(x.x), w1 = flag | __float_as_uint(x.y);
   const size_t off = (static_cast<size_t>(p.use) * p.world + p.rank) * count + i;
-  for (int q = 0; q < p.world; ++q)
-    asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p.peer_recv[q] + off), "l"(w0), "l"(w1)
-                 : "memory");
+  if (p.mc_recv != nullptr) {
+    // one store per word through the multicast address: NVSwitch delivers it to every rank
+    asm volatile("multimem.st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p.mc_recv + off), "l"(w0) : "memory");
+    asm volatile("multimem.st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p.mc_recv + off + 1), "l"(w1) : "memory");
+  } else {
+    for (int q = 0; q < p.world; ++q)
+      asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p.peer_recv[q] + off), "l"(w0), "l"(w1)
+                   : "memory");
+  }
 }
 
 }  // namespace ar
@@ -61,7 +68,7 @@ __global__ void __launch_bounds__(kThreads) reduce_push_kernel(const __grid_cons
 using namespace fb;
 
 extern "C" int fb_reduce_push(const void* partials, int splits, int m, int n, int world, int rank, int use,
-                              void* const* peer_recv, const int64_t* epoch, void* stream) {
+                              void* const* peer_recv, void* multicast_recv, const int64_t* epoch, void* stream) {
   if (!partials || !peer_recv || !epoch || splits <= 0 || m <= 0 || n <= 0) return FB_ERR_ARG;
   if (world < 1 || world > ar::kMaxWorld || rank < 0 || rank >= world || use < 0) return FB_ERR_ARG;
   if (n % 2 != 0) return FB_ERR_SHAPE;
@@ -74,6 +81,8 @@ extern "C" int fb_reduce_push(const void* partials, int splits, int m, int n, in
   p.rank = rank;
   p.use = use;
   p.epoch = epoch;
+  if (multicast_recv != nullptr && (reinterpret_cast<uintptr_t>(multicast_recv) & 15u)) return FB_ERR_ARG;
+  p.mc_recv = static_cast<uint64_t*>(multicast_recv);
   for (int r = 0; r < world; ++r) {
     if (!peer_recv[r] || (reinterpret_cast<uintptr_t>(peer_recv[r]) & 15u)) return FB_ERR_ARG;
     p.peer_recv[r] = static_cast<uint64_t*>(peer_recv[r]);

@@ -44,6 +44,7 @@ struct Params {
   int world, rank, use;
   long long index_base;  // kArgmax: vocabulary index of column 0
   uint64_t* peer_recv[kMaxPeers];
+  uint64_t* mc_recv;     // multicast address of the receive buffers (NVSwitch), or null
   const int64_t* epoch;  // the word's flag is (uint32)(*epoch) + 1
   unsigned* err;
 };
@@ -142,9 +143,15 @@ __device__ void epilogue(const Params& p, const float* vals, int tile, int tid, 
       const size_t off = (static_cast<size_t>(p.use) * p.world + p.rank) * slab + static_cast<size_t>(m) * p.n +
                          n0 + c2 * 2;
       const uint64_t w0 = flag | __float_as_uint(v.x), w1 = flag | __float_as_uint(v.y);
-      for (int q = 0; q < p.world; ++q)
-        asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p.peer_recv[q] + off), "l"(w0), "l"(w1)
-                     : "memory");
+      if (p.mc_recv != nullptr) {
+        // one store per word through the multicast address: NVSwitch delivers it to every rank
+        asm volatile("multimem.st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p.mc_recv + off), "l"(w0) : "memory");
+        asm volatile("multimem.st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p.mc_recv + off + 1), "l"(w1) : "memory");
+      } else {
+        for (int q = 0; q < p.world; ++q)
+          asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p.peer_recv[q] + off), "l"(w0), "l"(w1)
+                       : "memory");
+      }
     }
     return;
   }
@@ -412,7 +419,7 @@ extern "C" int fb_linear_splits(int m, int n, int k) {
 
 static int linear_impl(const void* x, const void* w, void* out, int m, int n, int k, int epilogue, int splits,
                        void* stream, int world, int rank, int use, void* const* peer_recv,
-                       const int64_t* epoch, int64_t index_base = 0) {
+                       const int64_t* epoch, int64_t index_base = 0, void* multicast_recv = nullptr) {
   if (!x || !w || !out || m <= 0 || n <= 0 || k <= 0 || splits <= 0) return FB_ERR_ARG;
   if (m > 64 || k % 8 != 0 || n % 8 != 0) return FB_ERR_SHAPE;
   if ((n + lin::kTileN - 1) / lin::kTileN > lin::kMaxTiles) return FB_ERR_SHAPE;
@@ -439,6 +446,7 @@ static int linear_impl(const void* x, const void* w, void* out, int m, int n, in
   p.index_base = index_base;
   if (epilogue == lin::kPush) {  // only the push form has peer buffers
     for (int r = 0; r < world && r < lin::kMaxPeers; ++r) p.peer_recv[r] = static_cast<uint64_t*>(peer_recv[r]);
+    p.mc_recv = static_cast<uint64_t*>(multicast_recv);
     p.epoch = epoch;
   }
   p.err = error_word();
@@ -466,13 +474,14 @@ extern "C" int fb_linear_argmax(const void* x, const void* w, int m, int n, int 
 }
 
 extern "C" int fb_linear_allreduce_push(const void* x, const void* w, int m, int n, int k, int splits, int world,
-                                        int rank, int use, void* const* peer_recv, const int64_t* epoch,
-                                        void* stream) {
+                                        int rank, int use, void* const* peer_recv, void* multicast_recv,
+                                        const int64_t* epoch, void* stream) {
   if (world < 1 || world > lin::kMaxPeers || rank < 0 || rank >= world || use < 0) return FB_ERR_ARG;
   if (!peer_recv || !epoch) return FB_ERR_ARG;
   for (int r = 0; r < world; ++r)
     if (!peer_recv[r] || (reinterpret_cast<uintptr_t>(peer_recv[r]) & 15u)) return FB_ERR_ARG;
   // the kernel writes nothing through `out` in this mode; pass a valid dummy
+  if (multicast_recv != nullptr && (reinterpret_cast<uintptr_t>(multicast_recv) & 15u)) return FB_ERR_ARG;
   return linear_impl(x, w, const_cast<void*>(x), m, n, k, lin::kPush, splits, stream, world, rank, use, peer_recv,
-                     epoch);
+                     epoch, 0, multicast_recv);
 }

@@ -89,12 +89,16 @@ class Communicator:
 class PeerBuffers:
     """Receive slabs in torch symmetric memory, uint64 words [uses, world, rows, width] (fp32
     bits + a 32-bit flag per value: the low-latency push protocol), with every rank's base
-    address for NVLink peer stores."""
+    address for NVLink peer stores and, where the driver binds the buffers to an NVSwitch
+    multicast object, its multicast address (one store reaches every rank).
+
+    FB_TP_MULTICAST=0 keeps plain peer mappings only (no multicast object), e.g. for runs that
+    may lose a rank: a rank that dies while bound to a multicast object can fault its peers."""
 
     def __init__(self, comm, uses, rows, width, device):
         import os
-        # Plain peer mappings only: no NVLink multicast object behind these buffers.
-        os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
+        if os.environ.get("FB_TP_MULTICAST", "1") == "0":
+            os.environ["TORCH_SYMM_MEM_DISABLE_MULTICAST"] = "1"
         import torch.distributed._symmetric_memory as symm_mem
         world = comm.size
         self.uses, self.world, self.rows, self.width = uses, world, rows, width
@@ -110,8 +114,10 @@ class PeerBuffers:
         self.buf = symm_mem.empty(total, dtype=torch.uint8, device=device)
         handle = symm_mem.rendezvous(self.buf, self.group)
         self.handle = handle
-        # a multicast object would show as a non-zero multicast address
-        self.multicast = bool(int(getattr(handle, "multicast_ptr", 0) or 0))
+        # a multicast object shows as a non-zero multicast address
+        mc = int(getattr(handle, "multicast_ptr", 0) or 0)
+        self.multicast = mc != 0
+        self.mc_ptr = ctypes.c_void_p(mc) if mc else None
         self.recv_ptrs = (ctypes.c_void_p * world)(*[int(b) for b in handle.buffer_ptrs])
         self.recv_local = ctypes.c_void_p(self.buf.data_ptr())
         self.exchange_ptrs = (ctypes.c_void_p * world)(*[int(b) + self.recv_bytes for b in handle.buffer_ptrs])
@@ -156,12 +162,13 @@ def _push_projection(x, weight, comm, peers, use, epoch):
     n, k = weight.shape
     if (k + 63) // 64 <= PUSH_SINGLE_SPLIT_CHUNKS:
         check(lib.fb_linear_allreduce_push(ptr(flat), ptr(weight), rows, n, k, 1, comm.size, comm.rank, use,
-                                           peers.recv_ptrs, ptr(epoch), stream()), "fb_linear_allreduce_push")
+                                           peers.recv_ptrs, peers.mc_ptr, ptr(epoch), stream()),
+              "fb_linear_allreduce_push")
         return
     splits = min(klinear.splits_for(rows, n, k, x.device), klinear.MAX_CLUSTER_SPLITS)
     partials = klinear.project(flat, weight, klinear.SPLITS_OUT, splits)
-    check(lib.fb_reduce_push(ptr(partials), splits, rows, n, comm.size, comm.rank, use, peers.recv_ptrs, ptr(epoch),
-                             stream()), "fb_reduce_push")
+    check(lib.fb_reduce_push(ptr(partials), splits, rows, n, comm.size, comm.rank, use, peers.recv_ptrs, peers.mc_ptr,
+                             ptr(epoch), stream()), "fb_reduce_push")
 
 
 def _reduce_add_norm(peers, use, epoch, residual, weight, eps):

@@ -284,7 +284,10 @@ int fb_spec_relocate(void* store, int planes, int batch, int kv_heads, int capac
  * *epoch must differ between two calls with the same `use` and stay below 2^31.
  * Producer: fb_linear_allreduce_push computes this rank's fp32 partial of y = x @ W^T
  *   (splits <= 8 K-splits summed in one thread-block cluster) and stores every value into
- *   slab `rank` of recv[use] on every rank (peer_recv[r] = rank r's recv base).
+ *   slab `rank` of recv[use] on every rank (peer_recv[r] = rank r's recv base). When
+ *   multicast_recv is not NULL it is the NVSwitch multicast address of the same buffers
+ *   (every rank's recv bound to one multicast object): each word is stored once through it
+ *   (multimem.st) instead of once per peer.
  * Consumer: fb_allreduce_add_rmsnorm polls (bounded, 2 s) this rank's recv[use] until
  *   every word of the world slabs carries the flag, sums the slabs in rank order (the same
  *   bits on every rank), rounds to bf16 and applies add_rms_norm (fb_add_rmsnorm's
@@ -292,12 +295,12 @@ int fb_spec_relocate(void* store, int planes, int batch, int kv_heads, int capac
  *   rank.
  * ---------------------------------------------------------------------------------- */
 int fb_linear_allreduce_push(const void* x, const void* w, int m, int n, int k, int splits, int world,
-                             int rank, int use, void* const* peer_recv, const int64_t* epoch,
-                             void* stream);
+                             int rank, int use, void* const* peer_recv, void* multicast_recv,
+                             const int64_t* epoch, void* stream);
 /* The producer's split-K form: sums fp32 partials [splits, M, N] in split order and pushes
  * every value like fb_linear_allreduce_push (same recv layout and flags); N % 2 == 0. */
 int fb_reduce_push(const void* partials, int splits, int m, int n, int world, int rank, int use,
-                   void* const* peer_recv, const int64_t* epoch, void* stream);
+                   void* const* peer_recv, void* multicast_recv, const int64_t* epoch, void* stream);
 int fb_allreduce_add_rmsnorm(const void* recv, int use, int world, const int64_t* epoch,
                              const void* residual, const void* w, void* out, void* sum, int rows,
                              int width, float eps, void* stream);

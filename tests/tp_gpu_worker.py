@@ -55,7 +55,8 @@ def main():
         comm0 = fdecode.Communicator(dist.group.WORLD, world, rank)
         push_checks = check_push_forms(comm0, device, rank, world)
         if rank == 0:
-            print("push forms", push_checks, flush=True)
+            print("push forms", push_checks, "multicast" if os.environ.get("FB_TP_MULTICAST", "1") != "0" else "peer stores",
+                  flush=True)
         ok = all(push_checks.values())
         fx = torch.load(os.path.join(HERE, "golden", "model.pt"), weights_only=False)
         cfg = qwen3.Config.make(**cases.TINY_QWEN3)
@@ -88,7 +89,10 @@ def main():
                 "ranks agree": all(torch.equal(t, gathered[0]) for t in gathered),
                 "logits": bool(err <= 2e-2 * scale),
             }
-            checks["no multicast"] = not graph_state.peers.multicast
+            if os.environ.get("FB_TP_MULTICAST", "1") == "0":
+                checks["no multicast"] = not graph_state.peers.multicast
+            else:
+                checks["multicast used"] = graph_state.peers.multicast
             if rank == 0:
                 print(case[0], checks, flush=True)
             ok = ok and all(checks.values())
