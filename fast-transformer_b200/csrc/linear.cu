@@ -177,7 +177,6 @@ __global__ void __launch_bounds__(kThreads)
     linear_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
                   const __grid_constant__ Params p) {
   using S = Smem<MT>;
-  constexpr int MP = S::MP;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));

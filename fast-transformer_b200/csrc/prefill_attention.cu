@@ -12,10 +12,12 @@
 //  * A UMMA lane issues S = Q K^T (M = 128 queries, N = 128 keys, K = D) into one of two TMEM
 //    buffers and O += P V (N = 128 dims, K = 128 keys; V read MN-major) into a TMEM
 //    accumulator; S of tile j+1 runs while the softmax warps work on tile j.
-//  * Four softmax warps, one thread per query row: row max, P = 2^(s - m) rounded to bf16 into
-//    a K-major swizzled tile in shared memory (double-buffered), row sum. The pivot m only
-//    moves when a row's max grows by more than 8 (P <= 2^8 otherwise); then the row's O in
-//    TMEM is rescaled in place after the previous product completes.
+//  * Eight softmax warps, two per query row (64 keys each, exchanging row maxima and sums
+//    through spare TMEM columns): row max, P = 2^(s - m) rounded to bf16 into a K-major
+//    swizzled tile in shared memory (double-buffered), row sum. The pivot m only moves when a
+//    row's max grows by more than 8 (P <= 2^8 otherwise); then the row's O in TMEM is
+//    rescaled in place after the previous product completes. Tiles below the diagonal skip
+//    the masks.
 //  * Every mbarrier wait is bounded; TMEM is freed on every path.
 #include "tcgen05.cuh"
 
@@ -23,11 +25,13 @@ namespace fb {
 namespace prefill {
 
 constexpr int kTile = 128;      // queries per CTA tile and keys per K/V tile
-constexpr int kSoftmaxWarps = 4;
-constexpr int kProducerWarp = 4;
-constexpr int kMmaWarp = 5;
-constexpr int kThreads = 6 * 32;
-constexpr int kTmemCols = 512;  // S double buffer (2 x 128) + O (128)
+constexpr int kSoftmaxWarps = 8;  // warp w: query rows 32*(w%4).., key half / O-column half w/4
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int kThreads = 10 * 32;
+constexpr int kTmemCols = 512;  // S double buffer (2 x 128) + O (<= 128) + row exchange columns
+constexpr int kTmemO = 256;
+constexpr int kTmemXchg = 384;  // [parity][half] row maxima, then [half] row sums
 constexpr float kRescaleAbove = 8.0f;  // log2 units
 
 struct Params {
@@ -93,7 +97,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&empty[x], 1);
       mbar_init(&s_full[x], 1);
       mbar_init(&s_free[x], kSoftmaxWarps);
-      mbar_init(&p_full[x], kSoftmaxWarps);
+      mbar_init(&p_full[x], kSoftmaxWarps);  // eight softmax warps arrive on each
       mbar_init(&o_done[x], 1);
     }
     mbar_init(q_full, 1);
@@ -113,7 +117,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc::fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tmem_o = tmem + 256;
+  const uint32_t tmem_o = tmem + kTmemO;
 
   if (warp == kProducerWarp) {
     // ============================ TMA producer ============================
@@ -189,13 +193,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ============================ softmax warps ============================
-    const int row = warp * 32 + lane;  // query row of the tile = TMEM lane
-    const int t = qt * kTile + row;    // its token
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    // Warp w reads TMEM lanes 32*(w%4).. (its query rows) and key columns [64h, 64h + 64) of S,
+    // h = w / 4, and owns O columns [h*D/2, (h+1)*D/2). The two warps of a row exchange their
+    // partial row maxima (and, at the end, row sums) through spare TMEM columns and a named
+    // barrier per warp pair; both then take identical pivot decisions. Control flow stays
+    // warp-uniform: tcgen05.ld/st are .sync.aligned.
+    const int quarter = warp & 3, half = warp >> 2;
+    const int row = quarter * 32 + lane;  // query row of the tile = TMEM lane
+    const int t = qt * kTile + row;       // its token
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t pair_bar = 1 + quarter;  // named barriers 1..4, 64 threads each
     const float sl2 = p.scale_log2;
+    const int last_key = min(t, p.tokens - 1);  // keys <= last_key are visible to this row
     float pivot = -INFINITY, lsum = 0.f;
     bool ok = true;
-    // Control flow stays warp-uniform: tcgen05.ld/st are .sync.aligned.
     for (int j = 0; j < kv_tiles; ++j) {
       const int x = j & 1;
       const bool waited = !*abort_flag && mbar_wait_bounded(&s_full[x], (j >> 1) & 1);
@@ -204,19 +215,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc::fence_after();
-      const uint32_t s_addr = tmem + 128 * x + lane_base;
-      const int key0 = j * kTile;
-      // keys past this row's token (the diagonal tile) and past the prompt are masked
-      const int last_key = min(t, p.tokens - 1);  // keys <= last_key are visible
+      const uint32_t s_addr = tmem + 128 * x + 64 * half + lane_base;
+      const int key0 = j * kTile + 64 * half;  // this warp's first key
+      // a tile below the diagonal is visible to every query row of this tile
+      const bool interior = j < qt;
       float mx = -INFINITY;
 #pragma unroll
-      for (int c0 = 0; c0 < kTile; c0 += 32) {
+      for (int c0 = 0; c0 < 64; c0 += 32) {
         float v[32];
         tc::ld32(s_addr + c0, v);
 #pragma unroll
         for (int c = 0; c < 32; ++c)
-          if (key0 + c0 + c <= last_key) mx = fmaxf(mx, v[c] * sl2);
+          if (interior || key0 + c0 + c <= last_key) mx = fmaxf(mx, v[c] * sl2);
       }
+      // the row's other half: exchange partial maxima through TMEM column [parity][half]
+      tc::st1(tmem + kTmemXchg + 2 * x + half + lane_base, mx);
+      tc::fence_before();
+      asm volatile("bar.sync %0, 64;" ::"r"(pair_bar) : "memory");
+      tc::fence_after();
+      mx = fmaxf(mx, tc::ld1(tmem + kTmemXchg + 2 * x + (1 - half) + lane_base));
       // lazy rescale: a row's pivot moves only when its max exceeds the pivot by more than 8
       float corr = 1.f;
       const bool need = mx > pivot + kRescaleAbove || (pivot == -INFINITY && mx > -INFINITY);
@@ -226,8 +243,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       lsum *= corr;
       if (j >= 1 && __any_sync(0xffffffffu, need)) {
-        // the previous tile's product must have landed in O before the warp's rows are
-        // rescaled (rows that keep their pivot multiply by 1)
+        // the previous tile's product must have landed in O before this warp's half of the
+        // rows' O is rescaled (rows that keep their pivot multiply by 1)
         const bool landed = mbar_wait_bounded(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1);
         if (!__all_sync(0xffffffffu, landed)) {
           ok = false;
@@ -235,12 +252,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc::fence_after();
 #pragma unroll
-        for (int c0 = 0; c0 < kDim; c0 += 32) {
+        for (int c0 = 0; c0 < kDim / 2; c0 += 32) {
           float o[32];
-          tc::ld32(tmem_o + lane_base + c0, o);
+          tc::ld32(tmem_o + half * (kDim / 2) + lane_base + c0, o);
 #pragma unroll
           for (int c = 0; c < 32; ++c) o[c] *= corr;
-          tc::st32(tmem_o + lane_base + c0, o);
+          tc::st32(tmem_o + half * (kDim / 2) + lane_base + c0, o);
         }
       }
       // P tile x was last read by the product of tile j - 2
@@ -252,41 +269,38 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       const float piv = pivot == -INFINITY ? 0.f : pivot;
-      uint8_t* pt = p_s + x * S::kPBytes;
+      // this warp's 64 keys are box `half` of the K-major P tile
+      uint8_t* pt = p_s + x * S::kPBytes + half * S::kBox;
 #pragma unroll
-      for (int c0 = 0; c0 < kTile; c0 += 32) {
+      for (int c0 = 0; c0 < 64; c0 += 32) {
         float v[32];
         tc::ld32(s_addr + c0, v);
         uint32_t packed[16];
 #pragma unroll
         for (int c = 0; c < 32; c += 2) {
-          const float p0 = key0 + c0 + c <= last_key ? tc::ex2_approx(v[c] * sl2 - piv) : 0.f;
-          const float p1 = key0 + c0 + c + 1 <= last_key ? tc::ex2_approx(v[c + 1] * sl2 - piv) : 0.f;
-          const uint32_t w = pack_bf16x2(p0, p1);
+          const bool see0 = interior || key0 + c0 + c <= last_key;
+          const bool see1 = interior || key0 + c0 + c + 1 <= last_key;
+          const float p0 = see0 ? tc::ex2_approx(v[c] * sl2 - piv) : 0.f;
+          const float p1 = see1 ? tc::ex2_approx(v[c + 1] * sl2 - piv) : 0.f;
           lsum += p0 + p1;
-          packed[c / 2] = w;
+          packed[c / 2] = pack_bf16x2(p0, p1);
         }
-        // 32 keys = four 16-byte chunks of this row in box (c0 / 64), swizzled
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int chunk = ((c0 & 63) >> 3) + q;
-          *reinterpret_cast<uint4*>(pt + (c0 >> 6) * S::kBox + sw128(row, chunk)) =
+        for (int q = 0; q < 4; ++q)
+          *reinterpret_cast<uint4*>(pt + sw128(row, (c0 >> 3) + q)) =
               make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
-        }
       }
       tc::fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[x]);
       // V rows past the prompt: zeroed so stale cache values never meet a zero weight
-      if (key0 + kTile > p.tokens) {
+      if (half == 0 && j * kTile + kTile > p.tokens && j * kTile + row >= p.tokens) {
         uint8_t* vt = stages + x * S::kStageBytes + S::kTileBytes;
-        if (key0 + row >= p.tokens) {
 #pragma unroll
-          for (int bx = 0; bx < D / 64; ++bx)
+        for (int bx = 0; bx < D / 64; ++bx)
 #pragma unroll
-            for (int c16 = 0; c16 < 8; ++c16)
-              *reinterpret_cast<uint4*>(vt + bx * S::kBox + row * 128 + c16 * 16) = make_uint4(0, 0, 0, 0);
-        }
+          for (int c16 = 0; c16 < 8; ++c16)
+            *reinterpret_cast<uint4*>(vt + bx * S::kBox + row * 128 + c16 * 16) = make_uint4(0, 0, 0, 0);
       }
       fence_proxy_async_smem();
       __syncwarp();
@@ -301,15 +315,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       *abort_flag = 1;
     }
     if (ok) {
-      // every lane reads its O row (the warp's TMEM loads stay uniform); rows past the
-      // prompt are not stored
+      // row sum = both halves' partial sums (TMEM exchange, column [half] past the maxima)
       tc::fence_after();
-      const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
-      __nv_bfloat16* dst = p.out + ((static_cast<size_t>(b) * p.tokens + t) * p.q_heads + hq) * kDim;
+      tc::st1(tmem + kTmemXchg + 4 + half + lane_base, lsum);
+      tc::fence_before();
+      asm volatile("bar.sync %0, 64;" ::"r"(pair_bar) : "memory");
+      tc::fence_after();
+      const float total = lsum + tc::ld1(tmem + kTmemXchg + 4 + (1 - half) + lane_base);
+      const float inv = total > 0.f ? 1.f / total : 0.f;
+      // every lane reads its O row half (uniform TMEM loads); rows past the prompt are not stored
+      __nv_bfloat16* dst =
+          p.out + ((static_cast<size_t>(b) * p.tokens + t) * p.q_heads + hq) * kDim + half * (kDim / 2);
 #pragma unroll
-      for (int c0 = 0; c0 < kDim; c0 += 32) {
+      for (int c0 = 0; c0 < kDim / 2; c0 += 32) {
         float o[32];
-        tc::ld32(tmem_o + lane_base + c0, o);
+        tc::ld32(tmem_o + half * (kDim / 2) + lane_base + c0, o);
         if (t < p.tokens) {
 #pragma unroll
           for (int q = 0; q < 4; ++q)

@@ -92,6 +92,18 @@ __device__ __forceinline__ void st32(uint32_t taddr, const float (&v)[32]) {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// One fp32 column of this warp's 32 TMEM lanes: store (waits for it) and load.
+__device__ __forceinline__ void st1(uint32_t taddr, float v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr), "r"(__float_as_uint(v)) : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float ld1(uint32_t taddr) {
+  uint32_t r;
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+  return __uint_as_float(r);
+}
+
 // 2^x with the PTX approximate base-2 exponential (what Triton's tl.exp2 lowers to); -inf
 // gives +0.
 __device__ __forceinline__ float ex2_approx(float x) {
