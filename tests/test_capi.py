@@ -55,6 +55,23 @@ def test_host_validation_without_gpu():
     assert lib.fb_add_rmsnorm(p, 1, p, p, p, p, 4, 70000, 1e-6, null) == -2  # row too wide (> 65536)
     assert lib.fb_decode_attention(p, p, p, p, 0, p, p, 1 << 20, 1, 16, 8, 96, 2048, 0.1, 148, null) == -2  # D=96
     assert lib.fb_decode_attention(p, p, p, p, 0, p, p, 1 << 20, 1, 72, 8, 128, 2048, 0.1, 148, null) == -2  # G=9
+    # prefill attention: head_dim 96 and capacity < tokens are unsupported; null -> ARG
+    assert lib.fb_prefill_attention(null, p, p, p, 1, 16, 8, 2, 128, 16, 0.1, null) == -1
+    assert lib.fb_prefill_attention(p, p, p, p, 1, 16, 8, 2, 96, 16, 0.1, null) == -2
+    assert lib.fb_prefill_attention(p, p, p, p, 1, 16, 8, 2, 128, 8, 0.1, null) == -2
+    # speculation bookkeeping: blocks wider than 64 tokens, drafts outside [1, T-1]
+    assert lib.fb_spec_propose(p, 64, p, p, 8, 4, p, p, p, p, 2, 65, 1, 1, 1, 1, 8, null) == -2
+    assert lib.fb_spec_propose(p, 64, p, p, 8, 4, p, p, p, p, 2, 8, 0, 1, 1, 1, 8, null) == -1
+    assert lib.fb_spec_propose(p, 64, p, p, 8, 4, p, p, p, p, 2, 8, 1, 1, 1, 8, 8, null) == -1
+    assert lib.fb_spec_settle(p, p, null, p, p, p, 64, p, p, p, p, p, 2, 65, null) == -2
+    assert lib.fb_spec_relocate(p, 4, 2, 2, 64, 60, p, p, null) == -2
+    # tensor-parallel producers: odd widths, unaligned peer buffers, bad ranks
+    peers = (ctypes.c_void_p * 2)(16, 32)
+    assert lib.fb_reduce_push(p, 2, 4, 5, 2, 0, 0, peers, null, p, null) == -2
+    assert lib.fb_reduce_push(p, 2, 4, 8, 2, 2, 0, peers, null, p, null) == -1
+    odd = (ctypes.c_void_p * 2)(16, 40)
+    assert lib.fb_reduce_push(p, 2, 4, 8, 2, 0, 0, odd, null, p, null) == -1
+    assert lib.fb_linear_argmax(p, p, 4, 128, 128, -1, p, null) == -1
     # workspace too small -> FB_ERR_WORKSPACE
     need = lib.fb_decode_attention_workspace(1, 16, 8, 128, 148)
     assert need > 0
