@@ -601,14 +601,14 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const P
 
 // ---------------------------------------------------------------------------------------
 // Cluster form, for a position shared by every row and few (row, KV head) pairs (tensor-
-// parallel shards, small batches): one thread-block cluster of C <= 8 CTAs per pair. CTA r
+// parallel shards, small batches): one thread-block cluster of C <= 16 CTAs per pair. CTA r
 // streams tiles [r*n/C, (r+1)*n/C) of the pair with the same per-tile arithmetic as the
 // persistent kernel, keeps its combined (max, denominator, O) in shared memory, and after one
 // cluster barrier every CTA merges its share of the pair's G*D outputs over the C partials
 // through distributed shared memory, in rank order: no global partials, fences, counters or
 // second pass.
 // ---------------------------------------------------------------------------------------
-constexpr int kMaxCluster = 8;
+constexpr int kMaxCluster = 16;  // 16 needs the non-portable cluster size attribute
 
 template <int D, int NS>
 struct ClusterSmem {
@@ -806,6 +806,9 @@ bool configure_cluster() {
     if (cudaFuncSetAttribute(decode_cluster_kernel<D, NS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              ClusterSmem<D, NS>::kTotal) != cudaSuccess)
       return false;
+    if (cudaFuncSetAttribute(decode_cluster_kernel<D, NS>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) !=
+        cudaSuccess)
+      cudaGetLastError();  // no clusters above 8: the occupancy query then reports none
     configured[dev] = true;
   }
   return true;
@@ -840,10 +843,11 @@ int resident_clusters(int c) {
   return n;
 }
 
-// The largest cluster size in {8, 4, 2} whose `pairs` clusters are all resident at once, or 0.
+// The largest cluster size in {limit, ..., 4, 2} (powers of two) whose `pairs` clusters are all
+// resident at once, or 0.
 template <int D, int NS>
-int cluster_size(int pairs) {
-  for (int c = kMaxCluster; c >= 2; c /= 2)
+int cluster_size(int pairs, int limit) {
+  for (int c = limit; c >= 2; c /= 2)
     if (resident_clusters<D, NS>(c) >= pairs) return c;
   return 0;
 }
@@ -855,16 +859,44 @@ int launch_cluster(const CUtensorMap& km, const CUtensorMap& vm, const Params& p
                    ClusterSmem<D, NS>::kTotal, stream, cluster, km, vm, p);
 }
 
-// Cluster form choice (measured on B200, 16 rows x 8193 tokens): the 4-stage ring (one CTA
-// per SM) while its clusters cover about two thirds of the SMs or more (32 pairs: 4 x 32
-// CTAs, 24.8 us against 26.7 us with 2 stages; 64 pairs: 2 x 64, 42.8 against 44.9); below
-// that the 2-stage ring (three CTAs per SM) fits larger clusters (16 pairs: 8 x 16 CTAs,
-// 19.2 us against 20.9 us for 4 x 16). Returns FB_ERR_SHAPE when neither fits in one wave.
+// Tuning override of the cluster form's shape (fb_decode_attention_cluster_shape): cluster
+// size and ring depth, 0 = automatic.
+int g_force_cluster = 0, g_force_stages = 0;
+
+template <int D>
+int launch_cluster_stages(const CUtensorMap& km, const CUtensorMap& vm, const Params& p, int c, int ns,
+                          cudaStream_t s) {
+  if (ns == 2) return launch_cluster<D, 2>(km, vm, p, c, s);
+  if (ns == 3) return launch_cluster<D, 3>(km, vm, p, c, s);
+  return launch_cluster<D, kStages>(km, vm, p, c, s);
+}
+
+template <int D>
+int resident_clusters_stages(int c, int ns) {
+  if (ns == 2) return resident_clusters<D, 2>(c);
+  if (ns == 3) return resident_clusters<D, 3>(c);
+  return resident_clusters<D, kStages>(c);
+}
+
+// Cluster form choice (measured on B200, 16 rows x 8193 tokens, graph-timed): the 4-stage ring
+// (one CTA per SM) while its clusters cover about two thirds of the SMs or more (64 pairs: 2 x
+// 64 CTAs, 45.9 us against 46.4-51.2 for 4x2, 4x3, 8x2; 32 pairs: 4 x 32, 25.2 us against
+// 25.7-31.0 for 8x3, 4x3, 8x2, 16x2); below that the larger clusters of the 3-stage ring (two
+// CTAs per SM) or the 2-stage ring (three) (16 pairs: 8 x 16 CTAs with 3 stages 17.1 us,
+// 2 stages 18.6, 16 x 16 with 2 stages 17.2, 4 x 16 with 4 stages 20.4). Returns FB_ERR_SHAPE
+// when none fits in one wave.
 template <int D>
 int launch_cluster_form(const CUtensorMap& km, const CUtensorMap& vm, const Params& p, int pairs, cudaStream_t s) {
-  const int c4 = cluster_size<D, kStages>(pairs);
+  if (g_force_cluster >= 2) {
+    const int ns = g_force_stages;
+    if (resident_clusters_stages<D>(g_force_cluster, ns) < pairs) return FB_ERR_SHAPE;
+    return launch_cluster_stages<D>(km, vm, p, g_force_cluster, ns, s);
+  }
+  const int c4 = cluster_size<D, kStages>(pairs, 8);
   if (c4 >= 2 && 3 * pairs * c4 >= 2 * sm_count()) return launch_cluster<D, kStages>(km, vm, p, c4, s);
-  const int c2 = cluster_size<D, kClusterStages>(pairs);
+  const int c3 = cluster_size<D, 3>(pairs, 8);
+  const int c2 = cluster_size<D, kClusterStages>(pairs, 8);
+  if (c3 > c4 && c3 >= c2) return launch_cluster<D, 3>(km, vm, p, c3, s);
   if (c2 > c4) return launch_cluster<D, kClusterStages>(km, vm, p, c2, s);
   if (c4 >= 2) return launch_cluster<D, kStages>(km, vm, p, c4, s);
   return FB_ERR_SHAPE;
@@ -908,6 +940,18 @@ extern "C" int fb_decode_attention_ctas(int batch, int kv_heads, int capacity, i
   (void)capacity;
   (void)head_dim;
   return sm_count();
+}
+
+extern "C" int fb_decode_attention_cluster_shape(int cluster, int stages) {
+  if (cluster == 0) {
+    g_force_cluster = g_force_stages = 0;
+    return FB_OK;
+  }
+  if ((cluster != 2 && cluster != 4 && cluster != 8 && cluster != 16) || stages < 2 || stages > kStages)
+    return FB_ERR_ARG;
+  g_force_cluster = cluster;
+  g_force_stages = stages;
+  return FB_OK;
 }
 
 extern "C" size_t fb_decode_attention_workspace(int batch, int q_heads, int kv_heads,

@@ -13,6 +13,7 @@
 // One warp per (token row, head); each lane owns D/32 consecutive dims, so the
 // rotate-half partner of a lane's dims sits in lane ^ 16 and one shuffle pairs them.
 #include "common.cuh"
+#include "rope_math.cuh"
 
 namespace fb {
 namespace rope {
@@ -107,17 +108,7 @@ __global__ void __launch_bounds__(128) qk_rope_kernel(const Params p) {
   // the norm gains are never written while decoding: load them before the dependency wait
   const __nv_bfloat16* gain = is_q ? p.q_weight : p.k_weight;
   float gw[E];
-  if constexpr (E == 4) {
-    const uint2 gv = __ldg(reinterpret_cast<const uint2*>(gain + d0));
-    gw[0] = bf16_lo(gv.x);
-    gw[1] = bf16_hi(gv.x);
-    gw[2] = bf16_lo(gv.y);
-    gw[3] = bf16_hi(gv.y);
-  } else {
-    const uint32_t gv = __ldg(reinterpret_cast<const uint32_t*>(gain + d0));
-    gw[0] = bf16_lo(gv);
-    gw[1] = bf16_hi(gv);
-  }
+  load_bf16<E>(gain + d0, gw);
   pdl_wait();
   pdl_trigger();
   // Every other global read is issued up front (the V head before any store that could
@@ -132,25 +123,6 @@ __global__ void __launch_bounds__(128) qk_rope_kernel(const Params p) {
     pos_base = __ldg(p.position + b);
   else if (p.mode == 0)
     pos_base = __ldg(p.position);
-  float ss = 0.f;
-#pragma unroll
-  for (int e = 0; e < E; ++e) ss += x[e] * x[e];
-  ss = warp_sum(ss);
-  const float eps = is_q ? p.q_eps : p.k_eps;
-  const float inv = 1.0f / sqrtf(ss / static_cast<float>(D) + eps);
-
-  float w[E];
-#pragma unroll
-  for (int e = 0; e < E; ++e) {
-    const float n = bf16_round(x[e] * inv);
-    w[e] = bf16_round(n * gw[e]);
-  }
-  // Rotate-half partner: dims (d + D/2) mod D live in lane ^ 16.
-  float partner[E];
-#pragma unroll
-  for (int e = 0; e < E; ++e) partner[e] = __shfl_xor_sync(0xffffffffu, w[e], 16);
-  const bool low_half = lane < 16;
-
   long long phase;
   if (p.table) {
     // whole tables: the phase row is the token's position (plus its verify-block phase)
@@ -158,20 +130,8 @@ __global__ void __launch_bounds__(128) qk_rope_kernel(const Params p) {
   } else {
     phase = p.mode == 2 ? row : t;
   }
-  const __nv_bfloat16* cs = p.cos + phase * D + d0;
-  const __nv_bfloat16* sn = p.sin + phase * D + d0;
-  float y[E];
-#pragma unroll
-  for (int e = 0; e < E; ++e) {
-    const float rot = low_half ? -partner[e] : partner[e];
-    const float direct = bf16_round(w[e] * __bfloat162float(cs[e]));
-    const float turn = bf16_round(rot * __bfloat162float(sn[e]));
-    y[e] = direct + turn;  // rounded once more by the bf16 store below
-  }
-
   __nv_bfloat16 outv[E];
-#pragma unroll
-  for (int e = 0; e < E; ++e) outv[e] = __float2bfloat16_rn(y[e]);
+  norm_rope<D>(x, gw, is_q ? p.q_eps : p.k_eps, p.cos + phase * D + d0, p.sin + phase * D + d0, lane, outv);
   if (is_q) {
     __nv_bfloat16* dst = p.query + (static_cast<size_t>(row) * p.q_heads + head) * D + d0;
 #pragma unroll

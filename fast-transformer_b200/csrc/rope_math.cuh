@@ -1,0 +1,68 @@
+// Per-head QK-RMSNorm + rotate-half RoPE on one warp, shared by the stand-alone kernel
+// (qk_rope.cu) and the qkv projection's fused epilogue (linear.cu).
+//
+// Arithmetic and cast points of the reference kernel `_qk_rope_cache`
+// (engine/kernels/qk_rope.py:34-66):
+//   inv  = 1 / sqrt(mean(x^2) + eps)            fp32
+//   n    = bf16(x * inv); w = bf16(n * gain)
+//   rot  = [-w[D/2:], w[:D/2]]
+//   out  = bf16(bf16(w * cos) + bf16(rot * sin)) both products rounded
+// Lane l holds dims [l*E, l*E + E), E = D/32, so the rotate-half partner of a lane's dims
+// sits in lane ^ 16.
+#pragma once
+
+#include "common.cuh"
+
+namespace fb {
+namespace rope {
+
+// Loads E consecutive bf16 values at `src` (8- or 4-byte aligned) as fp32.
+template <int E>
+__device__ __forceinline__ void load_bf16(const __nv_bfloat16* src, float (&x)[E]) {
+  if constexpr (E == 4) {
+    const uint2 w = __ldg(reinterpret_cast<const uint2*>(src));
+    x[0] = bf16_lo(w.x);
+    x[1] = bf16_hi(w.x);
+    x[2] = bf16_lo(w.y);
+    x[3] = bf16_hi(w.y);
+  } else {
+    const uint32_t w = __ldg(reinterpret_cast<const uint32_t*>(src));
+    x[0] = bf16_lo(w);
+    x[1] = bf16_hi(w);
+  }
+}
+
+// x: this lane's E values of one head (fp32 holding bf16 values); gw: the matching norm gains;
+// cs/sn: the cos/sin table row of the token's phase, offset to this lane's first dim.
+// Every lane of the warp must call it (one shuffle reduction, one partner exchange).
+template <int D>
+__device__ __forceinline__ void norm_rope(const float (&x)[D / 32], const float (&gw)[D / 32], float eps,
+                                          const __nv_bfloat16* cs, const __nv_bfloat16* sn, int lane,
+                                          __nv_bfloat16 (&out)[D / 32]) {
+  constexpr int E = D / 32;
+  float ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < E; ++e) ss += x[e] * x[e];
+  ss = warp_sum(ss);
+  const float inv = 1.0f / sqrtf(ss / static_cast<float>(D) + eps);
+  float w[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const float n = bf16_round(x[e] * inv);
+    w[e] = bf16_round(n * gw[e]);
+  }
+  float partner[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) partner[e] = __shfl_xor_sync(0xffffffffu, w[e], 16);
+  const bool low_half = lane < 16;
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const float rot = low_half ? -partner[e] : partner[e];
+    const float direct = bf16_round(w[e] * __bfloat162float(cs[e]));
+    const float turn = bf16_round(rot * __bfloat162float(sn[e]));
+    out[e] = __float2bfloat16_rn(direct + turn);
+  }
+}
+
+}  // namespace rope
+}  // namespace fb

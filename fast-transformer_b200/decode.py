@@ -148,24 +148,57 @@ def _qk_rope_decode(packed, layer, eps, cos, sin, position, keys, values, q_head
     return query.view(batch, q_heads, 1, dim)  # one token: token-major storage is [B, Hq, 1, D]
 
 
-#: K chunks (64 columns) up to which the push projection runs as one split with the push in
-#: its epilogue; longer K writes split partials that fb_reduce_push sums and pushes (on B200
-#: a cluster reduction of the splits inside the projection measured 3-5 us slower).
-PUSH_SINGLE_SPLIT_CHUNKS = 8
+def _qkv_rope_decode(x, layer, eps, cos, sin, position, keys, values, q_heads):
+    """qkv projection + QK-norm + RoPE + KV append for one decode token per row: one
+    fb_linear_qk_rope launch when the head dim is 128 (the projection's epilogue), else the
+    projection's split partials + fb_qk_norm_rope_append (the same bits)."""
+    batch, kv_heads, capacity, dim = keys.shape
+    rows = x.numel() // x.shape[-1]
+    n, k = layer.qkv.shape
+    if dim != 128 or not klinear.supported(rows, layer.qkv) or not FINISH_SPLITS_IN_PROJECTION:
+        return _qk_rope_decode(linear(x, layer.qkv, split_ok=True), layer, eps, cos, sin, position, keys, values,
+                               q_heads)
+    flat = x.reshape(rows, k).contiguous()
+    splits = klinear.splits_for(rows, n, k, x.device, finished=True)
+    query = torch.empty((batch, 1, q_heads, dim), device=keys.device, dtype=BF16)
+    status = lib.fb_linear_qk_rope(ptr(flat), ptr(layer.qkv), rows, n, k, splits, ptr(layer.q_norm),
+                                   ptr(layer.k_norm), float(eps), float(eps), ptr(cos), ptr(sin), ptr(position),
+                                   ptr(query), ptr(keys), ptr(values), q_heads, kv_heads, dim, capacity, stream())
+    if status == _native.FB_ERR_SHAPE:  # split heads beyond the fix-up storage: nothing launched
+        return _qk_rope_decode(linear(x, layer.qkv, split_ok=True), layer, eps, cos, sin, position, keys, values,
+                               q_heads)
+    check(status, "fb_linear_qk_rope")
+    return query.view(batch, q_heads, 1, dim)
 
 
-def _push_projection(x, weight, comm, peers, use, epoch):
+#: How a K-split projection whose result feeds a fixed follow-up is finished on the decode
+#: path: by split partials and a consumer kernel (fb_qk_norm_rope_append, fb_swiglu_blocked,
+#: fb_reduce_push; the default), or in the projection's own launch (split fix-up:
+#: fb_linear_qk_rope, the SwiGLU epilogue, the push epilogue). Both give the same bits. On B200
+#: the consumer form measured faster at every shape (captured Qwen3-8B step, one rank's shard
+#: alone: TP1 6172 against 6295 us, TP8 1990 against 2350 us): the consumer runs while the
+#: next projection's CTAs already stream their weights, whereas the fix-up's last CTA per
+#: tile holds its SM until the tile is summed.
+FINISH_SPLITS_IN_PROJECTION = False
+
+
+def _push_projection(x, weight, comm, peers, use, epoch, split_consumer=None):
     """This rank's fp32 partial of x @ W^T, pushed to every rank's recv[use] flagged with
-    epoch + 1 (fb_linear_allreduce_push, or split partials + fb_reduce_push)."""
+    epoch + 1: split partials + fb_reduce_push (``split_consumer``, the default), or
+    fb_linear_allreduce_push with the K splits summed in its launch. One split (K < 256)
+    always pushes from the projection's epilogue. Graph-timed at TP8 (o_proj, K = 512): 4.3 us
+    for 2 splits + fb_reduce_push against 5.0 us for one split with the push epilogue."""
+    if split_consumer is None:
+        split_consumer = not FINISH_SPLITS_IN_PROJECTION
     rows = x.numel() // x.shape[-1]
     flat = x.reshape(rows, x.shape[-1]).contiguous()
     n, k = weight.shape
-    if (k + 63) // 64 <= PUSH_SINGLE_SPLIT_CHUNKS:
-        check(lib.fb_linear_allreduce_push(ptr(flat), ptr(weight), rows, n, k, 1, comm.size, comm.rank, use,
+    splits = klinear.splits_for(rows, n, k, x.device, finished=True)
+    if splits == 1 or not split_consumer:
+        check(lib.fb_linear_allreduce_push(ptr(flat), ptr(weight), rows, n, k, splits, comm.size, comm.rank, use,
                                            peers.recv_ptrs, peers.mc_ptr, ptr(epoch), stream()),
               "fb_linear_allreduce_push")
         return
-    splits = min(klinear.splits_for(rows, n, k, x.device), klinear.MAX_CLUSTER_SPLITS)
     partials = klinear.project(flat, weight, klinear.SPLITS_OUT, splits)
     check(lib.fb_reduce_push(ptr(partials), splits, rows, n, comm.size, comm.rank, use, peers.recv_ptrs, peers.mc_ptr,
                              ptr(epoch), stream()), "fb_reduce_push")
@@ -231,9 +264,8 @@ class DecodeState:
         for index, layer in enumerate(layers):
             if index > 0 and peers is None:
                 normalized, residual = add_rms_norm(hidden, residual, layer.ln1, eps)
-            packed = linear(normalized, layer.qkv, split_ok=True)
-            query = _qk_rope_decode(packed, layer, eps, self.cos, self.sin, self.position,
-                                    cache.keys[index], cache.values[index], w.q_heads)
+            query = _qkv_rope_decode(normalized, layer, eps, self.cos, self.sin, self.position,
+                                     cache.keys[index], cache.values[index], w.q_heads)
             attention = attend_decode(query, cache.keys[index], cache.values[index], self.position, self.scale,
                                       out=self.attn_out, workspace=self.workspace, ctas=self.ctas)
             attention = attention.reshape(self.batch, 1, -1)
@@ -243,7 +275,7 @@ class DecodeState:
             else:
                 _push_projection(attention, layer.o, comm, peers, 2 * index, self.position)
                 normalized, residual = _reduce_add_norm(peers, 2 * index, self.position, residual, layer.ln2, eps)
-            activated = swiglu_linear(normalized, layer.gate_up)
+            activated = swiglu_linear(normalized, layer.gate_up, split_consumer=not FINISH_SPLITS_IN_PROJECTION)
             if peers is None:
                 hidden = linear(activated, layer.down, split_ok=True)
             else:

@@ -13,6 +13,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIBRARY_PATH = os.path.join(os.path.dirname(_HERE), "libfastb200.so")
 
 FB_OK = 0
+FB_ERR_SHAPE = -2
 _STATUS = {
     -1: "bad argument",
     -2: "unsupported shape",
@@ -50,6 +51,10 @@ _SIGNATURES = {
     "fb_embed_rmsnorm": (_c_int, [_vp, _vp, _c_i64, _vp, _vp, _vp, _c_int, _c_int, _c_float, _vp]),
     "fb_swiglu": (_c_int, [_vp, _c_int, _vp, _c_int, _c_int, _vp]),
     "fb_linear_splits": (_c_int, [_c_int, _c_int, _c_int]),
+    "fb_linear_finished_splits": (_c_int, [_c_int, _c_int, _c_int]),
+    "fb_decode_attention_cluster_shape": (_c_int, [_c_int, _c_int]),
+    "fb_linear_qk_rope": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _c_float, _c_float, _vp, _vp,
+                                   _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp]),
     "fb_linear": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _vp]),
     "fb_linear_allreduce_push": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _vp,
                                           _vp, _vp]),

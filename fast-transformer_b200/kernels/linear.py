@@ -4,8 +4,8 @@ Drop-in for engine/kernels/linear.py:489-523 ``linear(x, weight, split_ok)``: al
 accumulate in FP32 and round once to BF16. Decode-sized inputs (<= MAX_ROWS rows, aligned
 K/N) run the TMA + mma.sync kernel fb_linear over (N/128 tiles) x (K splits); with
 ``split_ok`` a split-K result comes back as a ``Split`` of FP32 partials for a consumer kernel
-to sum (merged.py), otherwise the splits of a tile (at most 8, one thread-block cluster) sum
-their partials through distributed shared memory and write BF16. Larger
+to sum (merged.py), otherwise the last-arriving split CTA of each tile sums the tile's
+partials in split order and writes BF16 (the split fix-up, same launch). Larger
 row counts (prefill) stay on cuBLAS through ``F.linear``, exactly as the reference routes them
 (linear.py:492).
 """
@@ -20,19 +20,18 @@ from kernels.merged import Split
 #: Rows the skinny kernel takes (x is staged as 16/32/64-row slabs).
 MAX_ROWS = 64
 BF16_OUT, FP32_OUT, SWIGLU_OUT, SPLITS_OUT = 0, 1, 2, 3
-#: K-splits of one finished tile form a thread-block cluster (portable size limit).
-MAX_CLUSTER_SPLITS = 8
 _SPLITS = {}
 
 
 def splits_for(rows, n, k, device, finished=False):
-    """fb_linear_splits' choice; capped at MAX_CLUSTER_SPLITS for finished-tile epilogues."""
-    key = (device, rows, n, k)
+    """fb_linear_splits' choice, or fb_linear_finished_splits' for finished-tile epilogues."""
+    key = (device, rows, n, k, finished)
     if key not in _SPLITS:
         if torch.cuda.is_current_stream_capturing():
             raise RuntimeError("projection selection must finish during eager warmup")
-        _SPLITS[key] = int(lib.fb_linear_splits(rows, n, k))
-    return min(_SPLITS[key], MAX_CLUSTER_SPLITS) if finished else _SPLITS[key]
+        choose = lib.fb_linear_finished_splits if finished else lib.fb_linear_splits
+        _SPLITS[key] = int(choose(rows, n, k))
+    return _SPLITS[key]
 
 
 def supported(rows, weight):
@@ -68,21 +67,23 @@ def linear(x, weight, split_ok=False):
     splits = splits_for(rows, n, k, x.device)
     if split_ok and splits > 1:
         return Split(project(flat, weight, SPLITS_OUT, splits), (*x.shape[:-1], n))
-    return project(flat, weight, BF16_OUT, min(splits, MAX_CLUSTER_SPLITS)).reshape(*x.shape[:-1], n)
+    return project(flat, weight, BF16_OUT, splits_for(rows, n, k, x.device, finished=True)).reshape(
+        *x.shape[:-1], n)
 
 
-def swiglu_linear(x, gate_up_blocked):
+def swiglu_linear(x, gate_up_blocked, split_consumer=True):
     """SwiGLU(x @ W^T), W's rows being [gate; up] interleaved in 64-row blocks: bf16(bf16(silu(
-    gate)) * up) per feature, the reference's projection + swiglu arithmetic. When one K split
-    fills the GPU, the projection's epilogue applies SwiGLU (one launch); when the shape needs
-    K splits, the projection writes split partials and fb_swiglu_blocked sums them and applies
-    SwiGLU (a finished-tile cluster reduction measured 3-5 us slower on B200)."""
+    gate)) * up) per feature, the reference's projection + swiglu arithmetic. At one K split the
+    projection's epilogue applies SwiGLU (one launch). With K splits the projection writes
+    split partials that fb_swiglu_blocked sums and activates (``split_consumer``, measured
+    faster inside the decode step), or, without it, the last split CTA of each tile sums them
+    and applies SwiGLU in the projection's launch (the split fix-up). The same bits either way."""
     rows = x.numel() // x.shape[-1]
     flat = x.reshape(rows, x.shape[-1]).contiguous()
     n, k = gate_up_blocked.shape
-    splits = min(splits_for(rows, n, k, x.device), MAX_CLUSTER_SPLITS)  # one batch of slab loads
-    if splits == 1:
-        return project(flat, gate_up_blocked, SWIGLU_OUT, 1).reshape(*x.shape[:-1], n // 2)
+    splits = splits_for(rows, n, k, x.device, finished=True)
+    if splits == 1 or not split_consumer:
+        return project(flat, gate_up_blocked, SWIGLU_OUT, splits).reshape(*x.shape[:-1], n // 2)
     partials = project(flat, gate_up_blocked, SPLITS_OUT, splits)
     out = torch.empty((rows, n // 2), device=x.device, dtype=torch.bfloat16)
     check(lib.fb_swiglu_blocked(ptr(partials), splits, ptr(out), rows, n // 2, stream()), "fb_swiglu_blocked")

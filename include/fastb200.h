@@ -80,6 +80,13 @@ int fb_decode_attention_partials(const void* q, const void* k, const void* v,
 int fb_decode_attention_combine(const int64_t* position, int per_row, void* out, void* workspace,
                                 size_t workspace_bytes, int batch, int q_heads, int kv_heads,
                                 int head_dim, int capacity, int ctas, void* stream);
+/* Tuning override for fb_decode_attention's cluster form (one shared position, few pairs):
+ * every later call uses clusters of `cluster` CTAs (2, 4, 8 or 16) with a `stages`-deep K/V
+ * ring (2: three CTAs per SM, 3: two, 4: one); cluster 0 restores the automatic choice.
+ * Process-wide; a shape whose clusters do not all fit one wave then fails with FB_ERR_SHAPE.
+ * For launch-shape sweeps, like the reference's tune.py launch-width search; not needed
+ * otherwise. */
+int fb_decode_attention_cluster_shape(int cluster, int stages);
 
 /* ------------------------------------------------------------------------------------
  * Decode attention without allocation. No counterpart in the reference.
@@ -151,6 +158,19 @@ int fb_qk_norm_rope_append(const void* packed, int packed_splits, const void* q_
                            int q_heads, int kv_heads, int head_dim, int capacity, int mode,
                            int table, void* stream);
 
+/* The decode form fused into the qkv projection: x bf16 [M, K] (M <= 64 rows, one token
+ * each, all at the shared slot position[0]) times the packed qkv weight W bf16
+ * [(Hq + 2 Hkv) * 128, K]; head_dim must be 128 (one output tile = one head). The K splits of
+ * a head (`splits`, fb_linear_finished_splits(); FB_ERR_SHAPE when a split head exceeds the
+ * split fix-up storage) are summed in split order in the same launch, rounded to bf16, and the head goes through fb_qk_norm_rope_append's mode-0
+ * whole-table arithmetic: q heads to query bf16 [M, Hq, 128], k heads (normalized, rotated)
+ * and v heads (copied) to slot position[0] of keys/values [M, Hkv, C, 128]. Bit-identical to
+ * fb_linear (epilogue 3) + fb_qk_norm_rope_append (mode 0, table 1), in one launch. */
+int fb_linear_qk_rope(const void* x, const void* w, int m, int n, int k, int splits, const void* q_weight,
+                      const void* k_weight, float q_eps, float k_eps, const void* cos, const void* sin,
+                      const int64_t* position, void* query, void* keys, void* values, int q_heads,
+                      int kv_heads, int head_dim, int capacity, void* stream);
+
 /* ------------------------------------------------------------------------------------
  * RMSNorm family. Replace engine/kernels/rmsnorm.py:
  *   fb_rmsnorm        <- `rms_norm` :49-72 (kernel :21-46): y = bf16(bf16(x*rsqrt) * w)
@@ -197,13 +217,19 @@ int fb_swiglu_blocked(const void* packed, int splits, void* out, int rows, int w
  *            3: out fp32 split-K partials [splits, M, N] (split s covers K range
  *               [s*K/splits, (s+1)*K/splits) in 64-wide chunks); consumers sum them in split
  *               order, then round (engine/kernels/merged.py:13-45). No workspace needed.
- * Grid = ceil(N/128) tiles x `splits` K-splits (fb_linear_splits() picks a default; for
- * epilogues 0-2 use min(that, 8)). For epilogues 0-2 with splits > 1 (at most 8) the splits
- * of a tile run as one thread-block cluster and sum their partials in split order through
- * distributed shared memory (deterministic). No workspace. Launched with programmatic
- * stream serialization (weights are prefetched before the previous kernel completes).
+ * Grid = ceil(N/128) tiles x `splits` K-splits (fb_linear_splits() picks a default for
+ * epilogue 3, fb_linear_finished_splits() for epilogues 0-2). For epilogues 0-2 with
+ * splits > 1 the partials of a tile are summed in split order (deterministic; the bits a
+ * split consumer produces) in the same launch: by the tile's last-arriving CTA through a
+ * library-owned device array and arrival counter when the shape fits it (splits <= 16,
+ * ceil(N/128) * splits * M * 128 <= 2^22), else through distributed shared memory of a
+ * thread-block cluster (splits <= 8). The array is shared by all launches on a device:
+ * such launches must not run concurrently on two streams. No caller workspace. Launched
+ * with programmatic stream serialization (weights are prefetched before the previous
+ * kernel completes).
  * ---------------------------------------------------------------------------------- */
 int fb_linear_splits(int m, int n, int k);
+int fb_linear_finished_splits(int m, int n, int k);
 int fb_linear(const void* x, const void* w, void* out, int m, int n, int k, int epilogue, int splits,
               void* stream);
 
@@ -283,7 +309,7 @@ int fb_spec_relocate(void* store, int planes, int batch, int kv_heads, int capac
  * (a device int64, the decode position) can repeat a value it had (a new generation).
  * *epoch must differ between two calls with the same `use` and stay below 2^31.
  * Producer: fb_linear_allreduce_push computes this rank's fp32 partial of y = x @ W^T
- *   (splits <= 8 K-splits summed in one thread-block cluster) and stores every value into
+ *   (K-splits summed in the same launch as fb_linear's finished tiles) and stores every value into
  *   slab `rank` of recv[use] on every rank (peer_recv[r] = rank r's recv base). When
  *   multicast_recv is not NULL it is the NVSwitch multicast address of the same buffers
  *   (every rank's recv bound to one multicast object): each word is stored once through it

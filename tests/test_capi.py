@@ -50,7 +50,10 @@ def test_host_validation_without_gpu():
     assert lib.fb_linear(p, p, p, 4, 128, 100, 0, 1, null) == -2      # K not a multiple of 8
     assert lib.fb_linear(p, p, p, 4, 128, 128, 7, 1, null) == -1      # unknown epilogue
     assert lib.fb_linear(p, p, p, 4, 128, 128, 0, 3, null) == -2      # more splits than K chunks
-    assert lib.fb_linear(p, p, p, 4, 128, 4096, 0, 9, null) == -2     # finished tile: cluster of <= 8 splits
+    assert lib.fb_linear(p, p, p, 4, 128, 4096, 0, 17, null) == -2    # finished tile: split fix-up of <= 16 splits
+    assert lib.fb_linear(p, p, p, 64, 151936, 4096, 0, 9, null) == -2  # too large for the fix-up: cluster of <= 8
+    assert lib.fb_linear_finished_splits(16, 3072, 4096) <= 16
+    assert lib.fb_linear_finished_splits(64, 151936, 4096) <= 8
     assert lib.fb_swiglu(p, 1, p, 4, 12, null) == -2                     # width % 8
     assert lib.fb_add_rmsnorm(p, 1, p, p, p, p, 4, 70000, 1e-6, null) == -2  # row too wide (> 65536)
     assert lib.fb_decode_attention(p, p, p, p, 0, p, p, 1 << 20, 1, 16, 8, 96, 2048, 0.1, 148, null) == -2  # D=96

@@ -141,6 +141,32 @@ def test_decode_attention_cluster_form(batch, q_heads, kv_heads, dim, length):
     assert torch.equal(cluster, again)  # deterministic
 
 
+@pytest.mark.parametrize("shape", [(2, 2), (4, 4), (8, 2), (8, 3), (16, 2), (16, 3)])
+def test_decode_attention_cluster_shapes(shape):
+    """Every cluster-form launch shape (cluster size x ring depth, fb_decode_attention_cluster_shape)
+    against the fp32 reference at a TP8 shard (16 rows x 1 KV head x 4 query heads, 8193 slots,
+    NaN past the length) and a ragged tile count (1000 slots); a shape that does not fit one
+    wave returns FB_ERR_SHAPE."""
+    from kernels._native import lib
+    from kernels.decode_attention import decode_attention
+    cluster, stages = shape
+    for batch, q_heads, kv_heads, length in ((16, 4, 1, 8193), (3, 16, 2, 1000)):
+        lengths = [length] * batch
+        q, k, v, position = _ragged(batch, q_heads, kv_heads, 128, lengths, seed=cluster * 10 + stages + length)
+        shared = position[:1].contiguous()
+        expect = torch_fp32_decode(q, k, v, lengths, 1 / math.sqrt(128))
+        assert lib.fb_decode_attention_cluster_shape(cluster, stages) == 0
+        try:
+            out = decode_attention(q, k, v, shared, 1 / math.sqrt(128))
+        except RuntimeError as exc:
+            assert "-2" in str(exc) or "SHAPE" in str(exc).upper(), exc
+            continue
+        finally:
+            lib.fb_decode_attention_cluster_shape(0, 0)
+        assert torch.isfinite(out.float()).all()
+        torch.testing.assert_close(out.float(), expect, atol=2e-2, rtol=2e-2)
+
+
 def test_decode_attention_graph_capture_and_determinism():
     from kernels.decode_attention import decode_attention
     q, k, v, position = _ragged(2, 32, 8, 128, [5000, 777], seed=5, poison=False)
@@ -232,8 +258,9 @@ def test_swiglu_matches_reference():
 
 def test_linear_matches_reference():
     """Every epilogue against the reference's projection contract (F.linear, verify_gpu.py:175-185)
-    for several split counts: bf16 and fp32 finished tiles (cluster sum of the splits), fp32
-    split partials; deterministic; finished tiles equal the split-order sum of the partials."""
+    for several split counts: bf16 and fp32 finished tiles (splits summed by the split fix-up, or
+    by a cluster for shapes too large for the fix-up storage), fp32 split partials;
+    deterministic; finished tiles equal the split-order sum of the partials."""
     from kernels import linear as klin
     from kernels._native import lib, ptr, stream, check
     fx = load("pointwise")
@@ -247,21 +274,46 @@ def test_linear_matches_reference():
         n = weight.shape[0]
         exact = x.float() @ weight.float().T
         chunks = (k + 63) // 64
-        for splits in sorted({1, 2, min(chunks, 7), min(chunks, 8), int(lib.fb_linear_splits(m, n, k)), chunks}):
-            part = torch.empty(splits, m, n, dtype=torch.float32, device=DEV)
-            check(lib.fb_linear(ptr(xd), ptr(wd), ptr(part), m, n, k, 3, splits, stream()), "fb_linear")
-            torch.cuda.synchronize()
-            torch.testing.assert_close(part.sum(0).cpu(), exact, atol=1e-4, rtol=1e-4)
-            if splits > klin.MAX_CLUSTER_SPLITS:
-                continue
-            out = torch.empty(m, n, dtype=torch.float32, device=DEV)
-            check(lib.fb_linear(ptr(xd), ptr(wd), ptr(out), m, n, k, 1, splits, stream()), "fb_linear")
-            torch.cuda.synchronize()
-            torch.testing.assert_close(out.cpu(), exact, atol=1e-4, rtol=1e-4)
-            ordered = part[0].clone()
-            for s in range(1, splits):
-                ordered += part[s]
-            assert torch.equal(out, ordered)  # rank-order cluster sum = split-order sum
+        for splits in sorted({1, 2, min(chunks, 7), min(chunks, 8), min(chunks, 12), min(chunks, 16),
+                              int(lib.fb_linear_splits(m, n, k)), int(lib.fb_linear_finished_splits(m, n, k)),
+                              chunks}):
+            _check_finished_splits(xd, wd, exact, splits)
+
+
+def _check_finished_splits(xd, wd, exact, splits):
+    """Split partials sum to the exact product; a finished fp32 tile over the same splits (fix-up
+    or cluster) equals their split-order sum bit for bit, twice in a row (the fix-up counters
+    return to zero)."""
+    from kernels._native import lib, ptr, stream, check
+    m, k = xd.shape
+    n = wd.shape[0]
+    part = torch.empty(splits, m, n, dtype=torch.float32, device=DEV)
+    check(lib.fb_linear(ptr(xd), ptr(wd), ptr(part), m, n, k, 3, splits, stream()), "fb_linear")
+    torch.cuda.synchronize()
+    torch.testing.assert_close(part.sum(0).cpu(), exact, atol=1e-4, rtol=1e-4)
+    ordered = part[0].clone()
+    for s in range(1, splits):
+        ordered += part[s]
+    for _ in range(2):
+        out = torch.empty(m, n, dtype=torch.float32, device=DEV)
+        status = lib.fb_linear(ptr(xd), ptr(wd), ptr(out), m, n, k, 1, splits, stream())
+        if splits > 16 or (splits > 8 and (n + 127) // 128 * 128 * splits * m > 1 << 22):
+            assert status == -2  # beyond the fix-up and the cluster
+            return
+        check(status, "fb_linear")
+        torch.cuda.synchronize()
+        assert torch.equal(out, ordered)  # split-order sum, fix-up or cluster
+
+
+def test_linear_finished_tiles_cluster_fallback():
+    """A shape too large for the split fix-up storage (64 rows x 512 tiles x S splits > 2^22
+    fp32 values) sums its splits through the thread-block cluster instead: same bits."""
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(64, 256, generator=g).bfloat16()
+    w = (torch.randn(65536, 256, generator=g) * 0.05).bfloat16()
+    exact = x.float() @ w.float().T
+    for splits in (2, 4):
+        _check_finished_splits(x.to(DEV), w.to(DEV), exact, splits)
 
 
 def test_linear_split_result_feeds_consumers():
@@ -278,8 +330,8 @@ def test_linear_split_result_feeds_consumers():
 def test_swiglu_linear_matches_oracle():
     """Projection + SwiGLU on 64-row gate/up blocks equals projecting gate and up separately and
     applying the reference's SwiGLU (swiglu.py:13-24), in every form: the split-partials path
-    with fb_swiglu_blocked (what swiglu_linear picks when the shape needs K splits) and the
-    fused epilogue at one split and over a cluster of splits."""
+    with fb_swiglu_blocked (what swiglu_linear runs by default) and the fused epilogue at one
+    split and over K splits summed by the split fix-up; the split forms agree bit for bit."""
     import qwen3
     from kernels import linear as klin
     g = torch.Generator().manual_seed(11)
@@ -290,13 +342,18 @@ def test_swiglu_linear_matches_oracle():
         blocked = qwen3.interleave_gate_up(gate, up).contiguous().to(DEV)
         expect = opw.swiglu(torch.cat((opw.linear(x, gate), opw.linear(x, up)), -1))
         xd = x.to(DEV)
-        forms = {"swiglu_linear": klin.swiglu_linear(xd, blocked)}
-        for splits in (1, 2):
+        forms = {"swiglu_linear": klin.swiglu_linear(xd, blocked),
+                 "split fix-up": klin.swiglu_linear(xd, blocked, split_consumer=False)}
+        chunks = hidden // 64
+        for splits in sorted({1, 2, min(chunks, 8), min(chunks, 12)}):
+            if splits > 8 and 2 * width * splits * rows > 1 << 22:
+                continue  # beyond the split fix-up storage: a cluster takes at most 8 splits
             forms[f"epilogue S={splits}"] = klin.project(xd, blocked, klin.SWIGLU_OUT, splits)
         for name, got in forms.items():
             got = got.cpu()
             assert (got == expect).float().mean() >= 0.99, name
             torch.testing.assert_close(got.float(), expect.float(), atol=0.015625, rtol=0.016, msg=name)
+        assert torch.equal(forms["swiglu_linear"], forms["split fix-up"])
 
 
 def test_argmax_matches_reference():
@@ -356,3 +413,88 @@ def test_decode_attention_fused_equals_two_launch_and_counters_reset():
         assert torch.equal(second, fused)
         counters = again_ws[-len(lengths) * 8 * 4:].view(torch.int32)
         assert int(counters.abs().sum()) == 0
+
+
+def test_push_producers_single_rank():
+    """The TP all-reduce producers at world 1 (the receive buffer is this GPU's own): every word
+    carries flag epoch + 1 in its high half and the fp32 value bits of x @ W^T in its low half,
+    the same bits for one split, K splits summed by the split fix-up, and split partials +
+    fb_reduce_push (split-order sums)."""
+    import ctypes
+    from kernels import linear as klin
+    from kernels._native import lib, ptr, stream, check
+    g = torch.Generator().manual_seed(21)
+    m, n, k = 16, 4096, 1536
+    x = torch.randn(m, k, generator=g).bfloat16().to(DEV)
+    w = (torch.randn(n, k, generator=g) * 0.05).bfloat16().to(DEV)
+    epoch = torch.full((1,), 9, dtype=torch.int64, device=DEV)
+    exact = x.float() @ w.float().T
+    splits = int(lib.fb_linear_finished_splits(m, n, k))
+    assert splits > 1
+    part = klin.project(x, w, klin.SPLITS_OUT, splits)
+    ordered = part[0].clone()
+    for s in range(1, splits):
+        ordered += part[s]
+    words = {}
+    for name in ("one split", "fix-up", "split consumer"):
+        recv = torch.zeros(1, 1, m, n, dtype=torch.int64, device=DEV)
+        peers = (ctypes.c_void_p * 1)(recv.data_ptr())
+        if name == "split consumer":
+            check(lib.fb_reduce_push(ptr(part), splits, m, n, 1, 0, 0, peers, None, ptr(epoch), stream()),
+                  "fb_reduce_push")
+        else:
+            s = 1 if name == "one split" else splits
+            check(lib.fb_linear_allreduce_push(ptr(x), ptr(w), m, n, k, s, 1, 0, 0, peers, None, ptr(epoch), stream()),
+                  "fb_linear_allreduce_push")
+        torch.cuda.synchronize()
+        halves = recv.view(torch.int32).view(m, n, 2)  # little-endian: [value bits, flag]
+        assert bool((halves[..., 1] == 10).all()), name
+        words[name] = halves[..., 0].contiguous().view(torch.float32)
+        torch.testing.assert_close(words[name], exact, atol=1e-4, rtol=1e-4, msg=name)
+    assert torch.equal(words["fix-up"], ordered)
+    assert torch.equal(words["split consumer"], ordered)
+
+
+@pytest.mark.parametrize("rows,q_heads,kv_heads,hidden", [(16, 4, 1, 4096), (16, 32, 8, 4096), (1, 16, 8, 1024),
+                                                           (33, 8, 2, 512), (64, 32, 8, 1024)])
+def test_linear_qk_rope_equals_two_launch(rows, q_heads, kv_heads, hidden):
+    """fb_linear_qk_rope (qkv projection with QK-norm + RoPE + KV append in its epilogue, K splits
+    summed by the split fix-up) writes the same query and cache bits as the projection's split
+    partials followed by fb_qk_norm_rope_append (mode 0, whole tables), at one split and at the
+    finished-tile split count; other cache slots keep their sentinel."""
+    from kernels import linear as klin
+    from kernels._native import lib, ptr, stream, check
+    g = torch.Generator().manual_seed(rows * 100 + q_heads)
+    d, capacity, pos = 128, 96, 77
+    n = (q_heads + 2 * kv_heads) * d
+    x = torch.randn(rows, hidden, generator=g).bfloat16().to(DEV)
+    w = (torch.randn(n, hidden, generator=g) * 0.05).bfloat16().to(DEV)
+    q_gain = (1 + 0.1 * torch.randn(d, generator=g)).bfloat16().to(DEV)
+    k_gain = (1 + 0.1 * torch.randn(d, generator=g)).bfloat16().to(DEV)
+    cos = torch.randn(capacity, d, generator=g).bfloat16().to(DEV)
+    sin = torch.randn(capacity, d, generator=g).bfloat16().to(DEV)
+    position = torch.tensor([pos], dtype=torch.int64, device=DEV)
+    finished = int(lib.fb_linear_finished_splits(rows, n, hidden))
+    for splits in sorted({1, finished}):
+        outs = []
+        for fused in (True, False):
+            keys = torch.full((rows, kv_heads, capacity, d), 17.0).bfloat16().to(DEV)
+            values = torch.full((rows, kv_heads, capacity, d), 17.0).bfloat16().to(DEV)
+            query = torch.empty(rows, 1, q_heads, d, dtype=torch.bfloat16, device=DEV)
+            if fused:
+                check(lib.fb_linear_qk_rope(ptr(x), ptr(w), rows, n, hidden, splits, ptr(q_gain), ptr(k_gain), 1e-6,
+                                            1e-6, ptr(cos), ptr(sin), ptr(position), ptr(query), ptr(keys),
+                                            ptr(values), q_heads, kv_heads, d, capacity, stream()),
+                      "fb_linear_qk_rope")
+            else:
+                part = klin.project(x, w, klin.SPLITS_OUT, splits)
+                check(lib.fb_qk_norm_rope_append(ptr(part), splits, ptr(q_gain), ptr(k_gain), 1e-6, 1e-6, ptr(cos),
+                                                 ptr(sin), ptr(position), None, ptr(query), ptr(keys), ptr(values),
+                                                 rows, 1, q_heads, kv_heads, d, capacity, 0, 1, stream()),
+                      "fb_qk_norm_rope_append")
+            torch.cuda.synchronize()
+            outs.append((query.cpu(), keys.cpu(), values.cpu()))
+        for name, a, b in zip(("query", "keys", "values"), outs[0], outs[1]):
+            assert torch.equal(a, b), (name, splits)
+        keys = outs[0][1]
+        assert bool((keys[:, :, pos] != 17).any()) and bool((keys[:, :, :pos] == 17).all())

@@ -18,29 +18,38 @@ import qwen3  # noqa: E402
 
 
 def check_push_forms(comm, device, rank, world):
-    """Both all-reduce producers (one-split projection with the push epilogue; split partials +
-    fb_reduce_push) through fb_allreduce_add_rmsnorm: every rank gets the same bits, close to
-    an NCCL all-reduce of the fp32 partials followed by the same add + RMSNorm."""
+    """Every all-reduce producer (one-split projection with the push epilogue; K splits summed
+    by the split fix-up before the push; split partials + fb_reduce_push) through
+    fb_allreduce_add_rmsnorm: every rank gets the same bits, the two split forms agree bit for
+    bit, all close to an NCCL all-reduce of the fp32 partials followed by the same add + RMSNorm."""
     from kernels.rmsnorm import add_rms_norm
-    peers = fdecode.PeerBuffers(comm, 2, 16, 4096, device)
+    forms = ((512, False), (1536, False), (1536, True))  # 8 chunks: one split; 24 chunks: K splits
+    peers = fdecode.PeerBuffers(comm, len(forms), 16, 4096, device)
     epoch = torch.full((1,), 41, dtype=torch.int64, device=device)
     g = torch.Generator(device=device).manual_seed(100 + rank)
     residual = torch.randn(16, 4096, device=device, generator=torch.Generator(device=device).manual_seed(7)).bfloat16()
     gain = torch.ones(4096, device=device).bfloat16()
-    checks = {}
-    for use, k in enumerate((512, 1536)):  # 8 chunks: one split; 24 chunks: split partials + reduce-push
-        x = torch.randn(16, k, device=device, generator=g).bfloat16()
-        weight = (torch.randn(4096, k, device=device, generator=g) * 0.05).bfloat16()
-        fdecode._push_projection(x, weight, comm, peers, use, epoch)
+    checks, outs = {}, {}
+    inputs = {}
+    for use, (k, split_consumer) in enumerate(forms):
+        if k not in inputs:
+            inputs[k] = (torch.randn(16, k, device=device, generator=g).bfloat16(),
+                         (torch.randn(4096, k, device=device, generator=g) * 0.05).bfloat16())
+        x, weight = inputs[k]
+        fdecode._push_projection(x, weight, comm, peers, use, epoch, split_consumer=split_consumer)
         out, summed = fdecode._reduce_add_norm(peers, use, epoch, residual, gain, 1e-6)
         partial = x.float() @ weight.float().T
         dist.all_reduce(partial)
         ref_out, ref_sum = add_rms_norm(partial.bfloat16(), residual, gain, 1e-6)
         gathered = [torch.empty_like(out) for _ in range(world)]
         dist.all_gather(gathered, out)
-        checks[f"K={k} ranks agree"] = all(torch.equal(t, gathered[0]) for t in gathered)
-        checks[f"K={k} vs NCCL"] = bool((out.float() - ref_out.float()).abs().max() <= 0.05) and \
+        name = f"K={k}{' split consumer' if split_consumer else ''}"
+        outs[name] = (out, summed)
+        checks[f"{name} ranks agree"] = all(torch.equal(t, gathered[0]) for t in gathered)
+        checks[f"{name} vs NCCL"] = bool((out.float() - ref_out.float()).abs().max() <= 0.05) and \
             bool((summed.float() - ref_sum.float()).abs().max() <= 0.05)
+    checks["fix-up == split consumer"] = all(torch.equal(a, b) for a, b in
+                                             zip(outs["K=1536"], outs["K=1536 split consumer"]))
     torch.cuda.synchronize()
     return checks
 
