@@ -412,6 +412,7 @@ def main():
     step_frac = step_bytes / (ms_per_step / 1e3) / 1e9 / peak
     assert _native.device_error() == 0, "a kernel raised the device error word"
     state.release()
+    multicast = bool(state.peers is not None and state.peers.multicast)
     del state
     torch.cuda.empty_cache()
 
@@ -429,7 +430,10 @@ def main():
     if clock:
         line["clocks"] = clock
     if world > 1:
-        line["allreduce"] = "fused: projection epilogue pushes fp32 tiles to peers over NVLink (symmetric memory, no multicast); consumer sums ranks in order + add/RMSNorm"
+        line["allreduce"] = ("flagged fp32 words pushed by the producer (split partials + fb_reduce_push, or the "
+                             "projection's epilogue at one split) into every rank's symmetric-memory receive buffer "
+                             + ("through the NVSwitch multicast address (multimem.st)" if multicast else
+                                "by NVLink peer stores") + "; consumer polls, sums ranks in order + add/RMSNorm")
 
     if world == 1 and not args.no_sweep:
         line["attention_sweep"] = attention_sweep(peak)

@@ -894,8 +894,10 @@ int launch_cluster_form(const CUtensorMap& km, const CUtensorMap& vm, const Para
   }
   const int c4 = cluster_size<D, kStages>(pairs, 8);
   if (c4 >= 2 && 3 * pairs * c4 >= 2 * sm_count()) return launch_cluster<D, kStages>(km, vm, p, c4, s);
-  const int c3 = cluster_size<D, 3>(pairs, 8);
-  const int c2 = cluster_size<D, kClusterStages>(pairs, 8);
+  // clusters of 16 (non-portable) only when clusters of 8 would leave half the SMs idle
+  const int limit = 2 * pairs * 8 <= sm_count() ? kMaxCluster : 8;
+  const int c3 = cluster_size<D, 3>(pairs, limit);
+  const int c2 = cluster_size<D, kClusterStages>(pairs, limit);
   if (c3 > c4 && c3 >= c2) return launch_cluster<D, 3>(km, vm, p, c3, s);
   if (c2 > c4) return launch_cluster<D, kClusterStages>(km, vm, p, c2, s);
   if (c4 >= 2) return launch_cluster<D, kStages>(km, vm, p, c4, s);

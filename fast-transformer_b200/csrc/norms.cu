@@ -22,6 +22,8 @@ constexpr int kMaxWorld = 8;      // tensor-parallel ranks summed by mode 3
 // 8 consecutive logical bf16 values starting at element `off` of a tensor that is either
 // bf16 (splits == 0) or fp32 split partials [splits, slab] (splits >= 1). Up to eight slabs
 // are loaded before they are added (in split order), so S <= 8 costs one memory round trip.
+__device__ __forceinline__ void sum8_fp32(const float* f, int splits, size_t slab, float (&x)[8]);
+
 __device__ __forceinline__ void load8(const void* src, int splits, size_t slab, size_t off,
                                       float (&x)[8]) {
   if (splits == 0) {
@@ -36,7 +38,13 @@ __device__ __forceinline__ void load8(const void* src, int splits, size_t slab, 
     x[7] = bf16_hi(w.w);
     return;
   }
-  const float* f = static_cast<const float*>(src) + off;
+  sum8_fp32(static_cast<const float*>(src) + off, splits, slab, x);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) x[e] = bf16_round(x[e]);
+}
+
+// The fp32 sum, in split order, of 8 consecutive values of `splits` slabs (no rounding).
+__device__ __forceinline__ void sum8_fp32(const float* f, int splits, size_t slab, float (&x)[8]) {
   for (int s0 = 0; s0 < splits; s0 += kSlabBatch) {
     float4 c[kSlabBatch], d[kSlabBatch];
 #pragma unroll
@@ -69,8 +77,6 @@ __device__ __forceinline__ void load8(const void* src, int splits, size_t slab, 
       }
     }
   }
-#pragma unroll
-  for (int e = 0; e < 8; ++e) x[e] = bf16_round(x[e]);
 }
 
 __device__ __forceinline__ void store8(__nv_bfloat16* dst, const float (&y)[8]) {
@@ -155,11 +161,16 @@ __device__ __forceinline__ bool load8_flagged(const uint64_t* src, int world, si
 
 // mode 0: rms_norm(x)          mode 1: add_rms_norm(x, residual)
 // mode 2: embed + rms_norm     mode 3: tensor-parallel all-reduce + add_rms_norm
+// mode 4: mode 3 preceded by this rank's push (fb_reduce_push fused in)
 //
 // Mode 3: every rank's projection pushed its fp32 [rows, W] partial, as flagged words, into
 // slab `rank` of this rank's receive buffer; once every word carries this step's flag the
 // slabs are summed in rank order (identical bits on every rank), rounded to bf16 (the
 // projection's output) and fed to add_rms_norm's arithmetic.
+// Mode 4: each thread first sums its chunks of this rank's fp32 split partials in split order
+// and pushes them, as flagged words, into slab `rank` of every rank's receive buffer (peer
+// stores, or one multimem store each through the multicast address), then runs mode 3 on the
+// same chunks. A chunk's push never waits, so every rank's pushes precede its polls.
 struct Params {
   const void* x;          // mode 3: this use's receive slabs, uint64 words [world, rows, W]
   int splits;             // fp32 slabs in x (0: x is bf16); mode 3: world
@@ -170,11 +181,39 @@ struct Params {
   __nv_bfloat16* sum;
   const int64_t* ids;     // mode 2
   int64_t vocab;
-  const int64_t* epoch;   // mode 3: the flag is (uint32)(*epoch) + 1
+  const int64_t* epoch;   // modes 3-4: the flag is (uint32)(*epoch) + 1
   int rows, width;
   float eps;
   unsigned* err;
+  // mode 4: this rank's split partials [psplits, rows, W] and where its slab goes
+  const float* partials;
+  int psplits, use, world, rank;
+  uint64_t* peer_recv[kMaxWorld];  // every rank's receive buffer (all uses)
+  uint64_t* mc_recv;               // their multicast address, or null
 };
+
+// Mode 4 push of one chunk: 8 fp32 values as flagged words into slab `rank` of recv[use] of
+// every rank; consecutive threads' chunks are consecutive, so a warp writes 2 KB contiguous.
+__device__ __forceinline__ void push8(const Params& p, size_t off, uint32_t flag, const float (&x)[8]) {
+  const uint64_t hi = static_cast<uint64_t>(flag) << 32;
+  uint64_t w[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) w[e] = hi | __float_as_uint(x[e]);
+  const size_t slab = static_cast<size_t>(p.rows) * p.width;
+  const size_t dst = (static_cast<size_t>(p.use) * p.world + p.rank) * slab + off;
+  if (p.mc_recv != nullptr) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      asm volatile("multimem.st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p.mc_recv + dst + e), "l"(w[e]) : "memory");
+    return;
+  }
+  for (int q = 0; q < p.world; ++q) {
+    uint64_t* d = p.peer_recv[q] + dst;
+#pragma unroll
+    for (int e = 0; e < 8; e += 2)
+      asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(d + e), "l"(w[e]), "l"(w[e + 1]) : "memory");
+  }
+}
 
 // Grid: rows * C CTAs, clusters of C (C = gridDim.x / rows) along x; CTA `rank` of a row's
 // cluster owns chunks [rank * per, (rank + 1) * per) of the row (8 values per chunk), each
@@ -214,23 +253,34 @@ __global__ void __launch_bounds__(kMaxThreads) rmsnorm_kernel(const Params p) {
     }
     base = static_cast<size_t>(id) * p.width;
   }
-  const uint32_t flag = MODE == 3 ? static_cast<uint32_t>(*p.epoch) + 1u : 0u;
-  const int split_count = (MODE == 1 || MODE == 3) ? p.splits : 0;
+  const uint32_t flag = MODE >= 3 ? static_cast<uint32_t>(*p.epoch) + 1u : 0u;
+  const int split_count = (MODE == 1 || MODE >= 3) ? p.splits : 0;
   const size_t slab = static_cast<size_t>(p.rows) * p.width;
+  if (MODE == 4) {
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i) {
+      const int ch = c0 + threadIdx.x + i * T;
+      if (ch < c1) {
+        float part[8];
+        sum8_fp32(p.partials + base + ch * 8, p.psplits, slab, part);
+        push8(p, base + ch * 8, flag, part);
+      }
+    }
+  }
   float v[kMaxPer][8];
   float ss = 0.f;
 #pragma unroll
   for (int i = 0; i < kMaxPer; ++i) {
     const int ch = c0 + threadIdx.x + i * T;
     if (ch < c1) {
-      if (MODE == 3) {
+      if (MODE >= 3) {
         if (!load8_flagged(static_cast<const uint64_t*>(src) + base + ch * 8, p.splits, slab, flag, p.err, v[i]))
 #pragma unroll
           for (int e = 0; e < 8; ++e) v[i][e] = 0.f;
       } else {
         load8(src, split_count, slab, base + ch * 8, v[i]);
       }
-      if (MODE == 1 || MODE == 3) {
+      if (MODE == 1 || MODE >= 3) {
         float r[8];
         load8(p.residual, 0, 0, static_cast<size_t>(row) * p.width + ch * 8, r);
 #pragma unroll
@@ -513,4 +563,39 @@ extern "C" int fb_allreduce_add_rmsnorm(const void* recv, int use, int world, co
   p.eps = eps;
   p.err = error_word();
   return norm::launch_rmsnorm<3>(p, stream);
+}
+
+extern "C" int fb_reduce_push_add_rmsnorm(const void* partials, int splits, void* const* peer_recv,
+                                          void* multicast_recv, const void* recv, int use, int world, int rank,
+                                          const int64_t* epoch, const void* residual, const void* w, void* out,
+                                          void* sum, int rows, int width, float eps, void* stream) {
+  if (!partials || !peer_recv || !recv || !epoch || !residual || !w || !out || !sum || splits <= 0)
+    return FB_ERR_ARG;
+  if (use < 0 || world < 1 || world > norm::kMaxWorld || rank < 0 || rank >= world || rows <= 0) return FB_ERR_ARG;
+  for (int q = 0; q < world; ++q)
+    if (!peer_recv[q] || (reinterpret_cast<uintptr_t>(peer_recv[q]) & 15u)) return FB_ERR_ARG;
+  if (multicast_recv != nullptr && (reinterpret_cast<uintptr_t>(multicast_recv) & 15u)) return FB_ERR_ARG;
+  int st = norm::check_width(width);
+  if (st != FB_OK) return st;
+  const size_t slab = static_cast<size_t>(rows) * width;
+  norm::Params p{};
+  p.x = static_cast<const uint64_t*>(recv) + static_cast<size_t>(use) * world * slab;
+  p.splits = world;
+  p.epoch = epoch;
+  p.residual = static_cast<const __nv_bfloat16*>(residual);
+  p.w = static_cast<const __nv_bfloat16*>(w);
+  p.y = static_cast<__nv_bfloat16*>(out);
+  p.sum = static_cast<__nv_bfloat16*>(sum);
+  p.rows = rows;
+  p.width = width;
+  p.eps = eps;
+  p.err = error_word();
+  p.partials = static_cast<const float*>(partials);
+  p.psplits = splits;
+  p.use = use;
+  p.world = world;
+  p.rank = rank;
+  for (int q = 0; q < world; ++q) p.peer_recv[q] = static_cast<uint64_t*>(peer_recv[q]);
+  p.mc_recv = static_cast<uint64_t*>(multicast_recv);
+  return norm::launch_rmsnorm<4>(p, stream);
 }

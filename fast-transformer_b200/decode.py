@@ -22,6 +22,7 @@ bit-identical data. Prefill (eager, untimed) uses NCCL all-reduces.
 import ctypes
 
 import math
+import os
 
 import torch
 import torch.nn.functional as F
@@ -92,12 +93,16 @@ class PeerBuffers:
     address for NVLink peer stores and, where the driver binds the buffers to an NVSwitch
     multicast object, its multicast address (one store reaches every rank).
 
-    FB_TP_MULTICAST=0 keeps plain peer mappings only (no multicast object), e.g. for runs that
-    may lose a rank: a rank that dies while bound to a multicast object can fault its peers."""
+    Plain peer mappings (no multicast object) by default; FB_TP_MULTICAST=1 asks for the
+    multicast object and its address. Measured on B200 (Qwen3-8B, B=16, one multimem.st per
+    flagged 8-byte word): TP2 4164 tok/s either way, but TP4 4324 and TP8 3351 tok/s with
+    multicast stores against 5986 and 6334 with peer stores. Peer mappings are also the safe
+    choice for runs that may lose a rank: a rank that dies while bound to a multicast object
+    can fault its peers."""
 
     def __init__(self, comm, uses, rows, width, device):
         import os
-        if os.environ.get("FB_TP_MULTICAST", "1") == "0":
+        if os.environ.get("FB_TP_MULTICAST", "0") != "1":
             os.environ["TORCH_SYMM_MEM_DISABLE_MULTICAST"] = "1"
         import torch.distributed._symmetric_memory as symm_mem
         world = comm.size
@@ -179,37 +184,54 @@ def _qkv_rope_decode(x, layer, eps, cos, sin, position, keys, values, q_heads):
 #: alone: TP1 6172 against 6295 us, TP8 1990 against 2350 us): the consumer runs while the
 #: next projection's CTAs already stream their weights, whereas the fix-up's last CTA per
 #: tile holds its SM until the tile is summed.
-FINISH_SPLITS_IN_PROJECTION = False
+FINISH_SPLITS_IN_PROJECTION = os.environ.get("FB_FINISH_SPLITS_IN_PROJECTION", "0") == "1"
+#: The split-consumer all-reduce: "reduce_push" (fb_reduce_push + fb_allreduce_add_rmsnorm,
+#: the default) or "fused" (fb_reduce_push_add_rmsnorm: push and consumer in one launch).
+#: Measured on 4 B200s (config 4, same box): reduce_push 5817 tok/s, fused 4914, the split
+#: fix-up push epilogue + consumer 4937 - pushing from the kernel that then polls, or from
+#: the projection's last CTA per tile, costs ~7 us per all-reduce more than a separate
+#: push kernel.
+ALLREDUCE_FORM = os.environ.get("FB_TP_ALLREDUCE", "reduce_push")
 
 
-def _push_projection(x, weight, comm, peers, use, epoch, split_consumer=None):
-    """This rank's fp32 partial of x @ W^T, pushed to every rank's recv[use] flagged with
-    epoch + 1: split partials + fb_reduce_push (``split_consumer``, the default), or
-    fb_linear_allreduce_push with the K splits summed in its launch. One split (K < 256)
-    always pushes from the projection's epilogue. Graph-timed at TP8 (o_proj, K = 512): 4.3 us
-    for 2 splits + fb_reduce_push against 5.0 us for one split with the push epilogue."""
+def _allreduce_add_norm(x, weight, comm, peers, use, epoch, residual, gain, eps, split_consumer=None, splits=None):
+    """(normalized, summed) = add_rms_norm(all-reduce over ranks of x @ W^T, residual): every
+    rank pushes its fp32 partial into recv[use] of every rank, flagged with epoch + 1, and
+    polls its own recv[use] for all ranks' slabs. With K splits (the default,
+    ``split_consumer``) the projection writes split partials, then fb_reduce_push +
+    fb_allreduce_add_rmsnorm (ALLREDUCE_FORM "reduce_push") or fb_reduce_push_add_rmsnorm
+    ("fused"); at one split, or with the K splits summed by the split fix-up, the projection's
+    push epilogue (fb_linear_allreduce_push) + fb_allreduce_add_rmsnorm. The same bits in every
+    form. ``splits`` overrides the K-split count (tests)."""
     if split_consumer is None:
         split_consumer = not FINISH_SPLITS_IN_PROJECTION
     rows = x.numel() // x.shape[-1]
     flat = x.reshape(rows, x.shape[-1]).contiguous()
     n, k = weight.shape
-    splits = klinear.splits_for(rows, n, k, x.device, finished=True)
-    if splits == 1 or not split_consumer:
-        check(lib.fb_linear_allreduce_push(ptr(flat), ptr(weight), rows, n, k, splits, comm.size, comm.rank, use,
-                                           peers.recv_ptrs, peers.mc_ptr, ptr(epoch), stream()),
-              "fb_linear_allreduce_push")
-        return
-    partials = klinear.project(flat, weight, klinear.SPLITS_OUT, splits)
-    check(lib.fb_reduce_push(ptr(partials), splits, rows, n, comm.size, comm.rank, use, peers.recv_ptrs, peers.mc_ptr,
-                             ptr(epoch), stream()), "fb_reduce_push")
-
-
-def _reduce_add_norm(peers, use, epoch, residual, weight, eps):
-    """(normalized, summed) = add_rms_norm(all-reduced recv[use], residual) (fb_allreduce_add_rmsnorm)."""
-    rows, width = residual.numel() // residual.shape[-1], residual.shape[-1]
+    width = residual.shape[-1]
     out = torch.empty_like(residual)
     summed = torch.empty_like(residual)
-    check(lib.fb_allreduce_add_rmsnorm(peers.recv_local, use, peers.world, ptr(epoch), ptr(residual), ptr(weight),
+    if splits is None:
+        splits = klinear.splits_for(rows, n, k, x.device, finished=not split_consumer)
+    if splits > 1 and split_consumer and ALLREDUCE_FORM == "reduce_push":
+        partials = klinear.project(flat, weight, klinear.SPLITS_OUT, splits)
+        check(lib.fb_reduce_push(ptr(partials), splits, rows, n, comm.size, comm.rank, use, peers.recv_ptrs,
+                                 peers.mc_ptr, ptr(epoch), stream()), "fb_reduce_push")
+        check(lib.fb_allreduce_add_rmsnorm(peers.recv_local, use, peers.world, ptr(epoch), ptr(residual),
+                                           ptr(gain), ptr(out), ptr(summed), rows, width, float(eps), stream()),
+              "fb_allreduce_add_rmsnorm")
+        return out, summed
+    if splits > 1 and split_consumer:
+        partials = klinear.project(flat, weight, klinear.SPLITS_OUT, splits)
+        check(lib.fb_reduce_push_add_rmsnorm(ptr(partials), splits, peers.recv_ptrs, peers.mc_ptr, peers.recv_local,
+                                             use, peers.world, comm.rank, ptr(epoch), ptr(residual), ptr(gain),
+                                             ptr(out), ptr(summed), rows, width, float(eps), stream()),
+              "fb_reduce_push_add_rmsnorm")
+        return out, summed
+    check(lib.fb_linear_allreduce_push(ptr(flat), ptr(weight), rows, n, k, splits, comm.size, comm.rank, use,
+                                       peers.recv_ptrs, peers.mc_ptr, ptr(epoch), stream()),
+          "fb_linear_allreduce_push")
+    check(lib.fb_allreduce_add_rmsnorm(peers.recv_local, use, peers.world, ptr(epoch), ptr(residual), ptr(gain),
                                        ptr(out), ptr(summed), rows, width, float(eps), stream()),
           "fb_allreduce_add_rmsnorm")
     return out, summed
@@ -273,15 +295,15 @@ class DecodeState:
                 out = linear(attention, layer.o, split_ok=True)
                 normalized, residual = add_rms_norm(out, residual, layer.ln2, eps)
             else:
-                _push_projection(attention, layer.o, comm, peers, 2 * index, self.position)
-                normalized, residual = _reduce_add_norm(peers, 2 * index, self.position, residual, layer.ln2, eps)
+                normalized, residual = _allreduce_add_norm(attention, layer.o, comm, peers, 2 * index, self.position,
+                                                           residual, layer.ln2, eps)
             activated = swiglu_linear(normalized, layer.gate_up, split_consumer=not FINISH_SPLITS_IN_PROJECTION)
             if peers is None:
                 hidden = linear(activated, layer.down, split_ok=True)
             else:
-                _push_projection(activated, layer.down, comm, peers, 2 * index + 1, self.position)
                 following = layers[index + 1].ln1 if index + 1 < len(layers) else w.final_norm
-                normalized, residual = _reduce_add_norm(peers, 2 * index + 1, self.position, residual, following, eps)
+                normalized, residual = _allreduce_add_norm(activated, layer.down, comm, peers, 2 * index + 1,
+                                                           self.position, residual, following, eps)
         if peers is None:
             normalized, _ = add_rms_norm(hidden, residual, w.final_norm, eps)
         if keep_logits:

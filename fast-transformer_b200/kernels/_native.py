@@ -63,6 +63,8 @@ _SIGNATURES = {
     "fb_merge_splits": (_c_int, [_vp, _c_int, _c_i64, _vp, _c_int, _vp]),
     "fb_swiglu_blocked": (_c_int, [_vp, _c_int, _vp, _c_int, _c_int, _vp]),
     "fb_reduce_push": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp, _vp]),
+    "fb_reduce_push_add_rmsnorm": (_c_int, [_vp, _c_int, _vp, _vp, _vp, _c_int, _c_int, _c_int, _vp, _vp, _vp, _vp,
+                                            _vp, _c_int, _c_int, _c_float, _vp]),
     "fb_prefill_attention": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float,
                                       _vp]),
     "fb_spec_propose": (_c_int, [_vp, _c_i64, _vp, _vp, _c_i64, _c_int, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int,

@@ -330,6 +330,16 @@ int fb_reduce_push(const void* partials, int splits, int m, int n, int world, in
 int fb_allreduce_add_rmsnorm(const void* recv, int use, int world, const int64_t* epoch,
                              const void* residual, const void* w, void* out, void* sum, int rows,
                              int width, float eps, void* stream);
+/* Producer and consumer in one launch: sums this rank's fp32 split partials [splits, rows,
+ * width] in split order, pushes every value into slab `rank` of recv[use] on every rank
+ * exactly like fb_reduce_push (peer_recv / multicast_recv), then, on the same columns, runs
+ * fb_allreduce_add_rmsnorm on this rank's receive buffer `recv`. Same bits as
+ * fb_reduce_push + fb_allreduce_add_rmsnorm, one launch fewer. Every rank's CTAs push before
+ * they poll, so the ranks cannot wait on one another's launches. */
+int fb_reduce_push_add_rmsnorm(const void* partials, int splits, void* const* peer_recv, void* multicast_recv,
+                               const void* recv, int use, int world, int rank, const int64_t* epoch,
+                               const void* residual, const void* w, void* out, void* sum, int rows, int width,
+                               float eps, void* stream);
 
 /* Sums fp32 split partials [splits, count] into bf16 [count] (or fp32 when out_fp32):
  * the reference's `_merge_projection` (linear.py:81-93). */

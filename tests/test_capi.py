@@ -74,6 +74,9 @@ def test_host_validation_without_gpu():
     assert lib.fb_reduce_push(p, 2, 4, 8, 2, 2, 0, peers, null, p, null) == -1
     odd = (ctypes.c_void_p * 2)(16, 40)
     assert lib.fb_reduce_push(p, 2, 4, 8, 2, 0, 0, odd, null, p, null) == -1
+    assert lib.fb_reduce_push_add_rmsnorm(p, 2, peers, null, p, 0, 2, 2, p, p, p, p, p, 4, 4096, 1e-6, null) == -1
+    assert lib.fb_reduce_push_add_rmsnorm(p, 2, odd, null, p, 0, 2, 0, p, p, p, p, p, 4, 4096, 1e-6, null) == -1
+    assert lib.fb_reduce_push_add_rmsnorm(p, 2, peers, null, p, 0, 2, 0, p, p, p, p, p, 4, 4100, 1e-6, null) == -2
     assert lib.fb_linear_argmax(p, p, 4, 128, 128, -1, p, null) == -1
     # workspace too small -> FB_ERR_WORKSPACE
     need = lib.fb_decode_attention_workspace(1, 16, 8, 128, 148)

@@ -498,3 +498,40 @@ def test_linear_qk_rope_equals_two_launch(rows, q_heads, kv_heads, hidden):
             assert torch.equal(a, b), (name, splits)
         keys = outs[0][1]
         assert bool((keys[:, :, pos] != 17).any()) and bool((keys[:, :, :pos] == 17).all())
+
+
+def test_reduce_push_add_rmsnorm_single_rank():
+    """fb_reduce_push_add_rmsnorm at world 1 (the push lands in this GPU's own receive buffer,
+    then the same kernel polls it): the same bits as add_rms_norm over the split partials
+    (fb_add_rmsnorm: split-order fp32 sum, bf16, + residual, RMSNorm), and every pushed word
+    carries flag epoch + 1 with the split-order fp32 sum."""
+    import ctypes
+    from kernels import linear as klin
+    from kernels._native import lib, ptr, stream, check
+    g = torch.Generator().manual_seed(31)
+    rows, width, k = 16, 4096, 1536
+    x = torch.randn(rows, k, generator=g).bfloat16().to(DEV)
+    w = (torch.randn(width, k, generator=g) * 0.05).bfloat16().to(DEV)
+    residual = torch.randn(rows, width, generator=g).bfloat16().to(DEV)
+    gain = (1 + 0.1 * torch.randn(width, generator=g)).bfloat16().to(DEV)
+    epoch = torch.full((1,), 12, dtype=torch.int64, device=DEV)
+    for splits in (1, 2, 6, 11):
+        part = klin.project(x, w, klin.SPLITS_OUT, splits)
+        ordered = part[0].clone()
+        for s in range(1, splits):
+            ordered += part[s]
+        recv = torch.zeros(2, 1, rows, width, dtype=torch.int64, device=DEV)  # two uses; use 1 is pushed
+        peers = (ctypes.c_void_p * 1)(recv.data_ptr())
+        out, summed = torch.empty_like(residual), torch.empty_like(residual)
+        check(lib.fb_reduce_push_add_rmsnorm(ptr(part), splits, peers, None, ptr(recv), 1, 1, 0, ptr(epoch),
+                                             ptr(residual), ptr(gain), ptr(out), ptr(summed), rows, width, 1e-6,
+                                             stream()), "fb_reduce_push_add_rmsnorm")
+        e_out, e_sum = torch.empty_like(residual), torch.empty_like(residual)
+        check(lib.fb_add_rmsnorm(ptr(part), splits, ptr(residual), ptr(gain), ptr(e_out), ptr(e_sum), rows, width,
+                                 1e-6, stream()), "fb_add_rmsnorm")
+        torch.cuda.synchronize()
+        assert torch.equal(out, e_out) and torch.equal(summed, e_sum), splits
+        halves = recv[1].view(torch.int32).view(rows, width, 2)
+        assert bool((halves[..., 1] == 13).all())
+        assert torch.equal(halves[..., 0].contiguous().view(torch.float32), ordered)
+        assert bool((recv[0] == 0).all())  # other uses untouched

@@ -18,38 +18,54 @@ import qwen3  # noqa: E402
 
 
 def check_push_forms(comm, device, rank, world):
-    """Every all-reduce producer (one-split projection with the push epilogue; K splits summed
-    by the split fix-up before the push; split partials + fb_reduce_push) through
-    fb_allreduce_add_rmsnorm: every rank gets the same bits, the two split forms agree bit for
-    bit, all close to an NCCL all-reduce of the fp32 partials followed by the same add + RMSNorm."""
+    """Every all-reduce form through the add+RMSNorm consumer: split partials + the fused push /
+    all-reduce / add+RMSNorm kernel (the decode default), split partials + fb_reduce_push +
+    fb_allreduce_add_rmsnorm, the projection's push epilogue at one split and with its K splits
+    summed by the split fix-up. Every rank gets the same bits, forms over the same K splits
+    agree bit for bit, and all are close to an NCCL all-reduce of the fp32 partials followed
+    by the same add + RMSNorm."""
+    from kernels import linear as klinear
+    from kernels._native import check, lib, ptr, stream
     from kernels.rmsnorm import add_rms_norm
-    forms = ((512, False), (1536, False), (1536, True))  # 8 chunks: one split; 24 chunks: K splits
+    forms = (("fused", 512, None), ("one split", 512, 1), ("fix-up", 512, None),
+             ("fused", 1536, None), ("reduce-push", 1536, None), ("fix-up", 1536, None))
     peers = fdecode.PeerBuffers(comm, len(forms), 16, 4096, device)
     epoch = torch.full((1,), 41, dtype=torch.int64, device=device)
     g = torch.Generator(device=device).manual_seed(100 + rank)
     residual = torch.randn(16, 4096, device=device, generator=torch.Generator(device=device).manual_seed(7)).bfloat16()
     gain = torch.ones(4096, device=device).bfloat16()
-    checks, outs = {}, {}
-    inputs = {}
-    for use, (k, split_consumer) in enumerate(forms):
+    checks, outs, inputs = {}, {}, {}
+    for use, (form, k, splits) in enumerate(forms):
         if k not in inputs:
             inputs[k] = (torch.randn(16, k, device=device, generator=g).bfloat16(),
                          (torch.randn(4096, k, device=device, generator=g) * 0.05).bfloat16())
         x, weight = inputs[k]
-        fdecode._push_projection(x, weight, comm, peers, use, epoch, split_consumer=split_consumer)
-        out, summed = fdecode._reduce_add_norm(peers, use, epoch, residual, gain, 1e-6)
+        if form == "reduce-push":
+            s = klinear.splits_for(16, 4096, k, device)
+            part = klinear.project(x, weight, klinear.SPLITS_OUT, s)
+            check(lib.fb_reduce_push(ptr(part), s, 16, 4096, world, rank, use, peers.recv_ptrs, peers.mc_ptr,
+                                     ptr(epoch), stream()), "fb_reduce_push")
+            out, summed = torch.empty_like(residual), torch.empty_like(residual)
+            check(lib.fb_allreduce_add_rmsnorm(peers.recv_local, use, world, ptr(epoch), ptr(residual), ptr(gain),
+                                               ptr(out), ptr(summed), 16, 4096, 1e-6, stream()),
+                  "fb_allreduce_add_rmsnorm")
+        else:
+            out, summed = fdecode._allreduce_add_norm(x, weight, comm, peers, use, epoch, residual, gain, 1e-6,
+                                                      split_consumer=form == "fused", splits=splits)
         partial = x.float() @ weight.float().T
         dist.all_reduce(partial)
         ref_out, ref_sum = add_rms_norm(partial.bfloat16(), residual, gain, 1e-6)
         gathered = [torch.empty_like(out) for _ in range(world)]
         dist.all_gather(gathered, out)
-        name = f"K={k}{' split consumer' if split_consumer else ''}"
+        name = f"K={k} {form}"
         outs[name] = (out, summed)
         checks[f"{name} ranks agree"] = all(torch.equal(t, gathered[0]) for t in gathered)
         checks[f"{name} vs NCCL"] = bool((out.float() - ref_out.float()).abs().max() <= 0.05) and \
             bool((summed.float() - ref_sum.float()).abs().max() <= 0.05)
-    checks["fix-up == split consumer"] = all(torch.equal(a, b) for a, b in
-                                             zip(outs["K=1536"], outs["K=1536 split consumer"]))
+    for k in (512, 1536):
+        same = [outs[f"K={k} fused"], outs[f"K={k} fix-up"]] + ([outs["K=1536 reduce-push"]] if k == 1536 else [])
+        checks[f"K={k} split forms equal"] = all(torch.equal(a[0], same[0][0]) and torch.equal(a[1], same[0][1])
+                                                 for a in same)
     torch.cuda.synchronize()
     return checks
 
@@ -64,7 +80,7 @@ def main():
         comm0 = fdecode.Communicator(dist.group.WORLD, world, rank)
         push_checks = check_push_forms(comm0, device, rank, world)
         if rank == 0:
-            print("push forms", push_checks, "multicast" if os.environ.get("FB_TP_MULTICAST", "1") != "0" else "peer stores",
+            print("push forms", push_checks, "multicast" if os.environ.get("FB_TP_MULTICAST", "0") == "1" else "peer stores",
                   flush=True)
         ok = all(push_checks.values())
         fx = torch.load(os.path.join(HERE, "golden", "model.pt"), weights_only=False)
@@ -98,7 +114,7 @@ def main():
                 "ranks agree": all(torch.equal(t, gathered[0]) for t in gathered),
                 "logits": bool(err <= 2e-2 * scale),
             }
-            if os.environ.get("FB_TP_MULTICAST", "1") == "0":
+            if os.environ.get("FB_TP_MULTICAST", "0") != "1":
                 checks["no multicast"] = not graph_state.peers.multicast
             else:
                 checks["multicast used"] = graph_state.peers.multicast
