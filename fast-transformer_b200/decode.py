@@ -95,8 +95,8 @@ class PeerBuffers:
 
     Plain peer mappings (no multicast object) by default; FB_TP_MULTICAST=1 asks for the
     multicast object and its address. Measured on B200 (Qwen3-8B, B=16, one multimem.st per
-    flagged 8-byte word): TP2 4164 tok/s either way, but TP4 4324 and TP8 3351 tok/s with
-    multicast stores against 5986 and 6334 with peer stores. Peer mappings are also the safe
+    flagged 8-byte word, otherwise identical code): TP2 4164 tok/s against 4156 with peer
+    stores, TP4 4324 against 5817, TP8 3351 against 6406. Peer mappings are also the safe
     choice for runs that may lose a rank: a rank that dies while bound to a multicast object
     can fault its peers."""
 
