@@ -4,9 +4,10 @@
 // projection's own arithmetic, as a single-split epilogue would see it) and stores every
 // value, as one 8-byte word with the flag (uint32)(*epoch) + 1 in its high half, into slab
 // `rank` of recv[use] on every rank - the low-latency push protocol that
-// fb_allreduce_add_rmsnorm polls. Used instead of a finished-tile push epilogue when the
-// projection needs K splits: on B200 a cluster reduction of the splits inside the
-// projection measured 3-5 us slower than split partials plus this pass.
+// fb_allreduce_add_rmsnorm polls. The decode step's producer whenever the projection has K
+// splits: on B200, summing the splits inside the projection (cluster reduction or the split
+// fix-up) and pushing from its epilogue, or pushing from the polling kernel itself
+// (fb_reduce_push_add_rmsnorm), each measured slower than split partials plus this pass.
 #include "common.cuh"
 
 namespace fb {
