@@ -210,7 +210,8 @@ def step(args):
     cfg = qwen3.Config.make(**qwen3.PRESETS[args.preset])
     # --tp-size N: one rank's shard shapes (rank 0 of N), run alone, for per-kernel times at TP N
     # (the all-reduce consumers then run as the single-rank add+norm)
-    fdecode.FINISH_SPLITS_IN_PROJECTION = not args.split_consumers
+    if args.finish_in_projection:
+        fdecode.FINISH_SPLITS_IN_PROJECTION = True
     weights = qwen3.random_init(cfg, "cuda", seed=0, tp_rank=0, tp_size=args.tp_size)
     state = fdecode.DecodeState(weights, args.batch, args.length, 8)
     # decode cost does not depend on cache contents: random K/V instead of a prefill
@@ -235,7 +236,7 @@ def step(args):
         end.record()
         end.synchronize()
         ms = start.elapsed_time(end) / 20
-        form = "split consumers" if args.split_consumers else "splits finished in the projections"
+        form = "splits finished in the projections" if fdecode.FINISH_SPLITS_IN_PROJECTION else "split consumers"
         print(f"step {args.preset} TP-shard 1/{args.tp_size} B={args.batch} L={args.length} ({form}): "
               f"{ms * 1e3:.1f} us per captured step ({args.batch / ms * 1e3:.0f} tok/s for this shard alone)")
         state.release()
@@ -262,8 +263,9 @@ def main():
     parser.add_argument("--preset", default="qwen3-8b")
     parser.add_argument("--tp-size", type=int, default=1)
     parser.add_argument("--timed", action="store_true", help="step: time the captured step instead of profiling")
-    parser.add_argument("--split-consumers", action="store_true",
-                        help="step: finish K splits in consumer kernels instead of in the projections")
+    parser.add_argument("--finish-in-projection", action="store_true",
+                        help="step: finish K splits inside the projections (split fix-up) instead of in consumer "
+                             "kernels (the decode default)")
     parser.add_argument("--copies", type=int, default=2)
     parser.add_argument("--shapes", default="", help="attention: cluster-form shapes to sweep, e.g. 8x2,8x3,16x2")
     parser.add_argument("--launches", type=int, default=2)
