@@ -89,7 +89,7 @@ def linear(args):
     from kernels.linear import SPLITS_OUT, project, splits_for
     x = torch.randn(args.m, args.k, device="cuda").bfloat16()
     weights = [(torch.randn(args.n, args.k, device="cuda") * 0.02).bfloat16() for _ in range(args.copies)]
-    splits = splits_for(args.m, args.n, args.k, x.device, finished=args.epilogue != SPLITS_OUT)
+    splits = args.splits or splits_for(args.m, args.n, args.k, x.device, finished=args.epilogue != SPLITS_OUT)
 
     def run():
         for w in weights:
@@ -260,6 +260,7 @@ def main():
     parser.add_argument("--n", type=int, default=24576)
     parser.add_argument("--k", type=int, default=4096)
     parser.add_argument("--epilogue", type=int, default=3, help="0 bf16, 1 fp32, 2 SwiGLU, 3 split partials")
+    parser.add_argument("--splits", type=int, default=0, help="linear: K splits (0: the library's choice)")
     parser.add_argument("--preset", default="qwen3-8b")
     parser.add_argument("--tp-size", type=int, default=1)
     parser.add_argument("--timed", action="store_true", help="step: time the captured step instead of profiling")
