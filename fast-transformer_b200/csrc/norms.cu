@@ -223,7 +223,7 @@ __device__ __forceinline__ void push8(const Params& p, size_t off, uint32_t flag
 template <int MODE>
 __global__ void __launch_bounds__(kMaxThreads) rmsnorm_kernel(const Params p) {
   __shared__ float scratch[kMaxThreads / 32];
-  __shared__ float cta_ss;
+  __shared__ float cluster_ss[kMaxCluster];  // every CTA's sum of squares, by cluster rank
   const int C = gridDim.x / p.rows;
   const int row = blockIdx.x / C;
   const int rank = blockIdx.x % C;
@@ -267,6 +267,19 @@ __global__ void __launch_bounds__(kMaxThreads) rmsnorm_kernel(const Params p) {
       }
     }
   }
+  // Every CTA of the row's cluster announces that it runs; the wait below, before the first
+  // remote shared-memory store, then costs nothing.
+  if (C > 1) cluster_arrive_relaxed();
+  // The residual's loads are issued with (not after) the input's: it was written before the
+  // previous kernel completed.
+  float res[kMaxPer][8];
+  if (MODE == 1 || MODE >= 3) {
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i) {
+      const int ch = c0 + threadIdx.x + i * T;
+      if (ch < c1) load8(p.residual, 0, 0, static_cast<size_t>(row) * p.width + ch * 8, res[i]);
+    }
+  }
   float v[kMaxPer][8];
   float ss = 0.f;
 #pragma unroll
@@ -281,10 +294,8 @@ __global__ void __launch_bounds__(kMaxThreads) rmsnorm_kernel(const Params p) {
         load8(src, split_count, slab, base + ch * 8, v[i]);
       }
       if (MODE == 1 || MODE >= 3) {
-        float r[8];
-        load8(p.residual, 0, 0, static_cast<size_t>(row) * p.width + ch * 8, r);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v[i][e] = bf16_round(v[i][e] + r[e]);
+        for (int e = 0; e < 8; ++e) v[i][e] = bf16_round(v[i][e] + res[i][e]);
         store8(p.sum + static_cast<size_t>(row) * p.width + ch * 8, v[i]);
       }
       if (MODE == 2) store8(p.sum + static_cast<size_t>(row) * p.width + ch * 8, v[i]);
@@ -294,11 +305,14 @@ __global__ void __launch_bounds__(kMaxThreads) rmsnorm_kernel(const Params p) {
   }
   ss = block_sum(ss, scratch);
   if (C > 1) {
-    if (threadIdx.x == 0) cta_ss = ss;
-    cluster_sync();  // every CTA's sum is in its shared memory
-    const uint32_t local = smem_u32(&cta_ss);
+    // thread q stores this CTA's sum into slot `rank` of cluster CTA q; after the barrier every
+    // CTA adds the C slots of its own shared memory in rank order (the same bits everywhere)
+    // and nothing reads or writes another CTA's shared memory any more.
+    cluster_wait();  // every CTA of the cluster has started
+    if (threadIdx.x < C) st_cluster_f32(map_shared(smem_u32(&cluster_ss[rank]), threadIdx.x), ss);
+    cluster_sync();
     float total = 0.f;
-    for (int q = 0; q < C; ++q) total += ld_cluster_f32(map_shared(local, q));
+    for (int q = 0; q < C; ++q) total += cluster_ss[q];
     ss = total;
   }
   const float inv = 1.0f / sqrtf(ss / static_cast<float>(p.width) + p.eps);
@@ -315,7 +329,6 @@ __global__ void __launch_bounds__(kMaxThreads) rmsnorm_kernel(const Params p) {
       store8(p.y + out, y);
     }
   }
-  if (C > 1) cluster_sync();  // no CTA leaves while another may still read its sum
 }
 
 constexpr int kSwigluThreads = 128;
