@@ -54,12 +54,13 @@ __device__ __forceinline__ void load_packed(const Params& p, size_t off, size_t 
     }
   } else {
     const float* src = static_cast<const float*>(p.packed) + off;
-    // Loads of up to eight slabs in flight before their in-order adds (one round trip for
-    // S <= 8).
-    for (int s0 = 0; s0 < p.splits; s0 += 8) {
-      float y[8][E];
+    // Loads of up to sixteen slabs in flight before their in-order adds (one round trip for
+    // S <= 16, the qkv projection's split count at decode shapes).
+    constexpr int kBatch = 16;
+    for (int s0 = 0; s0 < p.splits; s0 += kBatch) {
+      float y[kBatch][E];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < kBatch; ++j) {
         if (s0 + j < p.splits) {
           const float* q = src + (s0 + j) * split_stride;
           if constexpr (E == 4) {
@@ -72,7 +73,7 @@ __device__ __forceinline__ void load_packed(const Params& p, size_t off, size_t 
         }
       }
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < kBatch; ++j) {
         if (s0 + j == 0) {
 #pragma unroll
           for (int e = 0; e < E; ++e) x[e] = y[0][e];
