@@ -54,6 +54,20 @@ def test_host_validation_without_gpu():
     assert lib.fb_linear(p, p, p, 64, 151936, 4096, 0, 9, null) == -2  # too large for the fix-up: cluster of <= 8
     assert lib.fb_linear_finished_splits(16, 3072, 4096) <= 16
     assert lib.fb_linear_finished_splits(64, 151936, 4096) <= 8
+    # fused qkv + QK-norm/RoPE: head_dim must be 128 and N the packed q/k/v width
+    assert lib.fb_linear_qk_rope(null, p, 16, 768, 4096, 1, p, p, 1e-6, 1e-6, p, p, p, p, p, p, 4, 1, 128, 64,
+                                 null) == -1
+    assert lib.fb_linear_qk_rope(p, p, 16, 384, 4096, 1, p, p, 1e-6, 1e-6, p, p, p, p, p, p, 4, 1, 64, 64,
+                                 null) == -2
+    assert lib.fb_linear_qk_rope(p, p, 16, 640, 4096, 1, p, p, 1e-6, 1e-6, p, p, p, p, p, p, 4, 1, 128, 64,
+                                 null) == -2
+    assert lib.fb_linear_qk_rope(p, p, 65, 768, 4096, 1, p, p, 1e-6, 1e-6, p, p, p, p, p, p, 4, 1, 128, 64,
+                                 null) == -2
+    # cluster-shape override: powers of two up to 16, ring depth 2-4; (0, 0) restores automatic
+    assert lib.fb_decode_attention_cluster_shape(3, 2) == -1
+    assert lib.fb_decode_attention_cluster_shape(8, 5) == -1
+    assert lib.fb_decode_attention_cluster_shape(32, 2) == -1
+    assert lib.fb_decode_attention_cluster_shape(0, 0) == 0
     assert lib.fb_swiglu(p, 1, p, 4, 12, null) == -2                     # width % 8
     assert lib.fb_add_rmsnorm(p, 1, p, p, p, p, 4, 70000, 1e-6, null) == -2  # row too wide (> 65536)
     assert lib.fb_decode_attention(p, p, p, p, 0, p, p, 1 << 20, 1, 16, 8, 96, 2048, 0.1, 148, null) == -2  # D=96
