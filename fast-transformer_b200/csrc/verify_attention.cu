@@ -10,17 +10,19 @@
 // and an LSE merge across KV splits.
 //
 // B200 design:
-//  * One CTA per (row, KV head, KV split, 32-member group). A producer warp streams
-//    128-token K and V tiles with 2-D TMA (128-byte swizzle, no multicast) into a 2-stage ring.
+//  * One CTA per (row, KV head, KV split, 32-member group), warp-specialized. A producer lane
+//    streams 128-token K and V tiles with 2-D TMA (128-byte swizzle, no multicast) into a
+//    3-stage ring; one lane of the MMA warp issues every UMMA and the warp owns TMEM.
 //  * S^T = K_tile * Q^T is one tcgen05.mma chain (M = 128 tokens, N = 32 members, K = D)
-//    with the fp32 accumulator in TMEM. Q sits in shared memory in the same swizzled K-major
-//    layout, written once by the CTA.
-//  * Four softmax warps each read 32 TMEM lanes (one token per thread, 32 member columns),
-//    reduce column maxima with a shuffle transpose-reduce and shared memory, and write P as
-//    bf16 into a K-major swizzled tile.
+//    with the fp32 accumulator in TMEM (double-buffered). Q sits in shared memory in the same
+//    swizzled K-major layout, written once by the CTA.
+//  * Eight softmax warps (TMEM lane quarter x half of the member columns; one token per
+//    thread, 16 member columns) reduce column maxima with a shuffle transpose-reduce and
+//    shared memory, and write P as bf16 into a K-major swizzled tile (double-buffered).
 //  * O^T_tile = V^T * P^T is a second tcgen05.mma chain (M = 128 dims, N = 32 members,
-//    K = 128 tokens) with V read in place as an MN-major operand; each thread (one dim)
-//    folds the tile into its fp32 running output with the softmax correction.
+//    K = 128 tokens) with V read in place as an MN-major operand; each softmax thread (one dim)
+//    folds the tile into its fp32 running output with the softmax correction, one tile behind
+//    the scores, so the tensor core computes O(i-1) and S(i+1) while the warps work on tile i.
 //  * Every mbarrier wait is bounded; TMEM is freed on every path.
 #include "tcgen05.cuh"
 
