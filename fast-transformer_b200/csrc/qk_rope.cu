@@ -39,53 +39,7 @@ struct Params {
 template <int E>
 __device__ __forceinline__ void load_packed(const Params& p, size_t off, size_t split_stride,
                                             float (&x)[E]) {
-  if (p.splits == 0) {
-    const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(p.packed) + off;
-    if constexpr (E == 4) {
-      uint2 w = *reinterpret_cast<const uint2*>(src);
-      x[0] = bf16_lo(w.x);
-      x[1] = bf16_hi(w.x);
-      x[2] = bf16_lo(w.y);
-      x[3] = bf16_hi(w.y);
-    } else {
-      uint32_t w = *reinterpret_cast<const uint32_t*>(src);
-      x[0] = bf16_lo(w);
-      x[1] = bf16_hi(w);
-    }
-  } else {
-    const float* src = static_cast<const float*>(p.packed) + off;
-    // Loads of up to sixteen slabs in flight before their in-order adds (one round trip for
-    // S <= 16, the qkv projection's split count at decode shapes).
-    constexpr int kBatch = 16;
-    for (int s0 = 0; s0 < p.splits; s0 += kBatch) {
-      float y[kBatch][E];
-#pragma unroll
-      for (int j = 0; j < kBatch; ++j) {
-        if (s0 + j < p.splits) {
-          const float* q = src + (s0 + j) * split_stride;
-          if constexpr (E == 4) {
-            const float4 a = __ldcg(reinterpret_cast<const float4*>(q));
-            y[j][0] = a.x; y[j][1] = a.y; y[j][2] = a.z; y[j][3] = a.w;
-          } else {
-            const float2 a = __ldcg(reinterpret_cast<const float2*>(q));
-            y[j][0] = a.x; y[j][1] = a.y;
-          }
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < kBatch; ++j) {
-        if (s0 + j == 0) {
-#pragma unroll
-          for (int e = 0; e < E; ++e) x[e] = y[0][e];
-        } else if (s0 + j < p.splits) {
-#pragma unroll
-          for (int e = 0; e < E; ++e) x[e] += y[j][e];
-        }
-      }
-    }
-#pragma unroll
-    for (int e = 0; e < E; ++e) x[e] = bf16_round(x[e]);
-  }
+  load_packed_values<E>(p.packed, p.splits, off, split_stride, x);
 }
 
 template <int D>

@@ -32,6 +32,65 @@ __device__ __forceinline__ void load_bf16(const __nv_bfloat16* src, float (&x)[E
   }
 }
 
+// E consecutive values at element `off` of the packed qkv projection output, as fp32 holding
+// bf16 values: bf16 [rows, width] when splits == 0, else fp32 split-K partials [splits, rows,
+// width] (slab stride `split_stride`) summed in split order and rounded to bf16
+// (engine/kernels/merged.py:37-45). Up to kBatch slabs' loads are in flight before their
+// in-order adds (the batch changes only the load schedule, not the sum). The input was
+// written by an earlier kernel: plain / L2 loads, not __ldg.
+template <int E, int kBatch = 16>
+__device__ __forceinline__ void load_packed_values(const void* packed, int splits, size_t off, size_t split_stride,
+                                                   float (&x)[E]) {
+  if (splits == 0) {
+    const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(packed) + off;
+    if constexpr (E == 4) {
+      const uint2 w = *reinterpret_cast<const uint2*>(src);
+      x[0] = bf16_lo(w.x);
+      x[1] = bf16_hi(w.x);
+      x[2] = bf16_lo(w.y);
+      x[3] = bf16_hi(w.y);
+    } else {
+      const uint32_t w = *reinterpret_cast<const uint32_t*>(src);
+      x[0] = bf16_lo(w);
+      x[1] = bf16_hi(w);
+    }
+    return;
+  }
+  const float* src = static_cast<const float*>(packed) + off;
+  for (int s0 = 0; s0 < splits; s0 += kBatch) {
+    float y[kBatch][E];
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      if (s0 + j < splits) {
+        const float* q = src + (s0 + j) * split_stride;
+        if constexpr (E == 4) {
+          const float4 a = __ldcg(reinterpret_cast<const float4*>(q));
+          y[j][0] = a.x;
+          y[j][1] = a.y;
+          y[j][2] = a.z;
+          y[j][3] = a.w;
+        } else {
+          const float2 a = __ldcg(reinterpret_cast<const float2*>(q));
+          y[j][0] = a.x;
+          y[j][1] = a.y;
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      if (s0 + j == 0) {
+#pragma unroll
+        for (int e = 0; e < E; ++e) x[e] = y[0][e];
+      } else if (s0 + j < splits) {
+#pragma unroll
+        for (int e = 0; e < E; ++e) x[e] += y[j][e];
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < E; ++e) x[e] = bf16_round(x[e]);
+}
+
 // x: this lane's E values of one head (fp32 holding bf16 values); gw: the matching norm gains;
 // cs/sn: the cos/sin table row of the token's phase, offset to this lane's first dim.
 // Every lane of the warp must call it (one shuffle reduction, one partner exchange).

@@ -185,6 +185,13 @@ def _qkv_rope_decode(x, layer, eps, cos, sin, position, keys, values, q_heads):
 #: next projection's CTAs already stream their weights, whereas the fix-up's last CTA per
 #: tile holds its SM until the tile is summed.
 FINISH_SPLITS_IN_PROJECTION = os.environ.get("FB_FINISH_SPLITS_IN_PROJECTION", "0") == "1"
+#: Run the QK-norm/RoPE/KV append inside the decode attention kernel where the attention takes
+#: its cluster form (fb_qk_rope_decode_attention; same bits, one launch fewer per layer). Off by
+#: default: measured slower on B200 (one TP8 rank's shard alone 2000 against 1954-1963 us per
+#: step; Qwen3-0.6B at batch 1 953 against 918 us): every CTA of a cluster sums the qkv split
+#: partials for its query heads on the attention's critical path, which costs more than the
+#: separate kernel's launch.
+FUSE_ROPE_INTO_ATTENTION = os.environ.get("FB_FUSE_ROPE_ATTENTION", "0") == "1"
 #: The split-consumer all-reduce: "reduce_push" (fb_reduce_push + fb_allreduce_add_rmsnorm,
 #: the default) or "fused" (fb_reduce_push_add_rmsnorm: push and consumer in one launch).
 #: Measured on 4 B200s (config 4, same box): reduce_push 5817 tok/s, fused 4914, the split
@@ -270,6 +277,34 @@ class DecodeState:
             self.peers = PeerBuffers(self.comm, 2 * cfg.num_hidden_layers, batch, cfg.hidden_size, self.device)
 
     # ------------------------------------------------------------------ decode step
+    def _rope_attention(self, normalized, layer, index):
+        """qkv projection, QK-norm + RoPE + KV append, decode attention for one layer. Where the
+        attention takes its cluster form (few (row, KV head) pairs: tensor-parallel shards,
+        small batches) the norm/RoPE/append runs inside the attention kernel
+        (fb_qk_rope_decode_attention: one launch fewer); otherwise fb_qk_norm_rope_append then
+        fb_decode_attention. The same bits either way."""
+        cache, w = self.cache, self.w
+        keys, values = cache.keys[index], cache.values[index]
+        eps = self.cfg.rms_norm_eps
+        if FUSE_ROPE_INTO_ATTENTION and not FINISH_SPLITS_IN_PROJECTION:
+            packed = linear(normalized, layer.qkv, split_ok=True)
+            from kernels.merged import source
+            data, splits, _, _ = source(packed)
+            batch, kv_heads, capacity, dim = keys.shape
+            status = lib.fb_qk_rope_decode_attention(
+                ptr(data), splits if isinstance(packed, Split) else 0, ptr(layer.q_norm), ptr(layer.k_norm),
+                float(eps), float(eps), ptr(self.cos), ptr(self.sin), ptr(self.position), ptr(keys), ptr(values),
+                ptr(self.attn_out), batch, w.q_heads, kv_heads, dim, capacity, float(self.scale), stream())
+            if status != _native.FB_ERR_SHAPE:  # FB_ERR_SHAPE: not the cluster form, nothing launched
+                check(status, "fb_qk_rope_decode_attention")
+                return self.attn_out
+            query = _qk_rope_decode(packed, layer, eps, self.cos, self.sin, self.position, keys, values, w.q_heads)
+        else:
+            query = _qkv_rope_decode(normalized, layer, eps, self.cos, self.sin, self.position, keys, values,
+                                     w.q_heads)
+        return attend_decode(query, keys, values, self.position, self.scale, out=self.attn_out,
+                             workspace=self.workspace, ctas=self.ctas)
+
     def decode(self, keep_logits=False):
         """One greedy step for every row (the captured body).
 
@@ -286,10 +321,7 @@ class DecodeState:
         for index, layer in enumerate(layers):
             if index > 0 and peers is None:
                 normalized, residual = add_rms_norm(hidden, residual, layer.ln1, eps)
-            query = _qkv_rope_decode(normalized, layer, eps, self.cos, self.sin, self.position,
-                                     cache.keys[index], cache.values[index], w.q_heads)
-            attention = attend_decode(query, cache.keys[index], cache.values[index], self.position, self.scale,
-                                      out=self.attn_out, workspace=self.workspace, ctas=self.ctas)
+            attention = self._rope_attention(normalized, layer, index)
             attention = attention.reshape(self.batch, 1, -1)
             if peers is None:
                 out = linear(attention, layer.o, split_ok=True)

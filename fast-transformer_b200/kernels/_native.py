@@ -53,6 +53,8 @@ _SIGNATURES = {
     "fb_linear_splits": (_c_int, [_c_int, _c_int, _c_int]),
     "fb_linear_finished_splits": (_c_int, [_c_int, _c_int, _c_int]),
     "fb_decode_attention_cluster_shape": (_c_int, [_c_int, _c_int]),
+    "fb_qk_rope_decode_attention": (_c_int, [_vp, _c_int, _vp, _vp, _c_float, _c_float, _vp, _vp, _vp, _vp, _vp, _vp,
+                                             _c_int, _c_int, _c_int, _c_int, _c_int, _c_float, _vp]),
     "fb_linear_qk_rope": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _c_float, _c_float, _vp, _vp,
                                    _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp]),
     "fb_linear": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _vp]),

@@ -88,6 +88,22 @@ int fb_decode_attention_combine(const int64_t* position, int per_row, void* out,
  * otherwise. */
 int fb_decode_attention_cluster_shape(int cluster, int stages);
 
+/* Decode attention with the QK-norm + RoPE + KV append fused in (engine/kernels/qk_rope.py:87-129
+ * followed by decode_attention.py:238-257, one launch): the query heads and the newest K/V slot
+ * come from the packed qkv projection output `packed` (bf16 [B, (Hq + 2 Hkv) * 128] when
+ * packed_splits == 0, else fp32 split-K partials [packed_splits, B, (Hq + 2 Hkv) * 128]),
+ * with fb_qk_norm_rope_append's mode-0 whole-table arithmetic at the shared slot position[0]
+ * (q_weight/k_weight bf16 [128], cos/sin bf16 [>= capacity, 128]). The K and V heads are
+ * written into slot position[0] of keys/values [B, Hkv, capacity, 128], which the attention
+ * then reads; out bf16 [B, Hq, 128]. The same bits as fb_qk_norm_rope_append +
+ * fb_decode_attention. Runs only as the cluster form (head_dim 128, 2 * B * Hkv <= the SM
+ * count, every pair's cluster resident at once); otherwise returns FB_ERR_SHAPE and launches
+ * nothing (use the two calls). No workspace. No reference counterpart as one call. */
+int fb_qk_rope_decode_attention(const void* packed, int packed_splits, const void* q_weight, const void* k_weight,
+                                float q_eps, float k_eps, const void* cos, const void* sin, const int64_t* position,
+                                void* keys, void* values, void* out, int batch, int q_heads, int kv_heads,
+                                int head_dim, int capacity, float scale, void* stream);
+
 /* ------------------------------------------------------------------------------------
  * Decode attention without allocation. No counterpart in the reference.
  * Some callers cannot allocate device memory on the call path: a host runtime that owns a

@@ -535,3 +535,71 @@ def test_reduce_push_add_rmsnorm_single_rank():
         assert bool((halves[..., 1] == 13).all())
         assert torch.equal(halves[..., 0].contiguous().view(torch.float32), ordered)
         assert bool((recv[0] == 0).all())  # other uses untouched
+
+
+@pytest.mark.parametrize("batch,q_heads,kv_heads,length,splits",
+                         [(16, 4, 1, 8193, 16), (16, 16, 4, 1000, 12), (1, 16, 8, 640, 0), (3, 8, 2, 100, 4),
+                          (2, 8, 2, 64, 2)])
+def test_qk_rope_decode_attention_equals_two_launch(batch, q_heads, kv_heads, length, splits):
+    """fb_qk_rope_decode_attention (QK-norm + RoPE + KV append inside the cluster-form decode
+    attention) gives the same output and cache bits as fb_qk_norm_rope_append followed by
+    fb_decode_attention, from bf16 or split-partial qkv input; slots other than the position keep
+    their contents. Where the cluster form does not apply it launches nothing (FB_ERR_SHAPE)."""
+    from kernels._native import lib, ptr, stream, check
+    from kernels.decode_attention import attend
+    g = torch.Generator().manual_seed(batch * 1000 + length)
+    d = 128
+    capacity, pos = length + 8, length - 1
+    width = (q_heads + 2 * kv_heads) * d
+    if splits:
+        packed = (torch.randn(splits, batch, width, generator=g) * 0.5).to(DEV)
+    else:
+        packed = torch.randn(batch, width, generator=g).bfloat16().to(DEV)
+    q_gain = (1 + 0.1 * torch.randn(d, generator=g)).bfloat16().to(DEV)
+    k_gain = (1 + 0.1 * torch.randn(d, generator=g)).bfloat16().to(DEV)
+    cos = torch.randn(capacity, d, generator=g).bfloat16().to(DEV)
+    sin = torch.randn(capacity, d, generator=g).bfloat16().to(DEV)
+    keys0 = torch.randn(batch, kv_heads, capacity, d, generator=g).bfloat16().to(DEV)
+    values0 = torch.randn(batch, kv_heads, capacity, d, generator=g).bfloat16().to(DEV)
+    position = torch.tensor([pos], dtype=torch.int64, device=DEV)
+    scale = 1 / math.sqrt(d)
+    # two launches
+    keys2, values2 = keys0.clone(), values0.clone()
+    query = torch.empty(batch, 1, q_heads, d, dtype=torch.bfloat16, device=DEV)
+    check(lib.fb_qk_norm_rope_append(ptr(packed), splits, ptr(q_gain), ptr(k_gain), 1e-6, 1e-6, ptr(cos), ptr(sin),
+                                     ptr(position), None, ptr(query), ptr(keys2), ptr(values2), batch, 1, q_heads,
+                                     kv_heads, d, capacity, 0, 1, stream()), "fb_qk_norm_rope_append")
+    out2 = attend(query.view(batch, q_heads, 1, d), keys2, values2, position, scale)
+    # one launch
+    keys1, values1 = keys0.clone(), values0.clone()
+    out1 = torch.empty(batch, 1, q_heads, d, dtype=torch.bfloat16, device=DEV)
+    check(lib.fb_qk_rope_decode_attention(ptr(packed), splits, ptr(q_gain), ptr(k_gain), 1e-6, 1e-6, ptr(cos),
+                                          ptr(sin), ptr(position), ptr(keys1), ptr(values1), ptr(out1), batch,
+                                          q_heads, kv_heads, d, capacity, scale, stream()),
+          "fb_qk_rope_decode_attention")
+    torch.cuda.synchronize()
+    assert torch.equal(keys1, keys2) and torch.equal(values1, values2)
+    assert torch.equal(out1, out2)
+    assert torch.isfinite(out1.float()).all()
+    written = torch.zeros(capacity, dtype=torch.bool)
+    written[pos] = True
+    assert torch.equal(keys1[:, :, ~written.to(DEV)], keys0[:, :, ~written.to(DEV)])
+
+
+def test_qk_rope_decode_attention_refuses_non_cluster_shapes():
+    """Many (row, KV head) pairs (the persistent form's regime) or head_dim 64: FB_ERR_SHAPE,
+    nothing launched, the cache untouched."""
+    from kernels._native import lib, ptr, stream
+    d, capacity = 128, 72
+    keys = torch.zeros(16, 8, capacity, d, dtype=torch.bfloat16, device=DEV)
+    packed = torch.zeros(16, 48 * d, dtype=torch.bfloat16, device=DEV)
+    gain = torch.ones(d, dtype=torch.bfloat16, device=DEV)
+    table = torch.zeros(capacity, d, dtype=torch.bfloat16, device=DEV)
+    out = torch.empty(16, 1, 32, d, dtype=torch.bfloat16, device=DEV)
+    position = torch.tensor([5], dtype=torch.int64, device=DEV)
+    status = lib.fb_qk_rope_decode_attention(ptr(packed), 0, ptr(gain), ptr(gain), 1e-6, 1e-6, ptr(table), ptr(table),
+                                             ptr(position), ptr(keys), ptr(keys), ptr(out), 16, 32, 8, d, capacity,
+                                             0.088, stream())
+    assert status == -2
+    torch.cuda.synchronize()
+    assert bool((keys == 0).all())
