@@ -63,6 +63,13 @@ def test_host_validation_without_gpu():
                                  null) == -2
     assert lib.fb_linear_qk_rope(p, p, 65, 768, 4096, 1, p, p, 1e-6, 1e-6, p, p, p, p, p, p, 4, 1, 128, 64,
                                  null) == -2
+    # fused QK-norm/RoPE + decode attention: null -> ARG; head_dim 64 -> SHAPE (cluster form only)
+    assert lib.fb_qk_rope_decode_attention(null, 0, p, p, 1e-6, 1e-6, p, p, p, p, p, p, 16, 4, 1, 128, 64, 0.088,
+                                           null) == -1
+    assert lib.fb_qk_rope_decode_attention(p, 0, p, p, 1e-6, 1e-6, p, p, p, p, p, p, 16, 4, 1, 64, 64, 0.088,
+                                           null) == -2
+    assert lib.fb_qk_rope_decode_attention(p, -1, p, p, 1e-6, 1e-6, p, p, p, p, p, p, 16, 4, 1, 128, 64, 0.088,
+                                           null) == -1
     # cluster-shape override: powers of two up to 16, ring depth 2-4; (0, 0) restores automatic
     assert lib.fb_decode_attention_cluster_shape(3, 2) == -1
     assert lib.fb_decode_attention_cluster_shape(8, 5) == -1
