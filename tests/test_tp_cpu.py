@@ -1,4 +1,4 @@
-"""Tensor parallelism by KV head, on CPU ranks (gloo, world size 2): one decode step computed
+"""Tensor parallelism by KV head, on CPU ranks (gloo, world size 2 and 4): one decode step computed
 from the engine's TP shards (qwen3.from_state_dict / qwen3.random_init packing) with the
 oracle's arithmetic and an fp32 all-reduce after o_proj and down_proj must reproduce the
 unsharded oracle's logits; every rank must hold identical logits."""
@@ -95,12 +95,13 @@ def _worker(rank, world, port, queue, source):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("source", ["tiny", "random_init"])
-def test_tp2_decode_step_matches_unsharded_oracle(source):
+@pytest.mark.parametrize("source,world", [("tiny", 2), ("random_init", 2), ("random_init", 4)])
+def test_tp_decode_step_matches_unsharded_oracle(source, world):
+    """The tiny model has 2 KV heads (TP2 at most); the 0.6B-shaped random init has 8."""
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, queue, source)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, queue, source)) for r in range(world)]
     for p in procs:
         p.start()
     logits, expect, gathered = queue.get(timeout=300)
@@ -109,7 +110,7 @@ def test_tp2_decode_step_matches_unsharded_oracle(source):
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    assert torch.equal(gathered[0], gathered[1]), "ranks disagree"
+    assert all(torch.equal(gathered[0], t) for t in gathered[1:]), "ranks disagree"
     scale = expect.float().abs().max()
     assert (logits.float() - expect.float()).abs().max() <= 2e-2 * scale
     assert torch.equal(logits.float().argmax(-1), expect.float().argmax(-1))
