@@ -3,7 +3,8 @@
 //
 // Arithmetic and cast points of the reference kernel `_qk_rope_cache`
 // (engine/kernels/qk_rope.py:34-66):
-//   inv  = 1 / sqrt(mean(x^2) + eps)            fp32
+//   inv  = 1 / sqrt(mean(x^2) + eps)            fp32, the sum of squares in the reference's
+//                                               eager (torch CPU) order: bit-exact K and Q
 //   n    = bf16(x * inv); w = bf16(n * gain)
 //   rot  = [-w[D/2:], w[:D/2]]
 //   out  = bf16(bf16(w * cos) + bf16(rot * sin)) both products rounded
@@ -91,19 +92,63 @@ __device__ __forceinline__ void load_packed_values(const void* packed, int split
   for (int e = 0; e < E; ++e) x[e] = bf16_round(x[e]);
 }
 
+// Sum of the squares of one head's D values (lane l holds dims [l*E, l*E + E)), added in the
+// order of torch's CPU sum kernel for a contiguous fp32 row, which is the order the
+// reference's eager `x.pow(2).mean(-1)` uses (agent/local_cpu/shim/references.py:155):
+//   - the row is read as 8-wide vectors v_0 .. v_{D/8-1};
+//   - four interleaved vector accumulators, a_k = ((v_k + v_{k+4}) + v_{k+8}) + ...;
+//   - then ((a_0 + a_1) + a_2) + a_3, lane-wise;
+//   - then its 8 lanes in index order.
+// Every product and sum is rounded on its own (no fused multiply-add), so the result has the
+// bits torch computes on the host. Every lane of the warp must call it; all lanes return the
+// total.
+template <int D>
+__device__ __forceinline__ float sum_squares_host_order(const float (&x)[D / 32]) {
+  constexpr int E = D / 32;      // values per lane
+  constexpr int V = 8 / E;       // lanes per 8-wide vector
+  constexpr int R = D / 32;      // vectors per accumulator: (D / 8) / 4
+  static_assert(D == 64 || D == 128, "head_dim 64 or 128");
+  float sq[E], acc[E], vec[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) sq[e] = __fmul_rn(x[e], x[e]);
+  // lanes [0, 4V) hold vector k = lane / V; accumulator k adds vectors k, k+4, ... in order
+#pragma unroll
+  for (int e = 0; e < E; ++e) acc[e] = sq[e];
+#pragma unroll
+  for (int r = 1; r < R; ++r) {
+#pragma unroll
+    for (int e = 0; e < E; ++e) acc[e] = __fadd_rn(acc[e], __shfl_down_sync(0xffffffffu, sq[e], 4 * V * r));
+  }
+  // lanes [0, V) combine the four accumulators in order
+#pragma unroll
+  for (int e = 0; e < E; ++e) vec[e] = acc[e];
+#pragma unroll
+  for (int k = 1; k < 4; ++k) {
+#pragma unroll
+    for (int e = 0; e < E; ++e) vec[e] = __fadd_rn(vec[e], __shfl_down_sync(0xffffffffu, acc[e], V * k));
+  }
+  // the 8 vector lanes, held E at a time by lanes 0 .. V-1, in index order
+  float total = 0.f;
+#pragma unroll
+  for (int h = 0; h < V; ++h) {
+#pragma unroll
+    for (int e = 0; e < E; ++e) total = __fadd_rn(total, __shfl_sync(0xffffffffu, vec[e], h));
+  }
+  return total;
+}
+
 // x: this lane's E values of one head (fp32 holding bf16 values); gw: the matching norm gains;
 // cs/sn: the cos/sin table row of the token's phase, offset to this lane's first dim.
-// Every lane of the warp must call it (one shuffle reduction, one partner exchange).
+// Every lane of the warp must call it (shuffle reduction, one partner exchange).
 template <int D>
 __device__ __forceinline__ void norm_rope(const float (&x)[D / 32], const float (&gw)[D / 32], float eps,
                                           const __nv_bfloat16* cs, const __nv_bfloat16* sn, int lane,
                                           __nv_bfloat16 (&out)[D / 32]) {
   constexpr int E = D / 32;
-  float ss = 0.f;
-#pragma unroll
-  for (int e = 0; e < E; ++e) ss += x[e] * x[e];
-  ss = warp_sum(ss);
-  const float inv = 1.0f / sqrtf(ss / static_cast<float>(D) + eps);
+  const float ss = sum_squares_host_order<D>(x);
+  // mean = sum / D, then 1 / sqrt(mean + eps), each correctly rounded (torch.rsqrt on the
+  // host divides 1 by a correctly rounded square root)
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(D)), eps)));
   float w[E];
 #pragma unroll
   for (int e = 0; e < E; ++e) {

@@ -70,6 +70,27 @@ def argmax(logits):
     return logits.to(F32).argmax(-1)
 
 
+def sum_squares_host_order(x):
+    """Sum of squares over the last dim (a multiple of 32) in the order torch's CPU sum kernel
+    adds a contiguous fp32 row: 8-wide vectors, four interleaved vector accumulators
+    (a_k = v_k + v_{k+4} + ... in order), then ((a_0 + a_1) + a_2) + a_3, then the 8 lanes in
+    order. That is what the reference's eager ``x.pow(2).mean(-1)`` computes in the fixtures
+    (references.py:155); written out with elementwise adds so the answer does not depend on the
+    host's vector width."""
+    dim = x.shape[-1]
+    assert dim % 32 == 0
+    vectors = (x * x).reshape(*x.shape[:-1], dim // 8, 8)
+    acc = [vectors[..., k, :].clone() for k in range(4)]
+    for r in range(1, dim // 32):
+        for k in range(4):
+            acc[k] = acc[k] + vectors[..., 4 * r + k, :]
+    vec = ((acc[0] + acc[1]) + acc[2]) + acc[3]
+    total = vec[..., 0].clone()
+    for lane in range(1, 8):
+        total = total + vec[..., lane]
+    return total
+
+
 def qk_rope_cache(packed, q_weight, k_weight, q_eps, k_eps, cos, sin, position, keys, values,
                   q_heads, prefill=False, rows=False, phases=None):
     """qk_rope.py:13-84 / references.py:143-192.
@@ -87,7 +108,8 @@ def qk_rope_cache(packed, q_weight, k_weight, q_eps, k_eps, cos, sin, position, 
     heads = q_heads + kv_heads
     x = data[:, :heads].to(F32)
     eps = torch.cat((torch.full((q_heads,), q_eps), torch.full((kv_heads,), k_eps)))[None, :, None]
-    inv_std = torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps)
+    mean = (sum_squares_host_order(x) / dim)[..., None]
+    inv_std = torch.rsqrt(mean + eps)
     gain = torch.cat((q_weight.to(F32).expand(q_heads, dim), k_weight.to(F32).expand(kv_heads, dim)))[None]
     normalized = (x * inv_std).to(BF16).to(F32)
     weighted = (normalized * gain).to(BF16).to(F32)
