@@ -23,6 +23,10 @@
 //    K = 128 tokens) with V read in place as an MN-major operand; each softmax thread (one dim)
 //    folds the tile into its fp32 running output with the softmax correction, one tile behind
 //    the scores, so the tensor core computes O(i-1) and S(i+1) while the warps work on tile i.
+//  * head_dim 64 runs the same pipeline on the same 128-dim layout: TMA fills only the first
+//    64-dim box of each K/V stage, the second box of every stage (and of Q) is zeroed once, so
+//    the score product adds zeros and the value product's dims 64..127 come out zero and are
+//    not stored.
 //  * Every mbarrier wait is bounded; TMEM is freed on every path.
 #include "tcgen05.cuh"
 
@@ -46,7 +50,7 @@ struct Params {
   __nv_bfloat16* out;      // [B, T, Hq, D]
   float* acc;              // [pairs, S, members_pad, D] (splits > 1)
   float2* stats;           // [pairs, S, members_pad]
-  int batch, tokens, q_heads, kv_heads, groups, capacity, splits, chunk, members_pad;
+  int batch, tokens, q_heads, kv_heads, groups, capacity, splits, chunk, members_pad, dim;
   float scale_log2;
   unsigned* err;
 };
@@ -155,16 +159,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                  "r"(kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
+  const int D = p.dim;
+  if (D == 64) {
+    // head_dim 64: the second 64-dim box of every K and V stage stays zero (TMA never writes it)
+    for (int e = tid; e < kStages * 2 * kTile * 8; e += blockDim.x) {
+      const int st = e / (2 * kTile * 8), rest = e % (2 * kTile * 8);
+      const int which = rest / (kTile * 8), c = rest % (kTile * 8);
+      *reinterpret_cast<uint4*>(stages + st * Smem::kStageBytes + which * Smem::kTileBytes + kTile * 128 + c * 16) =
+          make_uint4(0, 0, 0, 0);
+    }
+  }
   // Q members [group0, group0 + 32) of this (row, KV head) into the swizzled K-major tile;
-  // rows past the real members are zero.
+  // rows past the real members, and dims past D, are zero.
   for (int e = tid; e < kMembers * 16; e += blockDim.x) {
-    const int r = e / 16, c16 = e % 16;  // member row, 16-byte chunk of D = 128
+    const int r = e / 16, c16 = e % 16;  // member row, 16-byte chunk of the 128-dim layout
     const int m = group0 + r;
     uint4 v = make_uint4(0, 0, 0, 0);
-    if (m < members) {
+    if (m < members && c16 * 8 < D) {
       const int t = m / G, g = m % G;
       const __nv_bfloat16* src =
-          p.q + ((static_cast<size_t>(b) * T + t) * p.q_heads + h * G + g) * 128 + c16 * 8;
+          p.q + ((static_cast<size_t>(b) * T + t) * p.q_heads + h * G + g) * D + c16 * 8;
       v = *reinterpret_cast<const uint4*>(src);
     }
     *reinterpret_cast<uint4*>(q_s + (c16 >> 3) * (kMembers * 128) + sw128(r, c16 & 7)) = v;
@@ -198,12 +212,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         uint8_t* kt = stages + st * Smem::kStageBytes;
         uint8_t* vt = kt + Smem::kTileBytes;
-        mbar_arrive_expect_tx(&full[st], Smem::kStageBytes);
+        mbar_arrive_expect_tx(&full[st], D == 128 ? Smem::kStageBytes : Smem::kStageBytes / 2);
         const int row = row0 + i * kTile;
         tma_load_2d(kt, &kmap, &full[st], 0, row);
-        tma_load_2d(kt + kTile * 128, &kmap, &full[st], 64, row);
         tma_load_2d(vt, &vmap, &full[st], 0, row);
-        tma_load_2d(vt + kTile * 128, &vmap, &full[st], 64, row);
+        if (D == 128) {
+          tma_load_2d(kt + kTile * 128, &kmap, &full[st], 64, row);
+          tma_load_2d(vt + kTile * 128, &vmap, &full[st], 64, row);
+        }
       }
     }
   } else if (warp == kMmaWarp) {
@@ -398,12 +414,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int c = 0; c < kHalf; ++c) {
         const int m = group0 + col0 + c;
-        if (m >= members) continue;
+        if (m >= members || d >= D) continue;
         const int mc = col0 + c;
         const float L = red[mc] + red[kMembers + mc] + red[2 * kMembers + mc] + red[3 * kMembers + mc];
         const int t = m / G, g = m % G;
         if (p.splits == 1) {
-          const size_t o_off = ((static_cast<size_t>(b) * T + t) * p.q_heads + h * G + g) * 128 + d;
+          const size_t o_off = ((static_cast<size_t>(b) * T + t) * p.q_heads + h * G + g) * D + d;
           p.out[o_off] = __float2bfloat16_rn(L > 0.f ? o[c] / L : 0.f);
         } else {
           const size_t slot = (static_cast<size_t>(pair) * p.splits + split) * p.members_pad + m;
@@ -435,6 +451,7 @@ __global__ void __launch_bounds__(128) verify_merge_kernel(const Params p) {
   const int pair = b * p.kv_heads + h;
   const int m = t * p.groups + g;
   const int d = threadIdx.x;
+  if (d >= p.dim) return;
   float M = -INFINITY;
   for (int s = 0; s < p.splits; ++s)
     M = fmaxf(M, p.stats[(static_cast<size_t>(pair) * p.splits + s) * p.members_pad + m].x);
@@ -448,7 +465,7 @@ __global__ void __launch_bounds__(128) verify_merge_kernel(const Params p) {
     L += st.y * w;
     O += p.acc[slot * 128 + d] * w;
   }
-  p.out[static_cast<size_t>(index) * 128 + d] = __float2bfloat16_rn(L > 0.f ? O / L : 0.f);
+  p.out[static_cast<size_t>(index) * p.dim + d] = __float2bfloat16_rn(L > 0.f ? O / L : 0.f);
 }
 
 }  // namespace verify
@@ -492,7 +509,7 @@ extern "C" int fb_verify_attention(const void* q, const void* k, const void* v, 
   if (!q || !k || !v || !position || !chain || !out) return FB_ERR_ARG;
   if (batch <= 0 || tokens <= 0 || q_heads <= 0 || kv_heads <= 0 || capacity <= 0 || splits <= 0)
     return FB_ERR_ARG;
-  if (head_dim != 128 || q_heads % kv_heads != 0) return FB_ERR_SHAPE;
+  if ((head_dim != 64 && head_dim != 128) || q_heads % kv_heads != 0) return FB_ERR_SHAPE;
   if (static_cast<long long>(batch) * kv_heads * capacity >= (1ll << 31)) return FB_ERR_SHAPE;
   if (batch * kv_heads > 65535 || splits > 65535) return FB_ERR_SHAPE;
   const int groups = q_heads / kv_heads;
@@ -526,6 +543,7 @@ extern "C" int fb_verify_attention(const void* q, const void* k, const void* v, 
   p.chunk = (per + verify::kTile - 1) / verify::kTile * verify::kTile;
   p.members_pad = static_cast<int>(pad);
   p.scale_log2 = static_cast<float>(static_cast<double>(scale) * 1.4426950408889634);
+  p.dim = head_dim;
   p.err = error_word();
   const uint64_t rows = static_cast<uint64_t>(batch) * kv_heads * capacity;
   CUtensorMap km, vm;

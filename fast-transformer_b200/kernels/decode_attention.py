@@ -96,8 +96,6 @@ def block_attention(query, key, value, position, scale, chain, splits=None):
     assert value.shape == key.shape and key.shape[3] == dim and dim in (64, 128)
     assert position.shape == (batch,) and position.dtype == torch.int64
     assert chain.shape == (batch,) and chain.dtype == torch.int64
-    if dim != 128:
-        raise ValueError("the tcgen05 verify kernel takes head_dim 128")
     _native.require_cuda(query, key, value, position, chain)
     shape = (query.device, batch, tokens, query_heads, kv_heads, capacity, dim)
     if splits is None:
