@@ -1,11 +1,10 @@
 """Run one decode-path kernel (or one eager decode step) at a chosen shape, for Nsight Compute.
 
-    python fast-transformer_b200/profile_kernels.py attention --batch 16 --length 8320
-    python fast-transformer_b200/profile_kernels.py linear --m 16 --n 24576 --k 4096 --epilogue 2
-    python fast-transformer_b200/profile_kernels.py verify --batch 8 --tokens 5 --length 4101
-    python fast-transformer_b200/profile_kernels.py prefill --batch 1 --length 8192
-    python fast-transformer_b200/profile_kernels.py forms --tp-size 8 --copies 8
-    python fast-transformer_b200/profile_kernels.py step --preset qwen3-8b --batch 16 --length 8192
+    python profile_kernels.py attention --batch 16 --length 8320
+    python profile_kernels.py linear --m 16 --n 24576 --k 4096 --epilogue 2
+    python profile_kernels.py verify --batch 8 --tokens 5 --length 4101
+    python profile_kernels.py prefill --batch 1 --length 8192
+    python profile_kernels.py step --preset qwen3-8b --batch 16 --length 8192
 
 Each mode warms up, then runs the measured launches inside the NVTX range "profiled", so
 `ncu --nvtx --nvtx-include "profiled/"` captures exactly those; it also prints the CUDA-event
@@ -19,7 +18,7 @@ import statistics
 import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-sys.path.insert(0, HERE)
+sys.path[:0] = [HERE, os.path.join(HERE, "fast-transformer_b200")]
 
 import torch  # noqa: E402
 
@@ -156,62 +155,12 @@ def prefill(args):
     torch.cuda.synchronize()
 
 
-def forms(args):
-    """Graph-timed per-launch cost of finishing a K-split projection in its own launch (split
-    fix-up) against split partials + a consumer kernel, at one tensor-parallel shard's shapes
-    (rank 0 of --tp-size, --batch rows): the SwiGLU gate_up, and the o_proj / down_proj
-    all-reduce producers pushing into this GPU's own receive buffer (world 1)."""
-    import ctypes
-    import qwen3
-    from kernels import linear as klin
-    from kernels._native import check, lib, ptr, stream
-    cfg = qwen3.PRESETS[args.preset]
-    r, m = args.tp_size, args.batch
-    hidden, inter = cfg["hidden_size"], cfg["intermediate_size"] // r
-    heads = cfg["num_attention_heads"] // r * cfg["head_dim"]
-    epoch = torch.full((1,), 5, dtype=torch.int64, device="cuda")
-    recv = torch.zeros(1, 1, m, hidden, dtype=torch.int64, device="cuda")
-    peers = (ctypes.c_void_p * 1)(recv.data_ptr())
-
-    def timed(name, n, k, fn):
-        x = torch.randn(m, k, device="cuda").bfloat16()
-        weights = [(torch.randn(n, k, device="cuda") * 0.02).bfloat16() for _ in range(args.copies)]
-        ms = graph_time(lambda: [fn(x, w) for w in weights]) / len(weights)
-        print(f"{name} TP-shard 1/{r} M={m} N={n} K={k}: {ms * 1e3:.2f} us per use, {n * k * 2 / ms / 1e6:.0f} GB/s")
-
-    def swiglu(split_consumer):
-        return lambda x, w: klin.swiglu_linear(x, w, split_consumer=split_consumer)
-
-    def push(split_consumer, single=False):
-        def run(x, w):
-            n, k = w.shape
-            s = 1 if single else klin.splits_for(m, n, k, x.device, finished=True)
-            if s > 1 and split_consumer:
-                part = klin.project(x, w, klin.SPLITS_OUT, s)
-                check(lib.fb_reduce_push(ptr(part), s, m, n, 1, 0, 0, peers, None, ptr(epoch), stream()), "push")
-            else:
-                check(lib.fb_linear_allreduce_push(ptr(x), ptr(w), m, n, k, s, 1, 0, 0, peers, None, ptr(epoch),
-                                                   stream()), "push")
-        return run
-
-    s_gu = klin.splits_for(m, 2 * inter, hidden, torch.device("cuda"), finished=True)
-    timed(f"gate_up+SwiGLU fix-up S={s_gu}", 2 * inter, hidden, swiglu(False))
-    timed(f"gate_up split partials S={s_gu} + fb_swiglu_blocked", 2 * inter, hidden, swiglu(True))
-    for name, k in (("o_proj", heads), ("down_proj", inter)):
-        s_p = klin.splits_for(m, hidden, k, torch.device("cuda"), finished=True)
-        timed(f"{name} push, one split", hidden, k, push(False, single=True))
-        timed(f"{name} push, fix-up S={s_p}", hidden, k, push(False))
-        timed(f"{name} split partials S={s_p} + fb_reduce_push", hidden, k, push(True))
-
-
 def step(args):
     import decode as fdecode
     import qwen3
     cfg = qwen3.Config.make(**qwen3.PRESETS[args.preset])
     # --tp-size N: one rank's shard shapes (rank 0 of N), run alone, for per-kernel times at TP N
     # (the all-reduce consumers then run as the single-rank add+norm)
-    if args.finish_in_projection:
-        fdecode.FINISH_SPLITS_IN_PROJECTION = True
     weights = qwen3.random_init(cfg, "cuda", seed=0, tp_rank=0, tp_size=args.tp_size)
     state = fdecode.DecodeState(weights, args.batch, args.length, 8)
     # decode cost does not depend on cache contents: random K/V instead of a prefill
@@ -236,8 +185,7 @@ def step(args):
         end.record()
         end.synchronize()
         ms = start.elapsed_time(end) / 20
-        form = "splits finished in the projections" if fdecode.FINISH_SPLITS_IN_PROJECTION else "split consumers"
-        print(f"step {args.preset} TP-shard 1/{args.tp_size} B={args.batch} L={args.length} ({form}): "
+        print(f"step {args.preset} TP-shard 1/{args.tp_size} B={args.batch} L={args.length}: "
               f"{ms * 1e3:.1f} us per captured step ({args.batch / ms * 1e3:.0f} tok/s for this shard alone)")
         state.release()
         return
@@ -250,7 +198,7 @@ def step(args):
 
 def main():
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    parser.add_argument("mode", choices=("attention", "linear", "verify", "prefill", "forms", "step"))
+    parser.add_argument("mode", choices=("attention", "linear", "verify", "prefill", "step"))
     parser.add_argument("--batch", type=int, default=16)
     parser.add_argument("--q-heads", type=int, default=32)
     parser.add_argument("--kv-heads", type=int, default=8)
@@ -264,15 +212,11 @@ def main():
     parser.add_argument("--preset", default="qwen3-8b")
     parser.add_argument("--tp-size", type=int, default=1)
     parser.add_argument("--timed", action="store_true", help="step: time the captured step instead of profiling")
-    parser.add_argument("--finish-in-projection", action="store_true",
-                        help="step: finish K splits inside the projections (split fix-up) instead of in consumer "
-                             "kernels (the decode default)")
     parser.add_argument("--copies", type=int, default=2)
     parser.add_argument("--shapes", default="", help="attention: cluster-form shapes to sweep, e.g. 8x2,8x3,16x2")
     parser.add_argument("--launches", type=int, default=2)
     args = parser.parse_args()
-    {"attention": attention, "linear": linear, "verify": verify, "prefill": prefill, "forms": forms,
-     "step": step}[args.mode](args)
+    {"attention": attention, "linear": linear, "verify": verify, "prefill": prefill, "step": step}[args.mode](args)
 
 
 if __name__ == "__main__":
