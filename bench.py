@@ -6,15 +6,23 @@
 Workload: Qwen3-8B architecture with random-init weights
 (seed 0; linear ~N(0, 0.02), norm weights 1, tied embeddings), batch 16, every row
 prefilled to 8192 random token ids (seed 0), then greedy decode steps, tensor-parallel by KV
-head over N GPUs with an NCCL all-reduce after o_proj and down_proj. One step = one
-greedy token for each of the 16 rows = one replay of the captured decode graph.
+head over N GPUs with an all-reduce (flagged-word NVLink peer stores) after o_proj and
+down_proj. One step = one greedy token for each of the 16 rows = one replay of the captured
+decode graph.
+
+Before any timing a parity gate runs the same step on the 2-layer truncation of the model at
+this TP size against the CPU oracle (teacher-forced) and checks graph == eager and that the
+ranks agree; a failed gate prints no number.
 
 Prints one JSON line (rank 0): whole-job decode tok/s (device time, max over ranks), the
 same through the host-facing step API with pinned host token ids (`e2e`), the roofline of
 the dominant kernel (split-KV decode attention: algorithmic K/V bytes per launch over its
-measured launch time), the reference's algorithm (the CPU oracle port) timed on this host,
-SM clocks sampled during the timed region, and the decode-attention GB/s sweep of BASELINE
-config 3 (N=1 only).
+measured launch time), SM clocks sampled during the timed region, and at N=1 the other
+BASELINE configs (1: decode attention op, 2: Qwen3-0.6B decode, 3: ragged attention sweep,
+5: verify attention) and the CPU baseline: the reference's eager path (HF Transformers Qwen3
+over a pre-filled DynamicCache) timed on this host's cores.
+
+`--impl reference` prints the CPU baseline alone as the reference arm's line.
 """
 
 import argparse
@@ -98,10 +106,121 @@ class Clocks:
 
 
 # ------------------------------------------------------------------------------ CPU side
-def cpu_decode_sample(layers_timed=1, repeats=1):
-    """The reference's algorithm (the CPU oracle port) for one decode step of config 4 on a
-    bounded sample: one Qwen3-8B layer at batch 16 over an 8192-slot cache, plus the LM head
-    and argmax; returns (seconds per full 36-layer step, threads, sample text)."""
+def host_memory_available():
+    """Bytes this process may still allocate on the host: the smaller of the free memory and the
+    container's cgroup limit minus its usage."""
+    import psutil
+    free = psutil.virtual_memory().available
+    try:
+        limit = open("/sys/fs/cgroup/memory.max").read().strip()
+        used = int(open("/sys/fs/cgroup/memory.current").read().strip())
+        if limit != "max":
+            free = min(free, int(limit) - used)
+    except OSError:
+        pass
+    return free
+
+
+def _tile(dst, block):
+    """Fill ``dst`` with copies of ``block`` (one parallel copy per whole repetition)."""
+    flat = dst.view(-1)
+    n, size = flat.numel(), block.numel()
+    whole = n // size * size
+    if whole:
+        flat[:whole].view(-1, size).copy_(block[None].expand(whole // size, size))
+    if whole < n:
+        flat[whole:].copy_(block[:n - whole])
+
+
+HF_NEED_BYTES = 48 << 30  # 8B bf16 weights (16.4 GB) + a 16 x 8192-slot cache (19.3 GB) + the step's copies
+
+
+def hf_decode_sample(steps, warmup=1, layers=None):
+    """The reference's own eager CPU path for config 4's decode step: HF Transformers'
+    Qwen3ForCausalLM (the model the reference engine wraps, engine/engine.py:27-35), bf16, SDPA
+    attention, greedy over a DynamicCache pre-filled with 8192 slots per row (BASELINE's CPU plan;
+    the pattern of agent/local_cpu/smoke_engine.py:77-86). Whole 36-layer steps at batch 16 on all
+    host cores. A 16 x 8192 prefill of an 8B model is impractical on a CPU, so the cache is filled
+    with seeded N(0, 1) values instead (decode cost does not depend on them); weights are a seeded
+    N(0, 0.02) block tiled over every matrix, norm weights 1, embeddings tied.
+    ``layers`` < 36 times a truncated model (the bounded sample of the main line's cpu_baseline)
+    and scales its per-layer time to 36 layers, the LM head and argmax timed on their own.
+    Returns (seconds per 36-layer step, steps run, threads, sample text), or None when the host
+    lacks the memory (about 48 GB for the whole model)."""
+    import qwen3
+    total_layers = qwen3.PRESETS[PRESET]["num_hidden_layers"]
+    layers = layers or total_layers
+    if host_memory_available() < HF_NEED_BYTES * layers / total_layers + (4 << 30):
+        return None
+    import warnings
+    from transformers import DynamicCache, Qwen3Config, Qwen3ForCausalLM
+    from transformers.initialization import no_init_weights
+    warnings.filterwarnings("ignore")
+    torch.set_num_threads(os.cpu_count() or 1)
+    preset = {**qwen3.PRESETS[PRESET], "num_hidden_layers": layers}
+    cfg = Qwen3Config(**preset, max_position_embeddings=40960)
+    cfg._attn_implementation = "sdpa"
+    default = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        with no_init_weights():
+            model = Qwen3ForCausalLM(cfg)
+    finally:
+        torch.set_default_dtype(default)
+    model.eval()
+    g = torch.Generator().manual_seed(0)
+    block = (torch.randn(1 << 24, generator=g) * 0.02).to(torch.bfloat16)
+    with torch.no_grad():
+        model.lm_head.weight = model.model.embed_tokens.weight  # tied embeddings
+        for name, param in model.named_parameters():
+            if name.endswith("norm.weight"):
+                param.fill_(1.0)
+            else:
+                _tile(param.data, block)
+        cache = DynamicCache(config=cfg)
+        kv = torch.randn(1 << 24, generator=g).to(torch.bfloat16)
+        hkv, d = preset["num_key_value_heads"], preset["head_dim"]
+        for layer in range(preset["num_hidden_layers"]):
+            k = torch.empty(BATCH, hkv, PROMPT, d, dtype=torch.bfloat16)
+            v = torch.empty_like(k)
+            _tile(k, kv)
+            _tile(v, kv)
+            cache.update(k, v, layer)
+        ids = torch.randint(0, preset["vocab_size"], (BATCH, 1), generator=g)
+    times, head_times = [], []
+    with torch.inference_mode():
+        for step in range(warmup + steps):
+            t0 = time.perf_counter()
+            logits = model(input_ids=ids, past_key_values=cache, use_cache=True).logits
+            ids = logits[:, -1].argmax(-1, keepdim=True)
+            if step >= warmup:
+                times.append(time.perf_counter() - t0)
+            if layers < total_layers:
+                hidden = torch.randn(BATCH, 1, preset["hidden_size"], generator=g).to(torch.bfloat16)
+                t0 = time.perf_counter()
+                model.lm_head(model.model.norm(hidden))[:, -1].argmax(-1)
+                if step >= warmup:
+                    head_times.append(time.perf_counter() - t0)
+    del model, cache
+    step_s = statistics.median(times)
+    if layers < total_layers:
+        head = statistics.median(head_times)
+        step_s = (step_s - head) * total_layers / layers + head
+        sample = (f"HF Transformers Qwen3ForCausalLM eager (bf16, SDPA), the reference engine's model, truncated to "
+                  f"{layers} of {total_layers} layers: {steps} greedy steps at batch 16 over a DynamicCache "
+                  f"pre-filled to 8192 slots (seeded N(0,1) K/V), median step, the layers' time scaled to "
+                  f"{total_layers} layers plus the final norm, LM head and argmax timed alone")
+    else:
+        sample = (f"HF Transformers Qwen3ForCausalLM eager (bf16, SDPA), the reference engine's model: {steps} whole "
+                  f"{total_layers}-layer greedy steps at batch 16 over a DynamicCache pre-filled to 8192 slots "
+                  f"(seeded N(0,1) K/V instead of a prefill), after {warmup} warm-up step; median step")
+    return step_s, steps, torch.get_num_threads(), sample
+
+
+def port_decode_sample(repeats=1):
+    """Fallback when the host cannot hold the HF model and cache: the oracle port (torch CPU, fp32
+    with the reference's bf16 casts) for one Qwen3-8B layer at batch 16 over an 8192-slot cache
+    plus the LM head and argmax, scaled to 36 layers. Returns (seconds per step, threads, sample)."""
     from oracle import attention as oatt
     from oracle import pointwise as opw
     import qwen3
@@ -150,24 +269,36 @@ def cpu_decode_sample(layers_timed=1, repeats=1):
     tail()
     per_tail = time.perf_counter() - t0
     step = per_layer * qwen3.PRESETS[PRESET]["num_hidden_layers"] + per_tail
-    sample = (f"oracle port (torch CPU, fp32 with the reference's bf16 casts): {repeats} x one Qwen3-8B layer "
-              f"(B=16, 8192-slot cache, dense split-KV attention) + LM head/argmax once, scaled to 36 layers")
+    sample = (f"oracle port (torch CPU, fp32 with the reference's bf16 casts; the host lacked the ~48 GB the HF "
+              f"model and cache need): {repeats} x one Qwen3-8B layer (B=16, 8192-slot cache) + LM head/argmax "
+              f"once, scaled to 36 layers")
     return step, threads, sample
 
 
+def cpu_baseline(steps, layers=None):
+    """(tok/s, steps run, threads, kind, sample, seconds per step) of the CPU reference path on
+    this host: HF eager Qwen3 (whole steps, or ``layers`` of them scaled), else the oracle port."""
+    got = hf_decode_sample(steps, layers=layers)
+    if got is not None:
+        step_s, ran, threads, sample = got
+        return BATCH / step_s, ran, threads, "reference", sample, step_s
+    torch.set_num_threads(os.cpu_count() or 1)
+    step_s, threads, sample = port_decode_sample()
+    return BATCH / step_s, 1, threads, "port", sample, step_s
+
+
 def reference_arm(args):
-    """--impl reference: the reference's decode algorithm on this host's cores (oracle port)."""
+    """--impl reference: the reference's eager CPU decode on this host's cores (rank 0 only)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    torch.set_num_threads(os.cpu_count() or 1)
-    step_s, threads, sample = cpu_decode_sample(repeats=max(1, min(args.steps, 3)))
-    value = BATCH / step_s
+    steps = max(3, min(args.steps, 5))
+    value, ran, threads, kind, sample, step_s = cpu_baseline(steps)
     line = {"metric": METRIC, "value": value, "unit": "tok/s", "impl": "reference", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
+            "steps": ran, "warmup": 1, "ms_per_step": step_s * 1e3, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": config(args),
-            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": kind, "sample": sample},
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -292,6 +423,164 @@ def verify_config5(peak):
             "useful_TFLOP/s": flops / ms / 1e9, "kernel": "fb_verify_attention (tcgen05)"}
 
 
+def graph_time_ms(run, repeats=5):
+    """Median device time of one replay of ``run`` captured in a CUDA graph (CUDA events on the
+    replaying stream, after one eager warm-up pass)."""
+    run()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        run()
+    times = []
+    for _ in range(repeats):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        graph.replay()
+        end.record()
+        end.synchronize()
+        times.append(start.elapsed_time(end))
+    del graph
+    return statistics.median(times)
+
+
+def config1_attention(peak):
+    """decode attention, batch 1, 16/8 heads (G=2), D=128, 2048 valid slots,
+    N(0,1) bf16 (seed 0), scale 1/sqrt(128); BASELINE's 8 KV splits (the cluster form with 8 CTAs
+    per (row, KV head) pair, each streaming 1/8 of the slots) and the kernel's own split choice.
+    The north-star target (>= 80% of HBM peak) applies at >= 8k slots, so the same head shape is
+    also timed at 8192, 16384 and 32768 slots (the kernel's own choice). Graph-timed over enough
+    cache copies that every launch reads from HBM (> L2)."""
+    from kernels._native import lib
+    from kernels.decode_attention import _ctas, attend, workspace_bytes
+    results = {}
+    for length in (2048, 8192, 16384, 32768):
+        kv_bytes = 2 * 8 * length * 128 * 2
+        copies = max(2, int(math.ceil(400e6 / kv_bytes)))
+        g = torch.Generator(device="cuda").manual_seed(0)
+        q = torch.randn(1, 16, 1, 128, device="cuda", generator=g).to(torch.bfloat16)
+        sets = [(torch.randn(1, 8, length, 128, device="cuda", generator=g).to(torch.bfloat16),
+                 torch.randn(1, 8, length, 128, device="cuda", generator=g).to(torch.bfloat16)) for _ in range(copies)]
+        position = torch.tensor([length - 1], dtype=torch.int64, device="cuda")
+        ctas = _ctas((torch.device("cuda", torch.cuda.current_device()), 1, 8, length, 128))
+        ws = torch.zeros(workspace_bytes(1, 16, 8, 128, ctas), dtype=torch.uint8, device="cuda")
+        out = torch.empty(1, 1, 16, 128, dtype=torch.bfloat16, device="cuda")
+
+        def run():
+            for k, v in sets:
+                attend(q, k, v, position, 1 / math.sqrt(128), out=out, workspace=ws, ctas=ctas)
+
+        nbytes = kv_bytes + 2 * 16 * 128 * 2
+        forms = [("auto", None)] + ([("8 splits", (8, 4))] if length == 2048 else [])
+        for name, shape in forms:
+            if shape is not None:
+                assert lib.fb_decode_attention_cluster_shape(*shape) == 0
+            try:
+                ms = graph_time_ms(run) / copies
+            finally:
+                lib.fb_decode_attention_cluster_shape(0, 0)
+            results[f"L{length} {name}"] = {"us": ms * 1e3, "GB/s": nbytes / ms / 1e6, "frac": nbytes / ms / 1e6 / peak}
+        del sets
+        torch.cuda.empty_cache()
+    return {"workload": "BASELINE config 1: B=1, 16/8 heads, D=128, 2048 slots, N(0,1) bf16 seed 0 (plus the "
+                        "same head shape at 8k-32k slots)", "algorithmic_bytes_L2048": 2 * 8 * 2048 * 128 * 2 + 8192,
+            "results": results}
+
+
+def config2_decode(peak, new_tokens=256, prompt_length=512):
+    """Qwen3-0.6B architecture (random init, seed 0), batch 1, a 512-token
+    random prompt, 256 greedy tokens on one GPU: the first from the prefill, then 255 replays of
+    the captured decode step, device-timed. Per-step roofline: every weight once plus the K/V of
+    the valid slots (mean over the steps) per step time."""
+    import decode as fdecode
+    import qwen3
+    cfg = qwen3.Config.make(**qwen3.PRESETS["qwen3-0.6b"])
+    weights = qwen3.random_init(cfg, "cuda", seed=0)
+    prompt = torch.randint(0, cfg.vocab_size, (1, prompt_length), generator=torch.Generator().manual_seed(0))
+    state = fdecode.DecodeState(weights, 1, prompt_length, new_tokens + 8)
+    with torch.inference_mode():
+        state.prefill(prompt.cuda())
+    state.capture()
+    steps = new_tokens - 1
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        state.step()
+    end.record()
+    end.synchronize()
+    ms = start.elapsed_time(end) / steps
+    state.release()
+    step_bytes = weights.nbytes_per_step() + state.cache.nbytes_valid(prompt_length + 1 + steps // 2)
+    del state, weights
+    torch.cuda.empty_cache()
+    return {"workload": "BASELINE config 2: Qwen3-0.6B architecture, random init seed 0, batch 1, 512-token "
+                        "prompt, 256 greedy tokens, 1 GPU", "value": 1e3 / ms, "unit": "tok/s", "ms_per_step": ms,
+            "roofline": {"bound": "hbm", "algorithmic_bytes_per_step": step_bytes,
+                         "achieved": step_bytes / ms / 1e6, "peak": peak, "unit": "GB/s",
+                         "frac": step_bytes / ms / 1e6 / peak}}
+
+
+def parity_gate(comm, rank, world, device):
+    """Correctness before any number: the decode step at this tensor-parallel size on the real
+    Qwen3-8B architecture truncated to 2 layers (random init, seed 1, this rank's shard), batch
+    16, 16-token random prompts, 4 greedy tokens.
+      - the captured graph's tokens equal the eager step's;
+      - every rank holds the same token ids;
+      - rank 0 runs the CPU oracle (oracle/model.py, the reference's arithmetic) on the unsharded
+        weights, teacher-forced on the GPU's tokens: logits within 2e-2 of the logit scale and the
+        chosen token's gap to the row maximum within max(0.02, 2e-2 of the scale).
+    Returns (ok, details); every rank gets rank 0's verdict."""
+    import decode as fdecode
+    import qwen3
+    from oracle import model as omodel
+    cfg = qwen3.Config.make(**{**qwen3.PRESETS[PRESET], "num_hidden_layers": 2})
+    weights = qwen3.random_init(cfg, device, seed=1, tp_rank=rank, tp_size=world)
+    prompt = torch.randint(0, cfg.vocab_size, (BATCH, 16), generator=torch.Generator().manual_seed(1))
+    steps = 4
+    eager = fdecode.DecodeState(weights, BATCH, 16, steps + 4, comm=comm, device=device)
+    tokens, logits = fdecode.greedy(eager, prompt.to(device), steps)
+    graph = fdecode.DecodeState(weights, BATCH, 16, steps + 4, comm=comm, device=device)
+    graph.prefill(prompt.to(device))
+    replayed = [graph.token_ids[:, 0].clone()]
+    graph.capture()
+    for _ in range(steps - 1):
+        graph.step()
+        replayed.append(graph.token_ids[:, 0].clone())
+    torch.cuda.synchronize()
+    graph.release()
+    checks = {"graph == eager": bool(torch.equal(torch.stack(replayed, 1), tokens))}
+    if world > 1:
+        gathered = [torch.empty_like(tokens) for _ in range(world)]
+        torch.distributed.all_gather(gathered, tokens)
+        checks["ranks agree"] = all(bool(torch.equal(t, gathered[0])) for t in gathered)
+    detail = {}
+    if rank == 0:
+        full = qwen3.random_init(cfg, device, seed=1)
+        model = omodel.Model(omodel.Config(**qwen3.PRESETS[PRESET] | {"num_hidden_layers": 2}),
+                             qwen3.to_state_dict(full))
+        del full
+        cache = model.new_cache(BATCH, 16 + steps)
+        expect = [model.prefill(prompt, cache)]
+        host_tokens = tokens.cpu()
+        for step in range(steps - 1):
+            expect.append(model.decode(host_tokens[:, step], 16 + step, cache))
+        expect = torch.stack(expect, 1).float()
+        got = logits.cpu()
+        scale = float(expect.abs().max())
+        err = float((got - expect).abs().max())
+        chosen = expect.gather(-1, host_tokens[..., None])[..., 0]
+        gap = float((expect.max(-1).values - chosen).max())
+        checks["logits vs oracle"] = err <= 2e-2 * scale
+        checks["teacher-forced gap"] = gap <= max(0.02, 2e-2 * scale)
+        detail = {"max_abs_err": err, "logit_scale": scale, "max_gap": gap}
+    del eager, graph, weights
+    torch.cuda.empty_cache()
+    verdict = torch.tensor([1 if all(checks.values()) else 0], device=device)
+    if world > 1:
+        torch.distributed.broadcast(verdict, 0)
+    return bool(verdict.item()), {"checks": checks, **detail}
+
+
 def main():
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--gpus", type=int, default=1)
@@ -323,13 +612,18 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
         group = torch.distributed.group.WORLD
     peak, peak_kind = peaks()
+    comm = fdecode.Communicator(group, world, rank)
+    parity_ok, parity = parity_gate(comm, rank, world, device)
+    if not parity_ok:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        raise SystemExit(f"parity gate failed, no number printed: {json.dumps(parity)}")
     cfg = qwen3.Config.make(**qwen3.PRESETS[PRESET])
     weights = qwen3.random_init(cfg, device, seed=0, tp_rank=rank, tp_size=world)
     prompt = torch.randint(0, cfg.vocab_size, (BATCH, PROMPT), generator=torch.Generator().manual_seed(0)).to(device)
     total_steps = args.warmup + args.steps
     # capacity: the prompt, the warm-up and timed steps of both timed loops, plus one spare slot
-    state = fdecode.DecodeState(weights, BATCH, PROMPT, 2 * total_steps + 2,
-                                comm=fdecode.Communicator(group, world, rank), device=device)
+    state = fdecode.DecodeState(weights, BATCH, PROMPT, 2 * total_steps + 2, comm=comm, device=device)
     with torch.inference_mode():
         state.prefill(prompt)
     state.capture()
@@ -351,7 +645,6 @@ def main():
     clocks = Clocks(list(range(world)) if world > 1 else [local]) if rank == 0 else None
     if clocks:
         clocks.start()
-    launches_before = _native.launches
     barrier()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -414,7 +707,6 @@ def main():
     step_frac = step_bytes / (ms_per_step / 1e3) / 1e9 / peak
     assert _native.device_error() == 0, "a kernel raised the device error word"
     state.release()
-    multicast = bool(state.peers is not None and state.peers.multicast)
     del state
     torch.cuda.empty_cache()
 
@@ -428,23 +720,24 @@ def main():
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init weights and token ids, seed 0)",
             "config": config(args), "e2e": e2e, "roofline": roofline,
             "per_gpu_hbm_frac": step_frac,
-            "gpu_launches": per_step_launches * args.steps}
+            "gpu_launches": per_step_launches * args.steps,
+            "parity": "ok", "parity_gate": parity}
     if clock:
         line["clocks"] = clock
     if world > 1:
-        line["allreduce"] = ("flagged fp32 words pushed by the producer (split partials + fb_reduce_push, or the "
-                             "projection's epilogue at one split) into every rank's symmetric-memory receive buffer "
-                             + ("through the NVSwitch multicast address (multimem.st)" if multicast else
-                                "by NVLink peer stores") + "; consumer polls, sums ranks in order + add/RMSNorm")
+        line["allreduce"] = ("split-K partials summed by fb_reduce_push and stored as flagged fp32 words into every "
+                             "rank's symmetric-memory receive buffer by NVLink peer stores; the consumer polls, sums "
+                             "the ranks in order and applies add+RMSNorm")
 
     if world == 1 and not args.no_sweep:
         line["attention_sweep"] = attention_sweep(peak)
         line["verify_attention_config5"] = verify_config5(peak)
+        line["config1_attention"] = config1_attention(peak)
+        line["config2_qwen3_0_6b"] = config2_decode(peak)
     if world == 1 and not args.no_cpu:
-        torch.set_num_threads(os.cpu_count() or 1)
-        step_s, threads, sample = cpu_decode_sample()
-        line["cpu_baseline"] = {"value": BATCH / step_s, "unit": "tok/s", "cores": threads, "kind": "port",
-                                "sample": sample}
+        value_cpu, ran, threads, kind, sample, _ = cpu_baseline(2, layers=4)
+        line["cpu_baseline"] = {"value": value_cpu, "unit": "tok/s", "cores": threads, "kind": kind,
+                                "sample": sample, "steps": ran}
     print(json.dumps(line), flush=True)
 
 
