@@ -1,33 +1,51 @@
-// Tensor-parallel all-reduce producer for split-K projections (sm_100a).
+// Tensor-parallel all-reduce + add + RMSNorm over NVLink peer memory (sm_100a), owner-computes:
+// a reduce-scatter of fp32 partials followed by an all-gather of the summed bf16 rows.
 //
-// fb_reduce_push sums a projection's fp32 split-K partials [S, M, N] in split order (the
-// projection's own arithmetic, as a single-split epilogue would see it) and stores every
-// value, as one 8-byte word with the flag (uint32)(*epoch) + 1 in its high half, into slab
-// `rank` of recv[use] on every rank - the low-latency push protocol that
-// fb_allreduce_add_rmsnorm polls. The decode step's producer whenever the projection has K
-// splits: on B200, summing the splits inside the projection (cluster reduction or the split
-// fix-up) and pushing from its epilogue, or pushing from the polling kernel itself
-// (fb_reduce_push_add_rmsnorm), each measured slower than split partials plus this pass.
+// The reference is single-GPU; this replaces the all-reduce a tensor-parallel decode step needs
+// after o_proj and down_proj, and folds the residual add + RMSNorm that follows
+// (engine/kernels/rmsnorm.py:75-95 arithmetic) into it.
+//
+// Every value travels inside an 8-byte word whose high half is the flag (uint32)(*epoch) + 1
+// and is stored whole, so a reader that sees the flag sees the value: no fence, counter, reset
+// or barrier sits on the step's path. Column slice q = [q*W/world, (q+1)*W/world) of the
+// hidden width W is owned by rank q.
+//  1. fb_reduce_scatter_push (after the projection's split-K partials): each rank sums its
+//     partials in split order and stores every fp32 value, flagged, only into the owner's
+//     receive slab rs[use][rank] - M*W words per rank in total.
+//  2. fb_allreduce_add_rmsnorm, phase B (the owner): polls rs[use][0..world) for its slice,
+//     sums the ranks in rank order (the same bits a rank-order sum of whole rows gives), rounds
+//     to bf16, adds the residual (rounded again), and stores the summed bf16 pairs, flagged,
+//     into ag[use] of every rank; it also stores each row's fp32 sum of squares over its
+//     slice into ss[use][rank] of every rank.
+//     Phase C (every rank, every row): polls ag[use] for the whole row and the world partial
+//     sums of squares, adds those in rank order (identical bits on every rank), and writes the
+//     normalized row bf16(bf16(s * inv) * w) and the summed row (the next residual).
+// NVLink volume per use and rank: M*W*8 bytes of partials plus M*W*4 bytes of summed values
+// (1/world of each stays local), against world*M*W*8 for pushing whole partials to every rank.
+//
+// The consumer's CTAs wait on one another's stores (phase C on other ranks' phase B), so its
+// grid never exceeds the SM count: every CTA is resident, each does all its phase-B work before
+// any phase-C wait, and every wait is bounded (2 s; on timeout the error word is set and zeros
+// are used).
 #include "common.cuh"
 
 namespace fb {
 namespace ar {
 
-constexpr int kThreads = 128;
+constexpr int kThreads = 256;
 constexpr int kBatch = 8;  // split slabs in flight per thread
 constexpr int kMaxWorld = 8;
+constexpr int kChunk = 2 * kThreads;  // columns of one phase-C work item (one pair per thread)
 
-struct Params {
+struct PushParams {
   const float* partials;  // [splits, m, n]
   int splits, m, n, world, rank, use;
-  uint64_t* peer_recv[kMaxWorld];
-  uint64_t* mc_recv;  // multicast address of the receive buffers (NVSwitch), or null
+  uint64_t* peer_rs[kMaxWorld];
   const int64_t* epoch;
 };
 
-// Two values per thread, so one store instruction of a warp writes 512 contiguous bytes
-// (32 lanes x one 16-byte pair of flagged words) to each peer.
-__global__ void __launch_bounds__(kThreads) reduce_push_kernel(const __grid_constant__ Params p) {
+// One pair of columns per thread: the pair's owner gets one 16-byte store of two flagged words.
+__global__ void __launch_bounds__(kThreads) reduce_scatter_push_kernel(const __grid_constant__ PushParams p) {
   pdl_wait();
   pdl_trigger();
   const int64_t i = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) * 2;
@@ -50,16 +68,155 @@ __global__ void __launch_bounds__(kThreads) reduce_push_kernel(const __grid_cons
     }
   }
   const uint64_t flag = static_cast<uint64_t>(static_cast<uint32_t>(*p.epoch) + 1u) << 32;
+  const int m = static_cast<int>(i / p.n), col = static_cast<int>(i % p.n);
+  const int slice = p.n / p.world;
+  const int owner = col / slice;
+  const size_t off = ((static_cast<size_t>(p.use) * p.world + p.rank) * p.m + m) * slice + (col - owner * slice);
   const uint64_t w0 = flag | __float_as_uint(x.x), w1 = flag | __float_as_uint(x.y);
-  const size_t off = (static_cast<size_t>(p.use) * p.world + p.rank) * count + i;
-  if (p.mc_recv != nullptr) {
-    // one store per word through the multicast address: NVSwitch delivers it to every rank
-    asm volatile("multimem.st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p.mc_recv + off), "l"(w0) : "memory");
-    asm volatile("multimem.st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p.mc_recv + off + 1), "l"(w1) : "memory");
-  } else {
-    for (int q = 0; q < p.world; ++q)
-      asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p.peer_recv[q] + off), "l"(w0), "l"(w1)
-                   : "memory");
+  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p.peer_rs[owner] + off), "l"(w0), "l"(w1)
+               : "memory");
+}
+
+struct NormParams {
+  const uint64_t* rs;             // this rank's reduce-scatter slabs, all uses
+  const uint64_t* ag;             // this rank's all-gather rows, all uses
+  const uint64_t* ss;             // this rank's partial sums of squares, all uses
+  uint64_t* peer_ag[kMaxWorld];   // every rank's all-gather rows
+  uint64_t* peer_ss[kMaxWorld];   // every rank's partial sums of squares
+  const int64_t* epoch;
+  const __nv_bfloat16* residual;  // [m, n]
+  const __nv_bfloat16* w;         // [n]
+  __nv_bfloat16* out;             // [m, n]
+  __nv_bfloat16* sum;             // [m, n]
+  int m, n, world, rank, use, chunks;
+  float eps;
+  unsigned* err;
+};
+
+// Polls `count` (<= kMaxWorld) flagged words at src[0], src[stride], ... until all carry `flag`;
+// false after the wait budget (or at once when an earlier wait gave up).
+__device__ __forceinline__ bool poll_words(const uint64_t* src, size_t stride, int count, uint32_t flag,
+                                           unsigned* err, uint64_t (&words)[kMaxWorld]) {
+  unsigned long long start = 0;
+  for (;;) {
+    bool ready = true;
+#pragma unroll
+    for (int q = 0; q < kMaxWorld; ++q)
+      if (q < count) {
+        asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(words[q]) : "l"(src + q * stride));
+        ready = ready && static_cast<uint32_t>(words[q] >> 32) == flag;
+      }
+    if (ready) return true;
+    if (start == 0) start = globaltimer();
+    if ((err != nullptr && (*reinterpret_cast<volatile unsigned*>(err) & kErrTimeoutFull) != 0) ||
+        globaltimer() - start > kWaitBudgetNs) {
+      raise_error(err, kErrTimeoutFull);
+      return false;
+    }
+  }
+}
+
+// Two consecutive values of each rank's slab (one 16-byte load per rank), summed in rank order.
+__device__ __forceinline__ bool poll_pair(const uint64_t* src, size_t stride, int world, uint32_t flag,
+                                          unsigned* err, float& x0, float& x1) {
+  unsigned long long start = 0;
+  for (;;) {
+    bool ready = true;
+    uint64_t a[kMaxWorld], b[kMaxWorld];
+#pragma unroll
+    for (int q = 0; q < kMaxWorld; ++q)
+      if (q < world)
+        asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a[q]), "=l"(b[q]) : "l"(src + q * stride));
+#pragma unroll
+    for (int q = 0; q < kMaxWorld; ++q)
+      if (q < world) {
+        ready = ready && static_cast<uint32_t>(a[q] >> 32) == flag && static_cast<uint32_t>(b[q] >> 32) == flag;
+        const float u = __uint_as_float(static_cast<uint32_t>(a[q]));
+        const float v = __uint_as_float(static_cast<uint32_t>(b[q]));
+        x0 = q == 0 ? u : x0 + u;
+        x1 = q == 0 ? v : x1 + v;
+      }
+    if (ready) return true;
+    if (start == 0) start = globaltimer();
+    if ((err != nullptr && (*reinterpret_cast<volatile unsigned*>(err) & kErrTimeoutFull) != 0) ||
+        globaltimer() - start > kWaitBudgetNs) {
+      raise_error(err, kErrTimeoutFull);
+      x0 = x1 = 0.f;
+      return false;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) allreduce_norm_kernel(const __grid_constant__ NormParams p) {
+  __shared__ float scratch[kThreads / 32];
+  // the gains are never written while decoding: none of this kernel's inputs before the wait
+  pdl_wait();
+  pdl_trigger();
+  const uint32_t flag = static_cast<uint32_t>(*p.epoch) + 1u;
+  const uint64_t hi = static_cast<uint64_t>(flag) << 32;
+  const int W = p.world, slice = p.n / W, half = p.n / 2;
+  const size_t use_rs = static_cast<size_t>(p.use) * W * p.m * slice;
+  const size_t use_ag = static_cast<size_t>(p.use) * p.m * half;
+  const size_t use_ss = static_cast<size_t>(p.use) * W * p.m;
+
+  // ---- phase B: this rank's slice of rows blockIdx.x, blockIdx.x + gridDim.x, ... ----
+  for (int row = blockIdx.x; row < p.m; row += gridDim.x) {
+    float ss = 0.f;
+    for (int j = threadIdx.x; j < slice / 2; j += kThreads) {
+      const int col = p.rank * slice + 2 * j;
+      float x0, x1;
+      poll_pair(p.rs + use_rs + static_cast<size_t>(row) * slice + 2 * j, static_cast<size_t>(p.m) * slice, W,
+                flag, p.err, x0, x1);
+      const uint32_t r2 = *reinterpret_cast<const uint32_t*>(p.residual + static_cast<size_t>(row) * p.n + col);
+      const float s0 = bf16_round(bf16_round(x0) + bf16_lo(r2));
+      const float s1 = bf16_round(bf16_round(x1) + bf16_hi(r2));
+      ss += s0 * s0;
+      ss += s1 * s1;
+      const uint64_t word = hi | pack_bf16x2(s0, s1);
+      const size_t off = use_ag + static_cast<size_t>(row) * half + col / 2;
+      for (int q = 0; q < W; ++q)
+        asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p.peer_ag[q] + off), "l"(word) : "memory");
+    }
+    ss = warp_sum(ss);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) scratch[warp] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float total = 0.f;
+      for (int i = 0; i < kThreads / 32; ++i) total += scratch[i];
+      const uint64_t word = hi | __float_as_uint(total);
+      const size_t off = use_ss + static_cast<size_t>(p.rank) * p.m + row;
+      for (int q = 0; q < W; ++q)
+        asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p.peer_ss[q] + off), "l"(word) : "memory");
+    }
+    __syncthreads();
+  }
+
+  // ---- phase C: (row, chunk) items; every thread one pair of columns ----
+  for (int item = blockIdx.x; item < p.m * p.chunks; item += gridDim.x) {
+    const int row = item / p.chunks, chunk = item % p.chunks;
+    const int col = chunk * kChunk + 2 * threadIdx.x;
+    if (col >= p.n) continue;
+    // the row's partial sums of squares, added in rank order (the same bits on every rank)
+    uint64_t words[kMaxWorld];
+    float total = 0.f;
+    if (poll_words(p.ss + use_ss + row, p.m, W, flag, p.err, words)) {
+#pragma unroll
+      for (int q = 0; q < kMaxWorld; ++q)
+        if (q < W) total += __uint_as_float(static_cast<uint32_t>(words[q]));
+    }
+    uint64_t pair[kMaxWorld];
+    float s0 = 0.f, s1 = 0.f;
+    if (poll_words(p.ag + use_ag + static_cast<size_t>(row) * half + col / 2, 0, 1, flag, p.err, pair)) {
+      s0 = bf16_lo(static_cast<uint32_t>(pair[0]));
+      s1 = bf16_hi(static_cast<uint32_t>(pair[0]));
+    }
+    const float inv = 1.0f / sqrtf(total / static_cast<float>(p.n) + p.eps);
+    const uint32_t w2 = __ldg(reinterpret_cast<const uint32_t*>(p.w + col));
+    const size_t o = static_cast<size_t>(row) * p.n + col;
+    *reinterpret_cast<uint32_t*>(p.sum + o) = pack_bf16x2(s0, s1);
+    *reinterpret_cast<uint32_t*>(p.out + o) =
+        pack_bf16x2(bf16_round(s0 * inv) * bf16_lo(w2), bf16_round(s1 * inv) * bf16_hi(w2));
   }
 }
 
@@ -68,12 +225,12 @@ __global__ void __launch_bounds__(kThreads) reduce_push_kernel(const __grid_cons
 
 using namespace fb;
 
-extern "C" int fb_reduce_push(const void* partials, int splits, int m, int n, int world, int rank, int use,
-                              void* const* peer_recv, void* multicast_recv, const int64_t* epoch, void* stream) {
-  if (!partials || !peer_recv || !epoch || splits <= 0 || m <= 0 || n <= 0) return FB_ERR_ARG;
+extern "C" int fb_reduce_scatter_push(const void* partials, int splits, int m, int n, int world, int rank, int use,
+                                      void* const* peer_rs, const int64_t* epoch, void* stream) {
+  if (!partials || !peer_rs || !epoch || splits <= 0 || m <= 0 || n <= 0) return FB_ERR_ARG;
   if (world < 1 || world > ar::kMaxWorld || rank < 0 || rank >= world || use < 0) return FB_ERR_ARG;
-  if (n % 2 != 0) return FB_ERR_SHAPE;
-  ar::Params p{};
+  if (n % (2 * world) != 0) return FB_ERR_SHAPE;
+  ar::PushParams p{};
   p.partials = static_cast<const float*>(partials);
   p.splits = splits;
   p.m = m;
@@ -82,15 +239,52 @@ extern "C" int fb_reduce_push(const void* partials, int splits, int m, int n, in
   p.rank = rank;
   p.use = use;
   p.epoch = epoch;
-  if (multicast_recv != nullptr && (reinterpret_cast<uintptr_t>(multicast_recv) & 15u)) return FB_ERR_ARG;
-  p.mc_recv = static_cast<uint64_t*>(multicast_recv);
   for (int r = 0; r < world; ++r) {
-    if (!peer_recv[r] || (reinterpret_cast<uintptr_t>(peer_recv[r]) & 15u)) return FB_ERR_ARG;
-    p.peer_recv[r] = static_cast<uint64_t*>(peer_recv[r]);
+    if (!peer_rs[r] || (reinterpret_cast<uintptr_t>(peer_rs[r]) & 15u)) return FB_ERR_ARG;
+    p.peer_rs[r] = static_cast<uint64_t*>(peer_rs[r]);
   }
-  const int64_t threads = (static_cast<int64_t>(m) * n + 1) / 2;
+  const int64_t threads = static_cast<int64_t>(m) * n / 2;
   const int64_t blocks = (threads + ar::kThreads - 1) / ar::kThreads;
   if (blocks >= (1ll << 31)) return FB_ERR_SHAPE;
-  return launch_ex(ar::reduce_push_kernel, dim3(static_cast<unsigned>(blocks)), dim3(ar::kThreads), 0,
+  return launch_ex(ar::reduce_scatter_push_kernel, dim3(static_cast<unsigned>(blocks)), dim3(ar::kThreads), 0,
+                   static_cast<cudaStream_t>(stream), 1, p);
+}
+
+extern "C" int fb_allreduce_add_rmsnorm(const void* rs, const void* ag, const void* ss, void* const* peer_ag,
+                                        void* const* peer_ss, int use, int world, int rank, const int64_t* epoch,
+                                        const void* residual, const void* w, void* out, void* sum, int rows,
+                                        int width, float eps, void* stream) {
+  if (!rs || !ag || !ss || !peer_ag || !peer_ss || !epoch || !residual || !w || !out || !sum) return FB_ERR_ARG;
+  if (use < 0 || world < 1 || world > ar::kMaxWorld || rank < 0 || rank >= world || rows <= 0 || width <= 0)
+    return FB_ERR_ARG;
+  if (width % (2 * world) != 0 || width % 8 != 0) return FB_ERR_SHAPE;
+  ar::NormParams p{};
+  p.rs = static_cast<const uint64_t*>(rs);
+  p.ag = static_cast<const uint64_t*>(ag);
+  p.ss = static_cast<const uint64_t*>(ss);
+  for (int r = 0; r < world; ++r) {
+    if (!peer_ag[r] || !peer_ss[r] || (reinterpret_cast<uintptr_t>(peer_ag[r]) & 7u) ||
+        (reinterpret_cast<uintptr_t>(peer_ss[r]) & 7u))
+      return FB_ERR_ARG;
+    p.peer_ag[r] = static_cast<uint64_t*>(peer_ag[r]);
+    p.peer_ss[r] = static_cast<uint64_t*>(peer_ss[r]);
+  }
+  p.epoch = epoch;
+  p.residual = static_cast<const __nv_bfloat16*>(residual);
+  p.w = static_cast<const __nv_bfloat16*>(w);
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.sum = static_cast<__nv_bfloat16*>(sum);
+  p.m = rows;
+  p.n = width;
+  p.world = world;
+  p.rank = rank;
+  p.use = use;
+  p.chunks = (width + ar::kChunk - 1) / ar::kChunk;
+  p.eps = eps;
+  p.err = error_word();
+  // every CTA resident at once (phase C waits on phase B of other CTAs, here and on the peers)
+  long long grid = static_cast<long long>(rows) * p.chunks;
+  if (grid > sm_count()) grid = sm_count();
+  return launch_ex(ar::allreduce_norm_kernel, dim3(static_cast<unsigned>(grid)), dim3(ar::kThreads), 0,
                    static_cast<cudaStream_t>(stream), 1, p);
 }

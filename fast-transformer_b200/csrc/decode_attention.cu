@@ -28,7 +28,6 @@
 #include <mutex>
 
 #include "common.cuh"
-#include "rope_math.cuh"
 
 namespace fb {
 namespace attn {
@@ -51,18 +50,6 @@ struct Params {
   int batch, q_heads, kv_heads, groups, capacity, ctas;
   float scale_log2;
   unsigned* err;
-  // Fused QK-norm/RoPE/KV append (cluster form, D = 128): the query heads, and the newest K/V
-  // slot, come from the packed qkv projection output instead of `q` and the cache.
-  int rope;
-  const void* packed;  // bf16 [B, (Hq + 2 Hkv) D] (psplits 0) or fp32 split partials [psplits, B, ...]
-  int psplits;
-  const __nv_bfloat16* q_gain;
-  const __nv_bfloat16* k_gain;
-  float q_eps, k_eps;
-  const __nv_bfloat16* cos;  // whole RoPE tables [>= capacity, D]
-  const __nv_bfloat16* sin;
-  __nv_bfloat16* keys;  // the cache the tensor maps read, [B, Hkv, capacity, D]
-  __nv_bfloat16* values;
 };
 
 // Valid length of row b: position + 1 clamped into [0, capacity].
@@ -248,24 +235,6 @@ __device__ __forceinline__ void attend_tile(WarpAcc<D>& a, uint8_t* kt, uint8_t*
     ldmatrix_x4_trans(addr, a0, a1, a2, a3);
     mma_bf16_16816(a.o[i], a0, a1, a2, a3, pb0, pb1);
   }
-}
-
-// start_pair with the query heads staged in shared memory (bf16 [kHeadsPad][D], rows past G
-// zero): the fused QK-norm/RoPE form.
-template <int D>
-__device__ __forceinline__ void start_pair_staged(WarpAcc<D>& a, const __nv_bfloat16* q_s, int G, int lane) {
-  const int g = lane >> 2, c = lane & 3;
-  const bool live = g < G;
-  const uint32_t* qrow = reinterpret_cast<const uint32_t*>(q_s + (live ? g : 0) * D);
-#pragma unroll
-  for (int kk = 0; kk < D / 16; ++kk) {
-    a.qb[kk][0] = live ? qrow[(kk * 16 + 2 * c) / 2] : 0u;
-    a.qb[kk][1] = live ? qrow[(kk * 16 + 8 + 2 * c) / 2] : 0u;
-  }
-#pragma unroll
-  for (int i = 0; i < D / 16; ++i) a.o[i][0] = a.o[i][1] = a.o[i][2] = a.o[i][3] = 0.f;
-  a.m0 = a.m1 = -INFINITY;
-  a.l0 = a.l1 = 0.f;
 }
 
 // Parks this warp's state in shared memory for the cross-warp reduction: per-head (max,
@@ -654,12 +623,10 @@ struct ClusterSmem {
   static constexpr int kPartO = kHeadsPad * D * 4;  // this CTA's O per (head, dim)
   static constexpr int kPartML = kHeadsPad * 2 * 4;  // (max, denominator) per head
   static constexpr int kWeights = kMaxCluster * kHeadsPad * 4 + kHeadsPad * 4;
-  static constexpr int kQStaged = kHeadsPad * D * 2;  // fused form: the pair's query heads, bf16
-  static constexpr int kKvNew = 2 * D * 2;            // fused form: the newest K and V rows, bf16
   static constexpr int kBars = 2 * NS * 8;
   static constexpr int kTotal =
-      1024 + kStagesBytes + kRedML + kPartO + kPartML + kWeights + kQStaged + kKvNew + kBars + 16;
-  static_assert((kStagesBytes + kRedML + kPartO + kPartML + kWeights + kQStaged + kKvNew) % 16 == 0,
+      1024 + kStagesBytes + kRedML + kPartO + kPartML + kWeights + kBars + 16;
+  static_assert((kStagesBytes + kRedML + kPartO + kPartML + kWeights) % 16 == 0,
                 "mbarrier alignment");
 };
 
@@ -677,9 +644,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* part_ml = part_o + S::kPartO / 4;
   float* wts = part_ml + S::kPartML / 4;  // [rank][head] merge weights
   float* den = wts + kMaxCluster * kHeadsPad;
-  __nv_bfloat16* q_s = reinterpret_cast<__nv_bfloat16*>(den + kHeadsPad);  // fused form only
-  __nv_bfloat16* kv_new = q_s + kHeadsPad * D;                              // [K row | V row]
-  uint64_t* full = reinterpret_cast<uint64_t*>(kv_new + 2 * D);
+  uint64_t* full = reinterpret_cast<uint64_t*>(den + kHeadsPad);
   uint64_t* empty = full + NS;
   int* abort_word = reinterpret_cast<int*>(empty + NS);
 
@@ -714,13 +679,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Cache rows below the position were written by earlier steps: the ring is filled
       // before the dependency wait; the row's last tile (the previous kernel appends its
       // newest slot) waits for the previous kernel.
-      // (In the fused form this kernel writes the newest slot itself and patches it into the
-      // landed tile, so even the last tile is fetched before the wait.)
       bool waited = false;
       for (int k = 0; k < count; ++k) {
         const int s = k % NS;
         const int j = t0 + k;
-        if (!waited && (k >= NS || (j == n - 1 && !p.rope))) {
+        if (!waited && (k >= NS || j == n - 1)) {
           pdl_wait();
           waited = true;
         }
@@ -753,59 +716,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   pdl_trigger();
   const int ctid = threadIdx.x;  // 0..127
   WarpAcc<D> acc;
-  const long long pos = static_cast<long long>(len) - 1;  // the newest slot (fused form)
-  if constexpr (D == 128) {
-    if (p.rope) {
-      // QK-norm + RoPE of this pair's query heads from the packed projection (the stand-alone
-      // qk_rope kernel's arithmetic, rope_math.cuh) into q_s; the CTA holding the pair's last
-      // tile also normalizes/rotates the K head, copies the V head, writes both into the
-      // cache slot and keeps them for the tile patch below.
-      const int width = (p.q_heads + 2 * Hkv) * D;
-      const size_t stride = static_cast<size_t>(p.batch) * width;
-      const size_t row0 = static_cast<size_t>(b) * width;
-      const int d0 = lane * 4;
-      const long long phase = pos < 0 ? 0 : pos;
-      for (int gq = warp; gq < kHeadsPad; gq += kConsumerWarps) {
-        __nv_bfloat16 qo[4];
-        if (gq < G) {
-          float x[4], gw[4];
-          rope::load_packed_values<4, 4>(p.packed, p.psplits, row0 + (h * G + gq) * D + d0, stride, x);
-          rope::load_bf16<4>(p.q_gain + d0, gw);
-          rope::norm_rope<D>(x, gw, p.q_eps, p.cos + phase * D + d0, p.sin + phase * D + d0, lane, qo);
-        } else {
-          qo[0] = qo[1] = qo[2] = qo[3] = __float2bfloat16_rn(0.f);
-        }
-        uint2 w;
-        w.x = pack_bf16x2(__bfloat162float(qo[0]), __bfloat162float(qo[1]));
-        w.y = pack_bf16x2(__bfloat162float(qo[2]), __bfloat162float(qo[3]));
-        *reinterpret_cast<uint2*>(q_s + gq * D + d0) = w;
-      }
-      if (rank == C - 1 && warp == 0 && pos >= 0) {
-        float x[4], gw[4], v[4];
-        rope::load_packed_values<4, 4>(p.packed, p.psplits, row0 + (p.q_heads + h) * D + d0, stride, x);
-        rope::load_packed_values<4, 4>(p.packed, p.psplits, row0 + (p.q_heads + Hkv + h) * D + d0, stride, v);
-        rope::load_bf16<4>(p.k_gain + d0, gw);
-        __nv_bfloat16 ko[4];
-        rope::norm_rope<D>(x, gw, p.k_eps, p.cos + phase * D + d0, p.sin + phase * D + d0, lane, ko);
-        uint2 kw, vw;
-        kw.x = pack_bf16x2(__bfloat162float(ko[0]), __bfloat162float(ko[1]));
-        kw.y = pack_bf16x2(__bfloat162float(ko[2]), __bfloat162float(ko[3]));
-        vw.x = pack_bf16x2(v[0], v[1]);  // exact: v holds bf16 values
-        vw.y = pack_bf16x2(v[2], v[3]);
-        *reinterpret_cast<uint2*>(kv_new + d0) = kw;
-        *reinterpret_cast<uint2*>(kv_new + D + d0) = vw;
-        const size_t slot = ((static_cast<size_t>(b) * Hkv + h) * p.capacity + pos) * D + d0;
-        *reinterpret_cast<uint2*>(p.keys + slot) = kw;
-        *reinterpret_cast<uint2*>(p.values + slot) = vw;
-      }
-      asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
-      start_pair_staged<D>(acc, q_s, G, lane);
-    } else {
-      start_pair<D>(acc, p, b, h, lane);
-    }
-  } else {
-    start_pair<D>(acc, p, b, h, lane);
-  }
+  start_pair<D>(acc, p, b, h, lane);
   bool aborted = false;
   for (int k = 0; k < count; ++k) {
     const int s = k % NS;
@@ -819,22 +730,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       break;
     }
     uint8_t* kt = stages + s * S::kStageBytes;
-    if constexpr (D == 128) {
-      if (p.rope && t0 + k == n - 1) {
-        // The landed tile's copy of the newest slot predates this step: the warp that owns that
-        // row (tokens warp*16 .. warp*16+15 of the tile) overwrites it with the fresh K and V
-        // rows before reading it (lanes 0-15: K, 16-31: V; 16 bytes each, 128-byte swizzle).
-        const int r = static_cast<int>(pos - static_cast<long long>(n - 1) * kTile);
-        if (warp == r / 16) {
-          const int which = lane >> 4, c16 = lane & 15;
-          const int bx = c16 >> 3, ch = c16 & 7;
-          uint8_t* tile = kt + which * S::kTileBytes;
-          *reinterpret_cast<uint4*>(tile + bx * kTile * 128 + sw128(r, ch)) =
-              *reinterpret_cast<const uint4*>(kv_new + which * D + c16 * 8);
-          __syncwarp();
-        }
-      }
-    }
     attend_tile<D>(acc, kt, kt + S::kTileBytes, (t0 + k) * kTile, len, warp, lane, p.scale_log2);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
@@ -1103,13 +998,6 @@ static int make_params(Params* p, const void* q, const int64_t* position, int pe
   p->ctas = ctas;
   p->scale_log2 = static_cast<float>(static_cast<double>(scale) * 1.4426950408889634);
   p->err = error_word();
-  p->rope = 0;
-  p->packed = nullptr;
-  p->psplits = 0;
-  p->q_gain = p->k_gain = nullptr;
-  p->q_eps = p->k_eps = 0.f;
-  p->cos = p->sin = nullptr;
-  p->keys = p->values = nullptr;
   return FB_OK;
 }
 
@@ -1146,55 +1034,6 @@ extern "C" int fb_decode_attention(const void* q, const void* k, const void* v,
                                    void* stream) {
   return launch_decode(q, k, v, position, per_row, out, workspace, workspace_bytes, batch, q_heads,
                        kv_heads, head_dim, capacity, scale, ctas, stream, true);
-}
-
-extern "C" int fb_qk_rope_decode_attention(const void* packed, int packed_splits, const void* q_weight,
-                                           const void* k_weight, float q_eps, float k_eps, const void* cos,
-                                           const void* sin, const int64_t* position, void* keys, void* values,
-                                           void* out, int batch, int q_heads, int kv_heads, int head_dim,
-                                           int capacity, float scale, void* stream) {
-  if (!packed || !q_weight || !k_weight || !cos || !sin || !position || !keys || !values || !out)
-    return FB_ERR_ARG;
-  if (packed_splits < 0) return FB_ERR_ARG;
-  int st = validate(batch, q_heads, kv_heads, head_dim, capacity);
-  if (st != FB_OK) return st;
-  const int pairs = batch * kv_heads;
-  // the fused form is the cluster form only: D = 128 and clusters for every pair in one wave
-  if (head_dim != 128 || 2 * pairs > sm_count()) return FB_ERR_SHAPE;
-  Params p;
-  p.q = nullptr;
-  p.position = position;
-  p.per_row = 0;
-  p.out = static_cast<__nv_bfloat16*>(out);
-  p.acc = nullptr;
-  p.stats = nullptr;
-  p.counters = nullptr;
-  p.batch = batch;
-  p.q_heads = q_heads;
-  p.kv_heads = kv_heads;
-  p.groups = q_heads / kv_heads;
-  p.capacity = capacity;
-  p.ctas = 0;
-  p.scale_log2 = static_cast<float>(static_cast<double>(scale) * 1.4426950408889634);
-  p.err = error_word();
-  p.rope = 1;
-  p.packed = packed;
-  p.psplits = packed_splits;
-  p.q_gain = static_cast<const __nv_bfloat16*>(q_weight);
-  p.k_gain = static_cast<const __nv_bfloat16*>(k_weight);
-  p.q_eps = q_eps;
-  p.k_eps = k_eps;
-  p.cos = static_cast<const __nv_bfloat16*>(cos);
-  p.sin = static_cast<const __nv_bfloat16*>(sin);
-  p.keys = static_cast<__nv_bfloat16*>(keys);
-  p.values = static_cast<__nv_bfloat16*>(values);
-  const uint64_t rows = static_cast<uint64_t>(batch) * kv_heads * capacity;
-  CUtensorMap km, vm;
-  st = encode_bf16_2d(&km, keys, rows, head_dim, head_dim, 64, kTile, true);
-  if (st != FB_OK) return st;
-  st = encode_bf16_2d(&vm, values, rows, head_dim, head_dim, 64, kTile, true);
-  if (st != FB_OK) return st;
-  return launch_cluster_form<128>(km, vm, p, pairs, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int fb_decode_attention_partials(const void* q, const void* k, const void* v,

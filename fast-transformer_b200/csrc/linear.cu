@@ -14,16 +14,12 @@
 //    before griddepcontrol.wait, so the stream overlaps the previous kernel's tail; nothing an
 //    earlier kernel wrote is read before the wait.
 //  * Epilogues: fp32 split partials [S, M, N]; or a finished tile - bf16, fp32, SwiGLU on
-//    weights packed as 64-row gate/up blocks, (tensor parallelism) the fp32 tile pushed into
-//    every peer's receive buffer over NVLink as flagged words, or per-row argmax candidates.
-//  * Finished tiles with S > 1 (S <= 16): split fix-up. Every split CTA stores its fp32
-//    partial tile into a library-owned device array and counts itself in the tile's arrival
-//    counter; the CTA that arrives last sums the S partials in split order (the bits a split
-//    consumer produces), resets the counter and runs the epilogue. No cluster co-scheduling
-//    and no second launch. Shapes too large for the array fall back to a (1, S) thread-block
-//    cluster (S <= 8) whose CTAs sum the partials through distributed shared memory.
+//    weights packed as 64-row gate/up blocks, or per-row argmax candidates.
+//  * Finished tiles with S > 1 (S <= 8) run as a (1, S) thread-block cluster whose CTAs sum
+//    the S partials through distributed shared memory, in split order (the bits a split
+//    consumer produces). The decode step itself hands split partials to consumer kernels,
+//    which measured faster inside the captured step than any in-launch split sum.
 #include "common.cuh"
-#include "rope_math.cuh"
 
 namespace fb {
 namespace lin {
@@ -33,50 +29,15 @@ constexpr int kTileK = 64;
 constexpr int kConsumerWarps = 4;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kStages = 6;
-constexpr int kMaxPeers = 8;
 constexpr int kMaxTiles = 65535;       // grid x
 constexpr int kMaxClusterSplits = 8;  // portable cluster size: K-splits of one finished tile
-constexpr int kMaxFixupSplits = 16;   // K-splits of one finished tile summed by the fix-up
 
-// Split fix-up storage: partial tiles [tile][split][m][128] fp32 and one arrival counter per
-// tile (zero between launches: the last CTA of a tile resets its counter). Launches on one
-// stream never overlap here (each waits for its predecessor before touching them); concurrent
-// launches on different streams of one device would share them and must not both use the
-// fix-up.
-constexpr size_t kFixupFloats = size_t(4) << 20;  // 16 MiB
-constexpr int kFixupTiles = 4096;
-static __device__ __align__(16) float g_fixup_tiles[kFixupFloats];
-static __device__ int g_fixup_count[kFixupTiles];
-
-__host__ __device__ inline bool fixup_fits(int m, int n, int splits) {
-  const long long tiles = (n + kTileN - 1) / kTileN;
-  return splits > 1 && splits <= kMaxFixupSplits && tiles <= kFixupTiles &&
-         tiles * splits * m * kTileN <= static_cast<long long>(kFixupFloats);
-}
-
-enum Epilogue : int { kBf16 = 0, kFp32 = 1, kSwiGLU = 2, kSplits = 3, kPush = 4, kArgmax = 5, kQkRope = 6 };
+enum Epilogue : int { kBf16 = 0, kFp32 = 1, kSwiGLU = 2, kSplits = 3, kArgmax = 4 };
 
 struct Params {
   void* out;
   int m, n, k, splits, epilogue;
-  int fixup;  // finished tile with S > 1: split fix-up (1) or cluster reduction (0)
-  // kPush: every value of the tile as a flagged word into recv[use][rank][m][n] of every peer
-  int world, rank, use;
   long long index_base;  // kArgmax: vocabulary index of column 0
-  uint64_t* peer_recv[kMaxPeers];
-  uint64_t* mc_recv;     // multicast address of the receive buffers (NVSwitch), or null
-  const int64_t* epoch;  // the word's flag is (uint32)(*epoch) + 1
-  // kQkRope: tile h of the packed qkv projection is head h (D = 128 = the tile width)
-  const __nv_bfloat16* q_gain;
-  const __nv_bfloat16* k_gain;
-  float q_eps, k_eps;
-  const __nv_bfloat16* cos;  // whole RoPE tables [rows >= capacity, D]
-  const __nv_bfloat16* sin;
-  const int64_t* position;   // one shared decode position
-  __nv_bfloat16* query;      // [M, Hq, D]
-  __nv_bfloat16* keys;       // cache [M, Hkv, capacity, D]
-  __nv_bfloat16* values;
-  int q_heads, kv_heads, capacity;
   unsigned* err;
 };
 
@@ -145,49 +106,6 @@ __device__ void epilogue(const Params& p, const float* vals, int tile, int tid, 
     }
     return;
   }
-  if (p.epilogue == kQkRope) {
-    // Decode rows (one token each, shared position): head `tile` of every row, its K splits
-    // already summed in split order, rounded to bf16 as the packed projection would store it;
-    // q heads normalized + rotated into `query`, k heads normalized + rotated and v heads copied
-    // into the cache slot at the position (the stand-alone qk_rope kernel's arithmetic).
-    constexpr int E = kTileN / 32;
-    const int warp = tid >> 5, lane = tid & 31, d0 = lane * E;
-    const int head = tile;
-    const bool is_q = head < p.q_heads, is_k = !is_q && head < p.q_heads + p.kv_heads;
-    const long long pos = *p.position;
-    if (pos < 0 || pos >= p.capacity) {
-      if (tid == 0) raise_error(p.err, kErrBadShape);
-      return;
-    }
-    float gw[E];
-    if (is_q || is_k) rope::load_bf16<E>((is_q ? p.q_gain : p.k_gain) + d0, gw);
-    const int kvh = is_q ? 0 : (is_k ? head - p.q_heads : head - p.q_heads - p.kv_heads);
-    for (int m = warp; m < p.m; m += kConsumerWarps) {
-      float x[E];
-      const float4 v4 = *reinterpret_cast<const float4*>(vals + m * kTileN + d0);
-      x[0] = bf16_round(v4.x);
-      x[1] = bf16_round(v4.y);
-      x[2] = bf16_round(v4.z);
-      x[3] = bf16_round(v4.w);
-      __nv_bfloat16 out[E];
-      if (is_q || is_k) {
-        rope::norm_rope<kTileN>(x, gw, is_q ? p.q_eps : p.k_eps, p.cos + pos * kTileN + d0,
-                                p.sin + pos * kTileN + d0, lane, out);
-      } else {
-#pragma unroll
-        for (int e = 0; e < E; ++e) out[e] = __float2bfloat16_rn(x[e]);
-      }
-      __nv_bfloat16* dst =
-          is_q ? p.query + (static_cast<size_t>(m) * p.q_heads + head) * kTileN + d0
-               : (is_k ? p.keys : p.values) +
-                     ((static_cast<size_t>(m) * p.kv_heads + kvh) * p.capacity + pos) * kTileN + d0;
-      uint2 w;
-      w.x = pack_bf16x2(__bfloat162float(out[0]), __bfloat162float(out[1]));  // exact: already bf16
-      w.y = pack_bf16x2(__bfloat162float(out[2]), __bfloat162float(out[3]));
-      *reinterpret_cast<uint2*>(dst) = w;
-    }
-    return;
-  }
   if (p.epilogue == kSwiGLU) {
     // Tile rows [0, 64) are gate features f0..f0+63 and rows [64, 128) the up features of the
     // same f: out[m][f] = bf16(bf16(silu(bf16(g))) * bf16(u)).
@@ -200,32 +118,6 @@ __device__ void epilogue(const Params& p, const float* vals, int tile, int tid, 
       const float u = bf16_round(vals[m * kTileN + 64 + j]);
       static_cast<__nv_bfloat16*>(p.out)[static_cast<size_t>(m) * width + f0 + j] =
           __float2bfloat16_rn(silu_bf16(g) * u);
-    }
-    return;
-  }
-  if (p.epilogue == kPush) {
-    // Low-latency push: each fp32 value travels with its flag in one 8-byte word (stored
-    // whole), so a reader that sees the flag sees the value; no fence or counter is needed.
-    // Two values per thread: consecutive lanes store consecutive 16-byte pairs of flagged
-    // words, so a warp's store instruction writes 512 contiguous bytes to each peer.
-    const uint64_t flag = static_cast<uint64_t>(static_cast<uint32_t>(*p.epoch) + 1u) << 32;
-    const size_t slab = static_cast<size_t>(p.m) * p.n;
-    for (int e = tid; e < p.m * (kTileN / 2); e += kConsumerWarps * 32) {
-      const int m = e / (kTileN / 2), c2 = e % (kTileN / 2);
-      if (n0 + c2 * 2 >= p.n || !owned(c2 >> 1, kPush, r, S)) continue;
-      const float2 v = *reinterpret_cast<const float2*>(vals + m * kTileN + c2 * 2);
-      const size_t off = (static_cast<size_t>(p.use) * p.world + p.rank) * slab + static_cast<size_t>(m) * p.n +
-                         n0 + c2 * 2;
-      const uint64_t w0 = flag | __float_as_uint(v.x), w1 = flag | __float_as_uint(v.y);
-      if (p.mc_recv != nullptr) {
-        // one store per word through the multicast address: NVSwitch delivers it to every rank
-        asm volatile("multimem.st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p.mc_recv + off), "l"(w0) : "memory");
-        asm volatile("multimem.st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p.mc_recv + off + 1), "l"(w1) : "memory");
-      } else {
-        for (int q = 0; q < p.world; ++q)
-          asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p.peer_recv[q] + off), "l"(w0), "l"(w1)
-                       : "memory");
-      }
     }
     return;
   }
@@ -246,61 +138,6 @@ __device__ void epilogue(const Params& p, const float* vals, int tile, int tid, 
   (void)MP;
 }
 
-// Split fix-up of a finished tile whose fp32 partial this CTA holds in vals[m][128]: store it,
-// count this CTA in, and if it arrived last, sum all S partials in split order into vals and
-// reset the counter. Returns whether this CTA is the last (it then runs the epilogue). An
-// aborted CTA stores nothing but still counts, so the counter always returns to zero.
-__device__ bool fixup_reduce(const Params& p, float* vals, int tile, int split, int tid, volatile int* last,
-                             bool aborted) {
-  constexpr int kT = kConsumerWarps * 32;
-  const int S = p.splits;
-  const int words = p.m * (kTileN / 4);  // float4s of the tile's valid rows
-  float4* tiles = reinterpret_cast<float4*>(g_fixup_tiles) + static_cast<size_t>(tile) * S * words;
-  if (!aborted)
-    for (int e = tid; e < words; e += kT) __stcg(tiles + static_cast<size_t>(split) * words + e,
-                                                 reinterpret_cast<const float4*>(vals)[e]);
-  // The barrier orders every thread's stores before thread 0's GPU-scope fence (cumulative),
-  // which orders them before its arrival; the last arrival's fence orders the other CTAs'
-  // partials before the loads that follow the second barrier.
-  asm volatile("bar.sync 1, %0;" ::"r"(kT) : "memory");
-  if (tid == 0) {
-    int before;
-    asm volatile("fence.acq_rel.gpu;\n\tatom.relaxed.gpu.global.add.s32 %0, [%1], 1;"
-                 : "=r"(before) : "l"(&g_fixup_count[tile]) : "memory");
-    const bool is_last = before == S - 1;
-    if (is_last) asm volatile("fence.acq_rel.gpu;" ::: "memory");
-    *last = is_last;
-  }
-  asm volatile("bar.sync 1, %0;" ::"r"(kT) : "memory");
-  if (!*last) return false;
-  for (int e = tid; e < words; e += kT) {
-    // eight partial loads in flight, then their adds in split order
-    float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int q0 = 0; q0 < S; q0 += 8) {
-      float4 parts[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        if (q0 + j < S) parts[j] = __ldcg(tiles + static_cast<size_t>(q0 + j) * words + e);
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        if (q0 + j < S) {
-          if (q0 + j == 0) {
-            sum = parts[0];
-          } else {
-            sum.x += parts[j].x;
-            sum.y += parts[j].y;
-            sum.z += parts[j].z;
-            sum.w += parts[j].w;
-          }
-        }
-    }
-    reinterpret_cast<float4*>(vals)[e] = sum;
-  }
-  if (tid == 0) g_fixup_count[tile] = 0;
-  asm volatile("bar.sync 1, %0;" ::"r"(kT) : "memory");
-  return true;
-}
-
 template <int MT>
 __global__ void __launch_bounds__(kThreads)
     linear_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
@@ -312,7 +149,7 @@ __global__ void __launch_bounds__(kThreads)
   float* vals = reinterpret_cast<float*>(base);  // reused once the ring has drained
   uint64_t* full = reinterpret_cast<uint64_t*>(base + kStages * S::kStageBytes);
   uint64_t* empty = full + kStages;
-  volatile int* flags = reinterpret_cast<volatile int*>(empty + kStages);  // [0] abort, [1] last
+  volatile int* flags = reinterpret_cast<volatile int*>(empty + kStages);  // [0] abort
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x, split = blockIdx.y;
@@ -322,8 +159,7 @@ __global__ void __launch_bounds__(kThreads)
   const int c1 = static_cast<int>((static_cast<long long>(chunks) * (split + 1)) / p.splits);
   const int count = c1 - c0;
   // finished-tile epilogues reduce the K-splits of a tile across its cluster (dims 1 x S)
-  const bool clustered = p.epilogue != kSplits && p.splits > 1 && !p.fixup;
-  const bool fixup = p.epilogue != kSplits && p.splits > 1 && p.fixup;
+  const bool clustered = p.epilogue != kSplits && p.splits > 1;
 
   if (warp == kConsumerWarps && lane == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -417,7 +253,7 @@ __global__ void __launch_bounds__(kThreads)
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
   }
-  if (aborted && !clustered && !fixup) return;
+  if (aborted && !clustered) return;
 
   if (p.epilogue == kSplits) {
     // fp32 partials [S, M, N]: C fragment rows (g, g+8), columns (2c, 2c+1) of each 16x8 tile
@@ -450,7 +286,6 @@ __global__ void __launch_bounds__(kThreads)
     }
   if (!clustered) {
     asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
-    if (fixup && !fixup_reduce(p, vals, tile, split, tid, &flags[1], aborted)) return;
     epilogue<MT>(p, vals, tile, tid, 0, 1);
     return;
   }
@@ -509,7 +344,7 @@ int launch(const CUtensorMap& xm, const CUtensorMap& wm, const Params& p, cudaSt
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (p.epilogue != kSplits && p.splits > 1 && !p.fixup) {
+  if (p.epilogue != kSplits && p.splits > 1) {
     attr[1].id = cudaLaunchAttributeClusterDimension;
     attr[1].val.clusterDim.x = 1;
     attr[1].val.clusterDim.y = p.splits;
@@ -548,26 +383,21 @@ extern "C" int fb_linear_splits(int m, int n, int k) {
 }
 
 extern "C" int fb_linear_finished_splits(int m, int n, int k) {
-  // fb_linear_splits capped by how a finished tile's splits are summed: the split fix-up
-  // (up to 16) when its storage holds the shape, else one thread-block cluster (up to 8).
+  // fb_linear_splits capped by the thread-block cluster that sums a finished tile's splits
   const int s = fb_linear_splits(m, n, k);
   if (s <= 1) return 1;
-  const int fix = s < lin::kMaxFixupSplits ? s : lin::kMaxFixupSplits;
-  if (m > 0 && m <= 64 && lin::fixup_fits(m, n, fix)) return fix;
   return s < lin::kMaxClusterSplits ? s : lin::kMaxClusterSplits;
 }
 
 static int linear_impl(const void* x, const void* w, void* out, int m, int n, int k, int epilogue, int splits,
-                       void* stream, int world, int rank, int use, void* const* peer_recv,
-                       const int64_t* epoch, int64_t index_base = 0, void* multicast_recv = nullptr) {
+                       void* stream, int64_t index_base = 0) {
   if (!x || !w || !out || m <= 0 || n <= 0 || k <= 0 || splits <= 0) return FB_ERR_ARG;
   if (m > 64 || k % 8 != 0 || n % 8 != 0) return FB_ERR_SHAPE;
   if ((n + lin::kTileN - 1) / lin::kTileN > lin::kMaxTiles) return FB_ERR_SHAPE;
   if (epilogue == lin::kSwiGLU && n % lin::kTileN != 0) return FB_ERR_SHAPE;
   if (epilogue == lin::kArgmax && splits != 1) return FB_ERR_SHAPE;
   if (splits > (k + lin::kTileK - 1) / lin::kTileK || splits > 65535) return FB_ERR_SHAPE;
-  const bool fixup = epilogue != lin::kSplits && lin::fixup_fits(m, n, splits);
-  if (epilogue != lin::kSplits && splits > lin::kMaxClusterSplits && !fixup) return FB_ERR_SHAPE;
+  if (epilogue != lin::kSplits && splits > lin::kMaxClusterSplits) return FB_ERR_SHAPE;
   const int mt = lin::row_tiles(m);
   CUtensorMap xm, wm;
   int st = encode_bf16_2d(&xm, x, m, k, k, 64, mt * 16, true);
@@ -581,16 +411,7 @@ static int linear_impl(const void* x, const void* w, void* out, int m, int n, in
   p.k = k;
   p.splits = splits;
   p.epilogue = epilogue;
-  p.fixup = fixup ? 1 : 0;
-  p.world = world;
-  p.rank = rank;
-  p.use = use;
   p.index_base = index_base;
-  if (epilogue == lin::kPush) {  // only the push form has peer buffers
-    for (int r = 0; r < world && r < lin::kMaxPeers; ++r) p.peer_recv[r] = static_cast<uint64_t*>(peer_recv[r]);
-    p.mc_recv = static_cast<uint64_t*>(multicast_recv);
-    p.epoch = epoch;
-  }
   p.err = error_word();
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (mt == 1) return lin::launch<1>(xm, wm, p, s);
@@ -601,52 +422,7 @@ static int linear_impl(const void* x, const void* w, void* out, int m, int n, in
 extern "C" int fb_linear(const void* x, const void* w, void* out, int m, int n, int k, int epilogue, int splits,
                          void* stream) {
   if (epilogue < lin::kBf16 || epilogue > lin::kSplits) return FB_ERR_ARG;
-  return linear_impl(x, w, out, m, n, k, epilogue, splits, stream, 1, 0, 0, nullptr, nullptr);
-}
-
-extern "C" int fb_linear_qk_rope(const void* x, const void* w, int m, int n, int k, int splits, const void* q_weight,
-                                 const void* k_weight, float q_eps, float k_eps, const void* cos, const void* sin,
-                                 const int64_t* position, void* query, void* keys, void* values, int q_heads,
-                                 int kv_heads, int head_dim, int capacity, void* stream) {
-  if (!x || !w || !q_weight || !k_weight || !cos || !sin || !position || !query || !keys || !values)
-    return FB_ERR_ARG;
-  if (q_heads <= 0 || kv_heads <= 0 || capacity <= 0 || splits <= 0) return FB_ERR_ARG;
-  if (head_dim != lin::kTileN || n != (q_heads + 2 * kv_heads) * head_dim) return FB_ERR_SHAPE;
-  if (splits > 1 && !lin::fixup_fits(m, n, splits)) return FB_ERR_SHAPE;  // needs whole heads per tile
-  if (m > 64 || k % 8 != 0 || splits > (k + lin::kTileK - 1) / lin::kTileK) return FB_ERR_SHAPE;
-  const int mt = lin::row_tiles(m);
-  CUtensorMap xm, wm;
-  int st = encode_bf16_2d(&xm, x, m, k, k, 64, mt * 16, true);
-  if (st != FB_OK) return st;
-  st = encode_bf16_2d(&wm, w, n, k, k, 64, lin::kTileN, true);
-  if (st != FB_OK) return st;
-  lin::Params p{};
-  p.out = query;
-  p.m = m;
-  p.n = n;
-  p.k = k;
-  p.splits = splits;
-  p.epilogue = lin::kQkRope;
-  p.fixup = splits > 1 ? 1 : 0;
-  p.world = 1;
-  p.q_gain = static_cast<const __nv_bfloat16*>(q_weight);
-  p.k_gain = static_cast<const __nv_bfloat16*>(k_weight);
-  p.q_eps = q_eps;
-  p.k_eps = k_eps;
-  p.cos = static_cast<const __nv_bfloat16*>(cos);
-  p.sin = static_cast<const __nv_bfloat16*>(sin);
-  p.position = position;
-  p.query = static_cast<__nv_bfloat16*>(query);
-  p.keys = static_cast<__nv_bfloat16*>(keys);
-  p.values = static_cast<__nv_bfloat16*>(values);
-  p.q_heads = q_heads;
-  p.kv_heads = kv_heads;
-  p.capacity = capacity;
-  p.err = error_word();
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (mt == 1) return lin::launch<1>(xm, wm, p, s);
-  if (mt == 2) return lin::launch<2>(xm, wm, p, s);
-  return lin::launch<4>(xm, wm, p, s);
+  return linear_impl(x, w, out, m, n, k, epilogue, splits, stream);
 }
 
 extern "C" size_t fb_argmax_candidates_bytes(int m, int n) {
@@ -657,18 +433,5 @@ extern "C" size_t fb_argmax_candidates_bytes(int m, int n) {
 extern "C" int fb_linear_argmax(const void* x, const void* w, int m, int n, int k, int64_t index_base, void* cand,
                                 void* stream) {
   if (!cand || index_base < 0 || index_base + n > 0x7ffffffe) return FB_ERR_ARG;
-  return linear_impl(x, w, cand, m, n, k, lin::kArgmax, 1, stream, 1, 0, 0, nullptr, nullptr, index_base);
-}
-
-extern "C" int fb_linear_allreduce_push(const void* x, const void* w, int m, int n, int k, int splits, int world,
-                                        int rank, int use, void* const* peer_recv, void* multicast_recv,
-                                        const int64_t* epoch, void* stream) {
-  if (world < 1 || world > lin::kMaxPeers || rank < 0 || rank >= world || use < 0) return FB_ERR_ARG;
-  if (!peer_recv || !epoch) return FB_ERR_ARG;
-  for (int r = 0; r < world; ++r)
-    if (!peer_recv[r] || (reinterpret_cast<uintptr_t>(peer_recv[r]) & 15u)) return FB_ERR_ARG;
-  // the kernel writes nothing through `out` in this mode; pass a valid dummy
-  if (multicast_recv != nullptr && (reinterpret_cast<uintptr_t>(multicast_recv) & 15u)) return FB_ERR_ARG;
-  return linear_impl(x, w, const_cast<void*>(x), m, n, k, lin::kPush, splits, stream, world, rank, use, peer_recv,
-                     epoch, 0, multicast_recv);
+  return linear_impl(x, w, cand, m, n, k, lin::kArgmax, 1, stream, index_base);
 }

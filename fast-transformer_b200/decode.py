@@ -10,13 +10,14 @@ eagerly: cuBLAS for the big GEMMs (as the reference's prefill does, engine/layer
 the tcgen05 causal flash kernel (fb_prefill_attention) for the prompt attention, and the
 fused kernel writing the cache.
 
-Tensor parallelism (by KV head, see qwen3.py): o_proj and down_proj run as
-fb_linear_allreduce_push, which stores every finished fp32 output value straight into each
-rank's receive buffer (torch symmetric memory, NVLink peer stores) as an 8-byte word carrying
-a flag (the decode position + 1); fb_allreduce_add_rmsnorm polls the flags, sums the ranks'
-slabs in rank order and applies the residual add + RMSNorm. No fence, counter or barrier
-sits on the step's path. Every rank therefore runs the same norms, LM head and argmax on
-bit-identical data. Prefill (eager, untimed) uses NCCL all-reduces.
+Tensor parallelism (by KV head, see qwen3.py): o_proj and down_proj write fp32 split-K
+partials; fb_reduce_scatter_push sums them in split order and stores each value, as an 8-byte
+word carrying a flag (the decode position + 1), into the receive buffer of the rank that owns
+its column slice (torch symmetric memory, NVLink peer stores); fb_allreduce_add_rmsnorm has
+every owner sum its slice over the ranks in rank order, add the residual and send the summed
+bf16 pairs and its slice's sums of squares to every rank, which then normalizes whole rows. No
+fence, counter or barrier sits on the step's path. Every rank therefore runs the same norms, LM
+head and argmax on bit-identical data. Prefill (eager, untimed) uses NCCL all-reduces.
 """
 
 import ctypes
@@ -88,28 +89,30 @@ class Communicator:
 
 
 class PeerBuffers:
-    """Receive slabs in torch symmetric memory, uint64 words [uses, world, rows, width] (fp32
-    bits + a 32-bit flag per value: the low-latency push protocol), with every rank's base
-    address for NVLink peer stores and, where the driver binds the buffers to an NVSwitch
-    multicast object, its multicast address (one store reaches every rank).
-
-    Plain peer mappings (no multicast object) by default; FB_TP_MULTICAST=1 asks for the
-    multicast object and its address. Measured on B200 (Qwen3-8B, B=16, one multimem.st per
-    flagged 8-byte word, otherwise identical code): TP2 4164 tok/s against 4156 with peer
-    stores, TP4 4324 against 5817, TP8 3351 against 6406. Peer mappings are also the safe
-    choice for runs that may lose a rank: a rank that dies while bound to a multicast object
-    can fault its peers."""
+    """The tensor-parallel all-reduce's receive regions in torch symmetric memory (plain NVLink
+    peer mappings, never bound to an NVSwitch multicast object: a rank that dies while bound to
+    one can fault its peers), uint64 words carrying a 32-bit flag each:
+      rs [uses, world, rows, width/world]  fp32 partials this rank receives as a slice owner
+      ag [uses, rows, width/2]             summed bf16 pairs of whole rows
+      ss [uses, world, rows]               each owner's sum of squares of its slice of a row
+      exchange [rows, world, 2]            the vocabulary-parallel argmax's bests
+    with every rank's base address of each region."""
 
     def __init__(self, comm, uses, rows, width, device):
-        import os
-        if os.environ.get("FB_TP_MULTICAST", "0") != "1":
-            os.environ["TORCH_SYMM_MEM_DISABLE_MULTICAST"] = "1"
+        os.environ["TORCH_SYMM_MEM_DISABLE_MULTICAST"] = "1"
         import torch.distributed._symmetric_memory as symm_mem
         world = comm.size
         self.uses, self.world, self.rows, self.width = uses, world, rows, width
-        self.recv_bytes = uses * world * rows * width * 8
-        # argmax exchange slots after the slabs: uint64 [rows, world, 2]
-        total = self.recv_bytes + rows * world * 2 * 8
+
+        def pad(nbytes):
+            return (nbytes + 255) // 256 * 256
+
+        sizes = {"rs": pad(uses * rows * width * 8), "ag": pad(uses * rows * (width // 2) * 8),
+                 "ss": pad(uses * world * rows * 8), "exchange": pad(rows * world * 2 * 8)}
+        offsets, total = {}, 0
+        for name, size in sizes.items():
+            offsets[name] = total
+            total += size
         self.group = comm.group if comm.group is not None else torch.distributed.group.WORLD
         if hasattr(symm_mem, "enable_symm_mem_for_group"):
             try:
@@ -119,18 +122,15 @@ class PeerBuffers:
         self.buf = symm_mem.empty(total, dtype=torch.uint8, device=device)
         handle = symm_mem.rendezvous(self.buf, self.group)
         self.handle = handle
-        # a multicast object shows as a non-zero multicast address
-        mc = int(getattr(handle, "multicast_ptr", 0) or 0)
-        self.multicast = mc != 0
-        self.mc_ptr = ctypes.c_void_p(mc) if mc else None
-        self.recv_ptrs = (ctypes.c_void_p * world)(*[int(b) for b in handle.buffer_ptrs])
-        self.recv_local = ctypes.c_void_p(self.buf.data_ptr())
-        self.exchange_ptrs = (ctypes.c_void_p * world)(*[int(b) + self.recv_bytes for b in handle.buffer_ptrs])
-        self.exchange_local = ctypes.c_void_p(self.buf.data_ptr() + self.recv_bytes)
+        bases = [int(b) for b in handle.buffer_ptrs]
+        local = self.buf.data_ptr()
+        for name, offset in offsets.items():
+            setattr(self, f"{name}_ptrs", (ctypes.c_void_p * world)(*[b + offset for b in bases]))
+            setattr(self, f"{name}_local", ctypes.c_void_p(local + offset))
         self.reset()
 
     def reset(self):
-        """Zero every slab with all ranks idle (before first use and whenever the epoch, the
+        """Zero every region with all ranks idle (before first use and whenever the epoch, the
         decode position, may repeat a value: a new generation), then meet the other ranks so
         no push of the next step can land before the zeroing."""
         self.buf.zero_()
@@ -154,64 +154,19 @@ def _qk_rope_decode(packed, layer, eps, cos, sin, position, keys, values, q_head
 
 
 def _qkv_rope_decode(x, layer, eps, cos, sin, position, keys, values, q_heads):
-    """qkv projection + QK-norm + RoPE + KV append for one decode token per row: one
-    fb_linear_qk_rope launch when the head dim is 128 (the projection's epilogue), else the
-    projection's split partials + fb_qk_norm_rope_append (the same bits)."""
-    batch, kv_heads, capacity, dim = keys.shape
-    rows = x.numel() // x.shape[-1]
-    n, k = layer.qkv.shape
-    if dim != 128 or not klinear.supported(rows, layer.qkv) or not FINISH_SPLITS_IN_PROJECTION:
-        return _qk_rope_decode(linear(x, layer.qkv, split_ok=True), layer, eps, cos, sin, position, keys, values,
-                               q_heads)
-    flat = x.reshape(rows, k).contiguous()
-    splits = klinear.splits_for(rows, n, k, x.device, finished=True)
-    query = torch.empty((batch, 1, q_heads, dim), device=keys.device, dtype=BF16)
-    status = lib.fb_linear_qk_rope(ptr(flat), ptr(layer.qkv), rows, n, k, splits, ptr(layer.q_norm),
-                                   ptr(layer.k_norm), float(eps), float(eps), ptr(cos), ptr(sin), ptr(position),
-                                   ptr(query), ptr(keys), ptr(values), q_heads, kv_heads, dim, capacity, stream())
-    if status == _native.FB_ERR_SHAPE:  # split heads beyond the fix-up storage: nothing launched
-        return _qk_rope_decode(linear(x, layer.qkv, split_ok=True), layer, eps, cos, sin, position, keys, values,
-                               q_heads)
-    check(status, "fb_linear_qk_rope")
-    return query.view(batch, q_heads, 1, dim)
+    """qkv projection (split partials when it has K splits) + QK-norm + RoPE + KV append for one
+    decode token per row."""
+    return _qk_rope_decode(linear(x, layer.qkv, split_ok=True), layer, eps, cos, sin, position, keys, values,
+                           q_heads)
 
 
-#: How a K-split projection whose result feeds a fixed follow-up is finished on the decode
-#: path: by split partials and a consumer kernel (fb_qk_norm_rope_append, fb_swiglu_blocked,
-#: fb_reduce_push; the default), or in the projection's own launch (split fix-up:
-#: fb_linear_qk_rope, the SwiGLU epilogue, the push epilogue). Both give the same bits. On B200
-#: the consumer form measured faster at every shape (captured Qwen3-8B step, one rank's shard
-#: alone: TP1 6172 against 6295 us, TP8 1990 against 2350 us): the consumer runs while the
-#: next projection's CTAs already stream their weights, whereas the fix-up's last CTA per
-#: tile holds its SM until the tile is summed.
-FINISH_SPLITS_IN_PROJECTION = os.environ.get("FB_FINISH_SPLITS_IN_PROJECTION", "0") == "1"
-#: Run the QK-norm/RoPE/KV append inside the decode attention kernel where the attention takes
-#: its cluster form (fb_qk_rope_decode_attention; same bits, one launch fewer per layer). Off by
-#: default: measured slower on B200 (one TP8 rank's shard alone 2000 against 1954-1963 us per
-#: step; Qwen3-0.6B at batch 1 953 against 918 us): every CTA of a cluster sums the qkv split
-#: partials for its query heads on the attention's critical path, which costs more than the
-#: separate kernel's launch.
-FUSE_ROPE_INTO_ATTENTION = os.environ.get("FB_FUSE_ROPE_ATTENTION", "0") == "1"
-#: The split-consumer all-reduce: "reduce_push" (fb_reduce_push + fb_allreduce_add_rmsnorm,
-#: the default) or "fused" (fb_reduce_push_add_rmsnorm: push and consumer in one launch).
-#: Measured on 4 B200s (config 4, same box): reduce_push 5817 tok/s, fused 4914, the split
-#: fix-up push epilogue + consumer 4937 - pushing from the kernel that then polls, or from
-#: the projection's last CTA per tile, costs ~7 us per all-reduce more than a separate
-#: push kernel.
-ALLREDUCE_FORM = os.environ.get("FB_TP_ALLREDUCE", "reduce_push")
-
-
-def _allreduce_add_norm(x, weight, comm, peers, use, epoch, residual, gain, eps, split_consumer=None, splits=None):
-    """(normalized, summed) = add_rms_norm(all-reduce over ranks of x @ W^T, residual): every
-    rank pushes its fp32 partial into recv[use] of every rank, flagged with epoch + 1, and
-    polls its own recv[use] for all ranks' slabs. With K splits (the default,
-    ``split_consumer``) the projection writes split partials, then fb_reduce_push +
-    fb_allreduce_add_rmsnorm (ALLREDUCE_FORM "reduce_push") or fb_reduce_push_add_rmsnorm
-    ("fused"); at one split, or with the K splits summed by the split fix-up, the projection's
-    push epilogue (fb_linear_allreduce_push) + fb_allreduce_add_rmsnorm. The same bits in every
-    form. ``splits`` overrides the K-split count (tests)."""
-    if split_consumer is None:
-        split_consumer = not FINISH_SPLITS_IN_PROJECTION
+def _allreduce_add_norm(x, weight, comm, peers, use, epoch, residual, gain, eps, splits=None):
+    """(normalized, summed) = add_rms_norm(all-reduce over ranks of x @ W^T, residual): the
+    projection writes fp32 split partials, fb_reduce_scatter_push sums them in split order and
+    pushes each value, flagged with epoch + 1, to the rank owning its column slice, and
+    fb_allreduce_add_rmsnorm has every owner sum its slice over the ranks, add the residual and
+    share the summed slice with every rank, which normalizes whole rows. ``splits`` overrides
+    the K-split count (tests)."""
     rows = x.numel() // x.shape[-1]
     flat = x.reshape(rows, x.shape[-1]).contiguous()
     n, k = weight.shape
@@ -219,28 +174,13 @@ def _allreduce_add_norm(x, weight, comm, peers, use, epoch, residual, gain, eps,
     out = torch.empty_like(residual)
     summed = torch.empty_like(residual)
     if splits is None:
-        splits = klinear.splits_for(rows, n, k, x.device, finished=not split_consumer)
-    if splits > 1 and split_consumer and ALLREDUCE_FORM == "reduce_push":
-        partials = klinear.project(flat, weight, klinear.SPLITS_OUT, splits)
-        check(lib.fb_reduce_push(ptr(partials), splits, rows, n, comm.size, comm.rank, use, peers.recv_ptrs,
-                                 peers.mc_ptr, ptr(epoch), stream()), "fb_reduce_push")
-        check(lib.fb_allreduce_add_rmsnorm(peers.recv_local, use, peers.world, ptr(epoch), ptr(residual),
-                                           ptr(gain), ptr(out), ptr(summed), rows, width, float(eps), stream()),
-              "fb_allreduce_add_rmsnorm")
-        return out, summed
-    if splits > 1 and split_consumer:
-        partials = klinear.project(flat, weight, klinear.SPLITS_OUT, splits)
-        check(lib.fb_reduce_push_add_rmsnorm(ptr(partials), splits, peers.recv_ptrs, peers.mc_ptr, peers.recv_local,
-                                             use, peers.world, comm.rank, ptr(epoch), ptr(residual), ptr(gain),
-                                             ptr(out), ptr(summed), rows, width, float(eps), stream()),
-              "fb_reduce_push_add_rmsnorm")
-        return out, summed
-    check(lib.fb_linear_allreduce_push(ptr(flat), ptr(weight), rows, n, k, splits, comm.size, comm.rank, use,
-                                       peers.recv_ptrs, peers.mc_ptr, ptr(epoch), stream()),
-          "fb_linear_allreduce_push")
-    check(lib.fb_allreduce_add_rmsnorm(peers.recv_local, use, peers.world, ptr(epoch), ptr(residual), ptr(gain),
-                                       ptr(out), ptr(summed), rows, width, float(eps), stream()),
-          "fb_allreduce_add_rmsnorm")
+        splits = klinear.splits_for(rows, n, k, x.device)
+    partials = klinear.project(flat, weight, klinear.SPLITS_OUT, splits)
+    check(lib.fb_reduce_scatter_push(ptr(partials), splits, rows, n, comm.size, comm.rank, use, peers.rs_ptrs,
+                                     ptr(epoch), stream()), "fb_reduce_scatter_push")
+    check(lib.fb_allreduce_add_rmsnorm(peers.rs_local, peers.ag_local, peers.ss_local, peers.ag_ptrs, peers.ss_ptrs,
+                                       use, peers.world, comm.rank, ptr(epoch), ptr(residual), ptr(gain), ptr(out),
+                                       ptr(summed), rows, width, float(eps), stream()), "fb_allreduce_add_rmsnorm")
     return out, summed
 
 
@@ -278,30 +218,15 @@ class DecodeState:
 
     # ------------------------------------------------------------------ decode step
     def _rope_attention(self, normalized, layer, index):
-        """qkv projection, QK-norm + RoPE + KV append, decode attention for one layer. Where the
-        attention takes its cluster form (few (row, KV head) pairs: tensor-parallel shards,
-        small batches) the norm/RoPE/append runs inside the attention kernel
-        (fb_qk_rope_decode_attention: one launch fewer); otherwise fb_qk_norm_rope_append then
-        fb_decode_attention. The same bits either way."""
+        """qkv projection, QK-norm + RoPE + KV append (fb_qk_norm_rope_append), then decode
+        attention (fb_decode_attention) for one layer. Fusing the norm/RoPE/append into the
+        attention kernel's prologue measured slower on B200 (one TP8 rank's shard alone 2000
+        against 1954 us per step): every CTA of a pair's cluster summed the qkv split partials
+        of its query heads on the attention's critical path."""
         cache, w = self.cache, self.w
         keys, values = cache.keys[index], cache.values[index]
-        eps = self.cfg.rms_norm_eps
-        if FUSE_ROPE_INTO_ATTENTION and not FINISH_SPLITS_IN_PROJECTION:
-            packed = linear(normalized, layer.qkv, split_ok=True)
-            from kernels.merged import source
-            data, splits, _, _ = source(packed)
-            batch, kv_heads, capacity, dim = keys.shape
-            status = lib.fb_qk_rope_decode_attention(
-                ptr(data), splits if isinstance(packed, Split) else 0, ptr(layer.q_norm), ptr(layer.k_norm),
-                float(eps), float(eps), ptr(self.cos), ptr(self.sin), ptr(self.position), ptr(keys), ptr(values),
-                ptr(self.attn_out), batch, w.q_heads, kv_heads, dim, capacity, float(self.scale), stream())
-            if status != _native.FB_ERR_SHAPE:  # FB_ERR_SHAPE: not the cluster form, nothing launched
-                check(status, "fb_qk_rope_decode_attention")
-                return self.attn_out
-            query = _qk_rope_decode(packed, layer, eps, self.cos, self.sin, self.position, keys, values, w.q_heads)
-        else:
-            query = _qkv_rope_decode(normalized, layer, eps, self.cos, self.sin, self.position, keys, values,
-                                     w.q_heads)
+        query = _qkv_rope_decode(normalized, layer, self.cfg.rms_norm_eps, self.cos, self.sin, self.position, keys,
+                                 values, w.q_heads)
         return attend_decode(query, keys, values, self.position, self.scale, out=self.attn_out,
                              workspace=self.workspace, ctas=self.ctas)
 
@@ -329,7 +254,7 @@ class DecodeState:
             else:
                 normalized, residual = _allreduce_add_norm(attention, layer.o, comm, peers, 2 * index, self.position,
                                                            residual, layer.ln2, eps)
-            activated = swiglu_linear(normalized, layer.gate_up, split_consumer=not FINISH_SPLITS_IN_PROJECTION)
+            activated = swiglu_linear(normalized, layer.gate_up)
             if peers is None:
                 hidden = linear(activated, layer.down, split_ok=True)
             else:
@@ -356,8 +281,10 @@ class DecodeState:
         reading it."""
         current = torch.cuda.current_stream(self.device)
         side = torch.cuda.Stream(device=self.device)
-        side.wait_stream(current)
+        # the copies are enqueued on the current stream before the side stream starts waiting
+        # for it: the warm-up steps below run on the side stream and overwrite the originals
         saved_position, saved_tokens = self.position.clone(), self.token_ids.clone()
+        side.wait_stream(current)
         with torch.cuda.stream(side):
             for _ in range(warmup):
                 self.position.copy_(saved_position)

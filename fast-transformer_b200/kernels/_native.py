@@ -53,20 +53,12 @@ _SIGNATURES = {
     "fb_linear_splits": (_c_int, [_c_int, _c_int, _c_int]),
     "fb_linear_finished_splits": (_c_int, [_c_int, _c_int, _c_int]),
     "fb_decode_attention_cluster_shape": (_c_int, [_c_int, _c_int]),
-    "fb_qk_rope_decode_attention": (_c_int, [_vp, _c_int, _vp, _vp, _c_float, _c_float, _vp, _vp, _vp, _vp, _vp, _vp,
-                                             _c_int, _c_int, _c_int, _c_int, _c_int, _c_float, _vp]),
-    "fb_linear_qk_rope": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _c_float, _c_float, _vp, _vp,
-                                   _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp]),
     "fb_linear": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _vp]),
-    "fb_linear_allreduce_push": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _vp,
-                                          _vp, _vp]),
-    "fb_allreduce_add_rmsnorm": (_c_int, [_vp, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_float,
-                                          _vp]),
+    "fb_allreduce_add_rmsnorm": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp,
+                                          _c_int, _c_int, _c_float, _vp]),
     "fb_merge_splits": (_c_int, [_vp, _c_int, _c_i64, _vp, _c_int, _vp]),
     "fb_swiglu_blocked": (_c_int, [_vp, _c_int, _vp, _c_int, _c_int, _vp]),
-    "fb_reduce_push": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp, _vp]),
-    "fb_reduce_push_add_rmsnorm": (_c_int, [_vp, _c_int, _vp, _vp, _vp, _c_int, _c_int, _c_int, _vp, _vp, _vp, _vp,
-                                            _vp, _c_int, _c_int, _c_float, _vp]),
+    "fb_reduce_scatter_push": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp]),
     "fb_prefill_attention": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float,
                                       _vp]),
     "fb_spec_propose": (_c_int, [_vp, _c_i64, _vp, _vp, _c_i64, _c_int, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int,

@@ -4,10 +4,13 @@ Drop-in for engine/kernels/linear.py:489-523 ``linear(x, weight, split_ok)``: al
 accumulate in FP32 and round once to BF16. Decode-sized inputs (<= MAX_ROWS rows, aligned
 K/N) run the TMA + mma.sync kernel fb_linear over (N/128 tiles) x (K splits); with
 ``split_ok`` a split-K result comes back as a ``Split`` of FP32 partials for a consumer kernel
-to sum (merged.py), otherwise the last-arriving split CTA of each tile sums the tile's
-partials in split order and writes BF16 (the split fix-up, same launch). Larger
-row counts (prefill) stay on cuBLAS through ``F.linear``, exactly as the reference routes them
-(linear.py:492).
+to sum (merged.py), otherwise the split CTAs of each tile form a thread-block cluster that sums
+the tile's partials in split order and writes BF16 (same launch). Larger row counts (prefill)
+stay on cuBLAS through ``F.linear``, exactly as the reference routes them (linear.py:492).
+
+``keep_native`` is the reference's hook for leaving a shape on cuBLAS without tuning it
+(linear.py:484-486); the B200 kernels choose their launch shape by a fixed rule (no timed
+search), so it only records the request.
 """
 
 import torch
@@ -32,6 +35,17 @@ def splits_for(rows, n, k, device, finished=False):
         choose = lib.fb_linear_finished_splits if finished else lib.fb_linear_splits
         _SPLITS[key] = int(choose(rows, n, k))
     return _SPLITS[key]
+
+
+def keep_native(rows, weight):
+    """engine/kernels/linear.py:484-486: leave ``rows`` x ``weight`` on cuBLAS without spending
+    tuning time on it. The B200 projection has no timed search to skip, and the reference calls
+    this only for row counts above MAX_ROWS (its verify blocks), which ``linear`` already routes
+    to cuBLAS; the shape is recorded so ``linear`` keeps it there whatever its row count."""
+    _NATIVE.add((weight.device, rows, weight.shape[0], weight.shape[1]))
+
+
+_NATIVE = set()
 
 
 def supported(rows, weight):
@@ -61,6 +75,8 @@ def linear(x, weight, split_ok=False):
     rows = x.numel() // x.shape[-1]
     if x.dtype != torch.bfloat16 or not weight.is_contiguous() or not supported(rows, weight):
         return F.linear(x, weight)
+    if _NATIVE and (weight.device, rows, weight.shape[0], weight.shape[1]) in _NATIVE:
+        return F.linear(x, weight)
     _native.require_cuda(x, weight)
     flat = x.reshape(rows, x.shape[-1]).contiguous()
     n, k = weight.shape
@@ -71,18 +87,17 @@ def linear(x, weight, split_ok=False):
         *x.shape[:-1], n)
 
 
-def swiglu_linear(x, gate_up_blocked, split_consumer=True):
+def swiglu_linear(x, gate_up_blocked):
     """SwiGLU(x @ W^T), W's rows being [gate; up] interleaved in 64-row blocks: bf16(bf16(silu(
     gate)) * up) per feature, the reference's projection + swiglu arithmetic. At one K split the
     projection's epilogue applies SwiGLU (one launch). With K splits the projection writes
-    split partials that fb_swiglu_blocked sums and activates (``split_consumer``, measured
-    faster inside the decode step), or, without it, the last split CTA of each tile sums them
-    and applies SwiGLU in the projection's launch (the split fix-up). The same bits either way."""
+    split partials that fb_swiglu_blocked sums and activates (measured faster inside the decode
+    step than summing the splits in the projection's own launch). The same bits either way."""
     rows = x.numel() // x.shape[-1]
     flat = x.reshape(rows, x.shape[-1]).contiguous()
     n, k = gate_up_blocked.shape
-    splits = splits_for(rows, n, k, x.device, finished=True)
-    if splits == 1 or not split_consumer:
+    splits = splits_for(rows, n, k, x.device)
+    if splits == 1:
         return project(flat, gate_up_blocked, SWIGLU_OUT, splits).reshape(*x.shape[:-1], n // 2)
     partials = project(flat, gate_up_blocked, SPLITS_OUT, splits)
     out = torch.empty((rows, n // 2), device=x.device, dtype=torch.bfloat16)

@@ -88,22 +88,6 @@ int fb_decode_attention_combine(const int64_t* position, int per_row, void* out,
  * otherwise. */
 int fb_decode_attention_cluster_shape(int cluster, int stages);
 
-/* Decode attention with the QK-norm + RoPE + KV append fused in (engine/kernels/qk_rope.py:87-129
- * followed by decode_attention.py:238-257, one launch): the query heads and the newest K/V slot
- * come from the packed qkv projection output `packed` (bf16 [B, (Hq + 2 Hkv) * 128] when
- * packed_splits == 0, else fp32 split-K partials [packed_splits, B, (Hq + 2 Hkv) * 128]),
- * with fb_qk_norm_rope_append's mode-0 whole-table arithmetic at the shared slot position[0]
- * (q_weight/k_weight bf16 [128], cos/sin bf16 [>= capacity, 128]). The K and V heads are
- * written into slot position[0] of keys/values [B, Hkv, capacity, 128], which the attention
- * then reads; out bf16 [B, Hq, 128]. The same bits as fb_qk_norm_rope_append +
- * fb_decode_attention. Runs only as the cluster form (head_dim 128, 2 * B * Hkv <= the SM
- * count, every pair's cluster resident at once); otherwise returns FB_ERR_SHAPE and launches
- * nothing (use the two calls). No workspace. No reference counterpart as one call. */
-int fb_qk_rope_decode_attention(const void* packed, int packed_splits, const void* q_weight, const void* k_weight,
-                                float q_eps, float k_eps, const void* cos, const void* sin, const int64_t* position,
-                                void* keys, void* values, void* out, int batch, int q_heads, int kv_heads,
-                                int head_dim, int capacity, float scale, void* stream);
-
 /* ------------------------------------------------------------------------------------
  * Decode attention without allocation. No counterpart in the reference.
  * Some callers cannot allocate device memory on the call path: a host runtime that owns a
@@ -116,7 +100,9 @@ int fb_qk_rope_decode_attention(const void* packed, int packed_splits, const voi
  *   Limit: batch * kv_heads <= 512 (and the fb_decode_attention limits); a larger request
  *   returns FB_ERR_TOO_LARGE and launches nothing.
  *   The first call on a device looks up the array's device address for that device (it must
- *   be the current device); make that first call before any stream capture.
+ *   be the current device); make that first call before any stream capture. The address is
+ *   kept for the life of the process: after cudaDeviceReset (or anything else that destroys
+ *   and recreates the device's primary context) this entry point must not be called again.
  *   Every call shares the one array, which keeps the last call's contents; each call clears
  *   the part that must start at zero. Calls that overlap on the GPU (several streams, or
  *   several host threads on one device) race on the array: serialise them.
@@ -135,7 +121,7 @@ int fb_decode_attention_noalloc(const void* q, const void* k, const void* v,
  *   position int64 [B]; chain int64 [B]: tokens t < chain[b] see slots [0, position[b] + t];
  *            later tokens see [0, position[b]] plus their own slot
  *   out      bf16 [B, T, Hq, D]
- *   D = 128; T * (Hq / Hkv) <= 2048. `splits` KV splits per (row, KV head):
+ *   D in {64, 128}; T * (Hq / Hkv) <= 2048. `splits` KV splits per (row, KV head):
  *   fb_verify_attention_splits() gives the default; with splits > 1 the workspace must hold
  *   fb_verify_attention_workspace() bytes (partials merged by a second launch).
  * ---------------------------------------------------------------------------------- */
@@ -173,20 +159,6 @@ int fb_qk_norm_rope_append(const void* packed, int packed_splits, const void* q_
                            void* query, void* keys, void* values, int batch, int tokens,
                            int q_heads, int kv_heads, int head_dim, int capacity, int mode,
                            int table, void* stream);
-
-/* The decode form fused into the qkv projection: x bf16 [M, K] (M <= 64 rows, one token
- * each, all at the shared slot position[0]) times the packed qkv weight W bf16
- * [(Hq + 2 Hkv) * 128, K]; head_dim must be 128 (one output tile = one head). The K splits of
- * a head (`splits`, fb_linear_finished_splits(); FB_ERR_SHAPE when a split head exceeds the
- * split fix-up storage) are summed in split order in the same launch, rounded to bf16, and the head goes through fb_qk_norm_rope_append's mode-0
- * whole-table arithmetic: q heads to query bf16 [M, Hq, 128], k heads (normalized, rotated)
- * and v heads (copied) to slot position[0] of keys/values [M, Hkv, C, 128]. Bit-identical to
- * fb_linear (epilogue 3) + fb_qk_norm_rope_append (mode 0, table 1), in one launch. (Inside
- * the Qwen3-8B decode step on B200 the two-launch form measured faster.) */
-int fb_linear_qk_rope(const void* x, const void* w, int m, int n, int k, int splits, const void* q_weight,
-                      const void* k_weight, float q_eps, float k_eps, const void* cos, const void* sin,
-                      const int64_t* position, void* query, void* keys, void* values, int q_heads,
-                      int kv_heads, int head_dim, int capacity, void* stream);
 
 /* ------------------------------------------------------------------------------------
  * RMSNorm family. Replace engine/kernels/rmsnorm.py:
@@ -236,14 +208,10 @@ int fb_swiglu_blocked(const void* packed, int splits, void* out, int rows, int w
  *               order, then round (engine/kernels/merged.py:13-45). No workspace needed.
  * Grid = ceil(N/128) tiles x `splits` K-splits (fb_linear_splits() picks a default for
  * epilogue 3, fb_linear_finished_splits() for epilogues 0-2). For epilogues 0-2 with
- * splits > 1 the partials of a tile are summed in split order (deterministic; the bits a
- * split consumer produces) in the same launch: by the tile's last-arriving CTA through a
- * library-owned device array and arrival counter when the shape fits it (splits <= 16,
- * ceil(N/128) * splits * M * 128 <= 2^22), else through distributed shared memory of a
- * thread-block cluster (splits <= 8). The array is shared by all launches on a device:
- * such launches must not run concurrently on two streams. No caller workspace. Launched
- * with programmatic stream serialization (weights are prefetched before the previous
- * kernel completes).
+ * splits > 1 (at most 8) the CTAs of a tile form a thread-block cluster and sum their
+ * partials in split order through distributed shared memory (deterministic; the bits a
+ * split consumer produces), in the same launch. No workspace. Launched with programmatic
+ * stream serialization (weights are prefetched before the previous kernel completes).
  * ---------------------------------------------------------------------------------- */
 int fb_linear_splits(int m, int n, int k);
 int fb_linear_finished_splits(int m, int n, int k);
@@ -262,8 +230,8 @@ int fb_linear(const void* x, const void* w, void* out, int m, int n, int k, int 
  *   rule, argmax.py:1-9), into out int64 [rows] (and the winning value into top when not
  *   NULL). With world > 1 each rank holds a vocabulary slice (index_base = its offset) and
  *   the ranks exchange their bests through peer_exchange[r] = rank r's exchange buffer,
- *   uint64 [rows, world, 2], with the flagged-word protocol of fb_linear_allreduce_push
- *   (same epoch rule; bounded 2 s wait): every rank writes the same ids.
+ *   uint64 [rows, world, 2], with the flagged-word protocol of fb_reduce_scatter_push (same
+ *   epoch rule; bounded 2 s wait): every rank writes the same ids.
  * ---------------------------------------------------------------------------------- */
 size_t fb_argmax_candidates_bytes(int m, int n);
 int fb_linear_argmax(const void* x, const void* w, int m, int n, int k, int64_t index_base, void* cand,
@@ -317,47 +285,36 @@ int fb_spec_relocate(void* store, int planes, int batch, int kv_heads, int capac
                      const int64_t* move_from, const int64_t* move_to, void* stream);
 
 /* ------------------------------------------------------------------------------------
- * Tensor-parallel projection + all-reduce over NVLink peer memory (no counterpart in the
- * reference, which is single-GPU; this replaces an NCCL all-reduce after o_proj/down_proj).
- * Low-latency protocol: every value travels as one 8-byte word, low half the fp32 bits,
- * high half the flag (uint32)(*epoch) + 1, stored whole; a reader that sees the flag sees
- * the value, so there is no fence, counter or reset. recv[r] is rank r's receive buffer,
- * uint64 words [uses, world, M, N]; zero it before first use and again before `*epoch`
- * (a device int64, the decode position) can repeat a value it had (a new generation).
- * *epoch must differ between two calls with the same `use` and stay below 2^31.
- * Producer: fb_linear_allreduce_push computes this rank's fp32 partial of y = x @ W^T
- *   (K-splits summed in the same launch as fb_linear's finished tiles) and stores every value into
- *   slab `rank` of recv[use] on every rank (peer_recv[r] = rank r's recv base). When
- *   multicast_recv is not NULL it is the NVSwitch multicast address of the same buffers
- *   (every rank's recv bound to one multicast object): each word is stored once through it
- *   (multimem.st) instead of once per peer.
- * Consumer: fb_allreduce_add_rmsnorm polls (bounded, 2 s) this rank's recv[use] until
- *   every word of the world slabs carries the flag, sums the slabs in rank order (the same
- *   bits on every rank), rounds to bf16 and applies add_rms_norm (fb_add_rmsnorm's
- *   arithmetic) with `residual`/`w`. One call per use per step, in the same order on every
- *   rank.
+ * Tensor-parallel all-reduce + residual add + RMSNorm over NVLink peer memory (no counterpart
+ * in the reference, which is single-GPU; this replaces an NCCL all-reduce after o_proj/down_proj
+ * and the add_rms_norm that follows it, engine/kernels/rmsnorm.py:98-125 arithmetic).
+ * Owner-computes: rank q owns columns [q*N/world, (q+1)*N/world) of the N-wide rows.
+ * Low-latency protocol: every value travels inside one 8-byte word whose high half is the flag
+ * (uint32)(*epoch) + 1, stored whole, so a reader that sees the flag sees the value: no fence,
+ * counter or reset. *epoch (a device int64, the decode position) must differ between two calls
+ * with the same `use` and stay below 2^31. Each rank owns three uint64 regions (16-byte
+ * aligned; zero them before first use and again before *epoch can repeat a value it had):
+ *   rs [uses, world, M, N/world]  fp32 partials pushed to this rank as the owner
+ *   ag [uses, M, N/2]             summed bf16 pairs of whole rows, from every owner
+ *   ss [uses, world, M]           each owner's fp32 sum of squares of its slice of a row
+ * fb_reduce_scatter_push sums this rank's fp32 split-K partials [splits, M, N] of y = x @ W^T in
+ *   split order and stores every value only into the owner's rs[use][rank] (peer_rs[q] =
+ *   rank q's rs base). N % (2 * world) == 0.
+ * fb_allreduce_add_rmsnorm (one launch): as the owner, polls rs[use] (bounded, 2 s), sums the
+ *   ranks in rank order, rounds to bf16, adds `residual` (rounded again: the bf16 residual sum
+ *   of add_rms_norm), stores the summed pairs into every rank's ag[use] and the slice's sum of
+ *   squares per row into every rank's ss[use][rank]; then polls its own ag[use] and ss[use] and
+ *   writes, for every row, `sum` (the summed row, the next residual) and `out` =
+ *   bf16(bf16(sum * rsqrt(mean(sum^2) + eps)) * w), the sums of squares added in rank order (the
+ *   same bits on every rank). residual/out/sum bf16 [M, N], w bf16 [N]. One call per use per
+ *   step, in the same order on every rank.
  * ---------------------------------------------------------------------------------- */
-int fb_linear_allreduce_push(const void* x, const void* w, int m, int n, int k, int splits, int world,
-                             int rank, int use, void* const* peer_recv, void* multicast_recv,
-                             const int64_t* epoch, void* stream);
-/* The producer's split-K form: sums fp32 partials [splits, M, N] in split order and pushes
- * every value like fb_linear_allreduce_push (same recv layout and flags); N % 2 == 0. */
-int fb_reduce_push(const void* partials, int splits, int m, int n, int world, int rank, int use,
-                   void* const* peer_recv, void* multicast_recv, const int64_t* epoch, void* stream);
-int fb_allreduce_add_rmsnorm(const void* recv, int use, int world, const int64_t* epoch,
+int fb_reduce_scatter_push(const void* partials, int splits, int m, int n, int world, int rank, int use,
+                           void* const* peer_rs, const int64_t* epoch, void* stream);
+int fb_allreduce_add_rmsnorm(const void* rs, const void* ag, const void* ss, void* const* peer_ag,
+                             void* const* peer_ss, int use, int world, int rank, const int64_t* epoch,
                              const void* residual, const void* w, void* out, void* sum, int rows,
                              int width, float eps, void* stream);
-/* Producer and consumer in one launch: sums this rank's fp32 split partials [splits, rows,
- * width] in split order, pushes every value into slab `rank` of recv[use] on every rank
- * exactly like fb_reduce_push (peer_recv / multicast_recv), then, on the same columns, runs
- * fb_allreduce_add_rmsnorm on this rank's receive buffer `recv`. Same bits as
- * fb_reduce_push + fb_allreduce_add_rmsnorm, one launch fewer. Every rank's CTAs push before
- * they poll, so the ranks cannot wait on one another's launches. (Inside the Qwen3-8B decode
- * step on B200 the two-launch form measured faster: 5817 against 4914 tok/s at 4 ranks.) */
-int fb_reduce_push_add_rmsnorm(const void* partials, int splits, void* const* peer_recv, void* multicast_recv,
-                               const void* recv, int use, int world, int rank, const int64_t* epoch,
-                               const void* residual, const void* w, void* out, void* sum, int rows, int width,
-                               float eps, void* stream);
 
 /* Sums fp32 split partials [splits, count] into bf16 [count] (or fp32 when out_fp32):
  * the reference's `_merge_projection` (linear.py:81-93). */

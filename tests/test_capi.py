@@ -50,26 +50,9 @@ def test_host_validation_without_gpu():
     assert lib.fb_linear(p, p, p, 4, 128, 100, 0, 1, null) == -2      # K not a multiple of 8
     assert lib.fb_linear(p, p, p, 4, 128, 128, 7, 1, null) == -1      # unknown epilogue
     assert lib.fb_linear(p, p, p, 4, 128, 128, 0, 3, null) == -2      # more splits than K chunks
-    assert lib.fb_linear(p, p, p, 4, 128, 4096, 0, 17, null) == -2    # finished tile: split fix-up of <= 16 splits
-    assert lib.fb_linear(p, p, p, 64, 151936, 4096, 0, 9, null) == -2  # too large for the fix-up: cluster of <= 8
-    assert lib.fb_linear_finished_splits(16, 3072, 4096) <= 16
+    assert lib.fb_linear(p, p, p, 4, 128, 4096, 0, 9, null) == -2     # finished tile: a cluster of <= 8 splits
+    assert lib.fb_linear_finished_splits(16, 3072, 4096) <= 8
     assert lib.fb_linear_finished_splits(64, 151936, 4096) <= 8
-    # fused qkv + QK-norm/RoPE: head_dim must be 128 and N the packed q/k/v width
-    assert lib.fb_linear_qk_rope(null, p, 16, 768, 4096, 1, p, p, 1e-6, 1e-6, p, p, p, p, p, p, 4, 1, 128, 64,
-                                 null) == -1
-    assert lib.fb_linear_qk_rope(p, p, 16, 384, 4096, 1, p, p, 1e-6, 1e-6, p, p, p, p, p, p, 4, 1, 64, 64,
-                                 null) == -2
-    assert lib.fb_linear_qk_rope(p, p, 16, 640, 4096, 1, p, p, 1e-6, 1e-6, p, p, p, p, p, p, 4, 1, 128, 64,
-                                 null) == -2
-    assert lib.fb_linear_qk_rope(p, p, 65, 768, 4096, 1, p, p, 1e-6, 1e-6, p, p, p, p, p, p, 4, 1, 128, 64,
-                                 null) == -2
-    # fused QK-norm/RoPE + decode attention: null -> ARG; head_dim 64 -> SHAPE (cluster form only)
-    assert lib.fb_qk_rope_decode_attention(null, 0, p, p, 1e-6, 1e-6, p, p, p, p, p, p, 16, 4, 1, 128, 64, 0.088,
-                                           null) == -1
-    assert lib.fb_qk_rope_decode_attention(p, 0, p, p, 1e-6, 1e-6, p, p, p, p, p, p, 16, 4, 1, 64, 64, 0.088,
-                                           null) == -2
-    assert lib.fb_qk_rope_decode_attention(p, -1, p, p, 1e-6, 1e-6, p, p, p, p, p, p, 16, 4, 1, 128, 64, 0.088,
-                                           null) == -1
     # cluster-shape override: powers of two up to 16, ring depth 2-4; (0, 0) restores automatic
     assert lib.fb_decode_attention_cluster_shape(3, 2) == -1
     assert lib.fb_decode_attention_cluster_shape(8, 5) == -1
@@ -89,15 +72,16 @@ def test_host_validation_without_gpu():
     assert lib.fb_spec_propose(p, 64, p, p, 8, 4, p, p, p, p, 2, 8, 1, 1, 1, 8, 8, null) == -1
     assert lib.fb_spec_settle(p, p, null, p, p, p, 64, p, p, p, p, p, 2, 65, null) == -2
     assert lib.fb_spec_relocate(p, 4, 2, 2, 64, 60, p, p, null) == -2
-    # tensor-parallel producers: odd widths, unaligned peer buffers, bad ranks
+    # tensor-parallel all-reduce: widths that do not split into even slices, unaligned peer
+    # regions, bad ranks
     peers = (ctypes.c_void_p * 2)(16, 32)
-    assert lib.fb_reduce_push(p, 2, 4, 5, 2, 0, 0, peers, null, p, null) == -2
-    assert lib.fb_reduce_push(p, 2, 4, 8, 2, 2, 0, peers, null, p, null) == -1
+    assert lib.fb_reduce_scatter_push(p, 2, 4, 6, 2, 0, 0, peers, p, null) == -2   # 6 % (2 * 2)
+    assert lib.fb_reduce_scatter_push(p, 2, 4, 8, 2, 2, 0, peers, p, null) == -1   # rank >= world
     odd = (ctypes.c_void_p * 2)(16, 40)
-    assert lib.fb_reduce_push(p, 2, 4, 8, 2, 0, 0, odd, null, p, null) == -1
-    assert lib.fb_reduce_push_add_rmsnorm(p, 2, peers, null, p, 0, 2, 2, p, p, p, p, p, 4, 4096, 1e-6, null) == -1
-    assert lib.fb_reduce_push_add_rmsnorm(p, 2, odd, null, p, 0, 2, 0, p, p, p, p, p, 4, 4096, 1e-6, null) == -1
-    assert lib.fb_reduce_push_add_rmsnorm(p, 2, peers, null, p, 0, 2, 0, p, p, p, p, p, 4, 4100, 1e-6, null) == -2
+    assert lib.fb_reduce_scatter_push(p, 2, 4, 8, 2, 0, 0, odd, p, null) == -1     # not 16-byte aligned
+    assert lib.fb_allreduce_add_rmsnorm(p, p, p, peers, peers, 0, 9, 0, p, p, p, p, p, 4, 4096, 1e-6, null) == -1
+    assert lib.fb_allreduce_add_rmsnorm(p, p, p, peers, peers, 0, 2, 0, p, p, p, p, p, 4, 4100, 1e-6, null) == -2
+    assert lib.fb_allreduce_add_rmsnorm(null, p, p, peers, peers, 0, 2, 0, p, p, p, p, p, 4, 4096, 1e-6, null) == -1
     assert lib.fb_linear_argmax(p, p, 4, 128, 128, -1, p, null) == -1
     # workspace too small -> FB_ERR_WORKSPACE
     need = lib.fb_decode_attention_workspace(1, 16, 8, 128, 148)

@@ -208,12 +208,11 @@ def test_qk_rope_cache_matches_reference(case):
     assert torch.equal(values, fx["values"])
     written = fx["keys"] != 17
     assert torch.equal(keys[~written], fx["keys"][~written])
-    # K (the cache contents) and Q: bit-exact up to rare rsqrt/reduction-order ties
-    for actual, expected in ((query, fx["query"]), (keys, fx["keys"])):
-        equal = (actual == expected).float().mean().item()
-        assert equal >= 0.998, equal
-        assert ulps(actual, expected).max().item() <= 1
-        torch.testing.assert_close(actual.float(), expected.float(), atol=0.03125, rtol=0.008)
+    # K (the cache contents) and Q: bit-exact (the sum of squares is added in the reference's
+    # eager order, every step correctly rounded)
+    for name, actual, expected in (("query", query, fx["query"]), ("keys", keys, fx["keys"])):
+        differ = (actual != expected).nonzero()
+        assert differ.numel() == 0, f"{name}: {differ.shape[0]} elements differ, first {differ[:4].tolist()}"
 
 
 # ------------------------------------------------------------------ norms, SwiGLU, projections, argmax
@@ -258,9 +257,9 @@ def test_swiglu_matches_reference():
 
 def test_linear_matches_reference():
     """Every epilogue against the reference's projection contract (F.linear, verify_gpu.py:175-185)
-    for several split counts: bf16 and fp32 finished tiles (splits summed by the split fix-up, or
-    by a cluster for shapes too large for the fix-up storage), fp32 split partials;
-    deterministic; finished tiles equal the split-order sum of the partials."""
+    for several split counts: bf16 and fp32 finished tiles (splits summed by a thread-block
+    cluster), fp32 split partials; deterministic; finished tiles equal the split-order sum of
+    the partials."""
     from kernels import linear as klin
     from kernels._native import lib, ptr, stream, check
     fx = load("pointwise")
@@ -281,9 +280,8 @@ def test_linear_matches_reference():
 
 
 def _check_finished_splits(xd, wd, exact, splits):
-    """Split partials sum to the exact product; a finished fp32 tile over the same splits (fix-up
-    or cluster) equals their split-order sum bit for bit, twice in a row (the fix-up counters
-    return to zero)."""
+    """Split partials sum to the exact product; a finished fp32 tile over the same splits (summed
+    by the tile's cluster) equals their split-order sum bit for bit, twice in a row."""
     from kernels._native import lib, ptr, stream, check
     m, k = xd.shape
     n = wd.shape[0]
@@ -297,17 +295,17 @@ def _check_finished_splits(xd, wd, exact, splits):
     for _ in range(2):
         out = torch.empty(m, n, dtype=torch.float32, device=DEV)
         status = lib.fb_linear(ptr(xd), ptr(wd), ptr(out), m, n, k, 1, splits, stream())
-        if splits > 16 or (splits > 8 and (n + 127) // 128 * 128 * splits * m > 1 << 22):
-            assert status == -2  # beyond the fix-up and the cluster
+        if splits > 8:
+            assert status == -2  # a finished tile's splits form one cluster of at most 8 CTAs
             return
         check(status, "fb_linear")
         torch.cuda.synchronize()
-        assert torch.equal(out, ordered)  # split-order sum, fix-up or cluster
+        assert torch.equal(out, ordered)  # split-order sum through the cluster
 
 
-def test_linear_finished_tiles_cluster_fallback():
-    """A shape too large for the split fix-up storage (64 rows x 512 tiles x S splits > 2^22
-    fp32 values) sums its splits through the thread-block cluster instead: same bits."""
+def test_linear_finished_tiles_large_shape():
+    """A wide projection (64 rows x 512 tiles) sums its splits through the thread-block cluster
+    of each tile: the split-order bits."""
     g = torch.Generator().manual_seed(5)
     x = torch.randn(64, 256, generator=g).bfloat16()
     w = (torch.randn(65536, 256, generator=g) * 0.05).bfloat16()
@@ -330,8 +328,9 @@ def test_linear_split_result_feeds_consumers():
 def test_swiglu_linear_matches_oracle():
     """Projection + SwiGLU on 64-row gate/up blocks equals projecting gate and up separately and
     applying the reference's SwiGLU (swiglu.py:13-24), in every form: the split-partials path
-    with fb_swiglu_blocked (what swiglu_linear runs by default) and the fused epilogue at one
-    split and over K splits summed by the split fix-up; the split forms agree bit for bit."""
+    with fb_swiglu_blocked (what swiglu_linear runs when the projection has K splits) and the
+    fused epilogue at one split and over K splits summed by the tile's cluster; the split forms
+    agree bit for bit."""
     import qwen3
     from kernels import linear as klin
     g = torch.Generator().manual_seed(11)
@@ -342,18 +341,24 @@ def test_swiglu_linear_matches_oracle():
         blocked = qwen3.interleave_gate_up(gate, up).contiguous().to(DEV)
         expect = opw.swiglu(torch.cat((opw.linear(x, gate), opw.linear(x, up)), -1))
         xd = x.to(DEV)
-        forms = {"swiglu_linear": klin.swiglu_linear(xd, blocked),
-                 "split fix-up": klin.swiglu_linear(xd, blocked, split_consumer=False)}
+        forms = {"swiglu_linear": klin.swiglu_linear(xd, blocked)}
         chunks = hidden // 64
-        for splits in sorted({1, 2, min(chunks, 8), min(chunks, 12)}):
-            if splits > 8 and 2 * width * splits * rows > 1 << 22:
-                continue  # beyond the split fix-up storage: a cluster takes at most 8 splits
+        for splits in sorted({1, 2, min(chunks, 4), min(chunks, 8)}):
             forms[f"epilogue S={splits}"] = klin.project(xd, blocked, klin.SWIGLU_OUT, splits)
+        splits = klin.splits_for(rows, 2 * width, hidden, xd.device)
+        if splits > 1:
+            partials = klin.project(xd, blocked, klin.SPLITS_OUT, splits)
+            out = torch.empty(rows, width, dtype=torch.bfloat16, device=DEV)
+            from kernels._native import check, lib, ptr, stream
+            check(lib.fb_swiglu_blocked(ptr(partials), splits, ptr(out), rows, width, stream()), "fb_swiglu_blocked")
+            forms["split consumer"] = out
+            if splits <= 8:
+                assert torch.equal(out, forms.get(f"epilogue S={splits}", klin.project(xd, blocked, klin.SWIGLU_OUT,
+                                                                                       splits)))
         for name, got in forms.items():
             got = got.cpu()
             assert (got == expect).float().mean() >= 0.99, name
             torch.testing.assert_close(got.float(), expect.float(), atol=0.015625, rtol=0.016, msg=name)
-        assert torch.equal(forms["swiglu_linear"], forms["split fix-up"])
 
 
 def test_argmax_matches_reference():
@@ -415,191 +420,91 @@ def test_decode_attention_fused_equals_two_launch_and_counters_reset():
         assert int(counters.abs().sum()) == 0
 
 
-def test_push_producers_single_rank():
-    """The TP all-reduce producers at world 1 (the receive buffer is this GPU's own): every word
-    carries flag epoch + 1 in its high half and the fp32 value bits of x @ W^T in its low half,
-    the same bits for one split, K splits summed by the split fix-up, and split partials +
-    fb_reduce_push (split-order sums)."""
+def test_allreduce_single_rank():
+    """The TP all-reduce at world 1 (every region is this GPU's own): fb_reduce_scatter_push stores
+    the split-order sum of the projection's K-split partials as flagged fp32 words; the owner
+    phase of fb_allreduce_add_rmsnorm then writes the summed bf16 pairs and the row's sum of
+    squares, flagged, and the result equals add_rms_norm over the same partials (the residual sum
+    bit for bit, the normalized row within the norm's reduction-order ULPs)."""
     import ctypes
     from kernels import linear as klin
     from kernels._native import lib, ptr, stream, check
+    from kernels.merged import Split
+    from kernels.rmsnorm import add_rms_norm
     g = torch.Generator().manual_seed(21)
     m, n, k = 16, 4096, 1536
     x = torch.randn(m, k, generator=g).bfloat16().to(DEV)
     w = (torch.randn(n, k, generator=g) * 0.05).bfloat16().to(DEV)
+    residual = torch.randn(m, n, generator=g).bfloat16().to(DEV)
+    gain = torch.randn(n, generator=g).bfloat16().to(DEV)
     epoch = torch.full((1,), 9, dtype=torch.int64, device=DEV)
     exact = x.float() @ w.float().T
-    splits = int(lib.fb_linear_finished_splits(m, n, k))
+    splits = int(lib.fb_linear_splits(m, n, k))
     assert splits > 1
     part = klin.project(x, w, klin.SPLITS_OUT, splits)
     ordered = part[0].clone()
     for s in range(1, splits):
         ordered += part[s]
-    words = {}
-    for name in ("one split", "fix-up", "split consumer"):
-        recv = torch.zeros(1, 1, m, n, dtype=torch.int64, device=DEV)
-        peers = (ctypes.c_void_p * 1)(recv.data_ptr())
-        if name == "split consumer":
-            check(lib.fb_reduce_push(ptr(part), splits, m, n, 1, 0, 0, peers, None, ptr(epoch), stream()),
-                  "fb_reduce_push")
-        else:
-            s = 1 if name == "one split" else splits
-            check(lib.fb_linear_allreduce_push(ptr(x), ptr(w), m, n, k, s, 1, 0, 0, peers, None, ptr(epoch), stream()),
-                  "fb_linear_allreduce_push")
-        torch.cuda.synchronize()
-        halves = recv.view(torch.int32).view(m, n, 2)  # little-endian: [value bits, flag]
-        assert bool((halves[..., 1] == 10).all()), name
-        words[name] = halves[..., 0].contiguous().view(torch.float32)
-        torch.testing.assert_close(words[name], exact, atol=1e-4, rtol=1e-4, msg=name)
-    assert torch.equal(words["fix-up"], ordered)
-    assert torch.equal(words["split consumer"], ordered)
+    rs = torch.zeros(2, 1, m, n, dtype=torch.int64, device=DEV)  # two uses
+    ag = torch.zeros(2, m, n // 2, dtype=torch.int64, device=DEV)
+    ss = torch.zeros(2, 1, m, dtype=torch.int64, device=DEV)
+    use = 1
+    check(lib.fb_reduce_scatter_push(ptr(part), splits, m, n, 1, 0, use, (ctypes.c_void_p * 1)(rs.data_ptr()),
+                                     ptr(epoch), stream()), "fb_reduce_scatter_push")
+    out, summed = torch.empty_like(residual), torch.empty_like(residual)
+    check(lib.fb_allreduce_add_rmsnorm(ptr(rs), ptr(ag), ptr(ss), (ctypes.c_void_p * 1)(ag.data_ptr()),
+                                       (ctypes.c_void_p * 1)(ss.data_ptr()), use, 1, 0, ptr(epoch), ptr(residual),
+                                       ptr(gain), ptr(out), ptr(summed), m, n, 1e-6, stream()),
+          "fb_allreduce_add_rmsnorm")
+    torch.cuda.synchronize()
+    halves = rs[use].view(torch.int32).view(m, n, 2)  # little-endian: [value bits, flag]
+    assert bool((halves[..., 1] == 10).all())
+    words = halves[..., 0].contiguous().view(torch.float32)
+    torch.testing.assert_close(words, exact, atol=1e-4, rtol=1e-4)
+    assert torch.equal(words, ordered)
+    assert bool((rs[0] == 0).all()) and bool((ag[0] == 0).all())  # use 0 untouched
+    assert bool((ag[use].view(torch.int32).view(m, n // 2, 2)[..., 1] == 10).all())
+    e_out, e_sum = add_rms_norm(Split(part, (m, n)), residual, gain, 1e-6)
+    assert torch.equal(summed, e_sum)
+    assert (out == e_out).float().mean() >= 0.999 and ulps(out, e_out).max() <= 2
 
 
-@pytest.mark.parametrize("rows,q_heads,kv_heads,hidden", [(16, 4, 1, 4096), (16, 32, 8, 4096), (1, 16, 8, 1024),
-                                                           (33, 8, 2, 512), (64, 32, 8, 1024)])
-def test_linear_qk_rope_equals_two_launch(rows, q_heads, kv_heads, hidden):
-    """fb_linear_qk_rope (qkv projection with QK-norm + RoPE + KV append in its epilogue, K splits
-    summed by the split fix-up) writes the same query and cache bits as the projection's split
-    partials followed by fb_qk_norm_rope_append (mode 0, whole tables), at one split and at the
-    finished-tile split count; other cache slots keep their sentinel."""
-    from kernels import linear as klin
-    from kernels._native import lib, ptr, stream, check
-    g = torch.Generator().manual_seed(rows * 100 + q_heads)
-    d, capacity, pos = 128, 96, 77
-    n = (q_heads + 2 * kv_heads) * d
-    x = torch.randn(rows, hidden, generator=g).bfloat16().to(DEV)
-    w = (torch.randn(n, hidden, generator=g) * 0.05).bfloat16().to(DEV)
-    q_gain = (1 + 0.1 * torch.randn(d, generator=g)).bfloat16().to(DEV)
-    k_gain = (1 + 0.1 * torch.randn(d, generator=g)).bfloat16().to(DEV)
-    cos = torch.randn(capacity, d, generator=g).bfloat16().to(DEV)
-    sin = torch.randn(capacity, d, generator=g).bfloat16().to(DEV)
-    position = torch.tensor([pos], dtype=torch.int64, device=DEV)
-    finished = int(lib.fb_linear_finished_splits(rows, n, hidden))
-    for splits in sorted({1, finished}):
-        outs = []
-        for fused in (True, False):
-            keys = torch.full((rows, kv_heads, capacity, d), 17.0).bfloat16().to(DEV)
-            values = torch.full((rows, kv_heads, capacity, d), 17.0).bfloat16().to(DEV)
-            query = torch.empty(rows, 1, q_heads, d, dtype=torch.bfloat16, device=DEV)
-            if fused:
-                check(lib.fb_linear_qk_rope(ptr(x), ptr(w), rows, n, hidden, splits, ptr(q_gain), ptr(k_gain), 1e-6,
-                                            1e-6, ptr(cos), ptr(sin), ptr(position), ptr(query), ptr(keys),
-                                            ptr(values), q_heads, kv_heads, d, capacity, stream()),
-                      "fb_linear_qk_rope")
-            else:
-                part = klin.project(x, w, klin.SPLITS_OUT, splits)
-                check(lib.fb_qk_norm_rope_append(ptr(part), splits, ptr(q_gain), ptr(k_gain), 1e-6, 1e-6, ptr(cos),
-                                                 ptr(sin), ptr(position), None, ptr(query), ptr(keys), ptr(values),
-                                                 rows, 1, q_heads, kv_heads, d, capacity, 0, 1, stream()),
-                      "fb_qk_norm_rope_append")
-            torch.cuda.synchronize()
-            outs.append((query.cpu(), keys.cpu(), values.cpu()))
-        for name, a, b in zip(("query", "keys", "values"), outs[0], outs[1]):
-            assert torch.equal(a, b), (name, splits)
-        keys = outs[0][1]
-        assert bool((keys[:, :, pos] != 17).any()) and bool((keys[:, :, :pos] == 17).all())
-
-
-def test_reduce_push_add_rmsnorm_single_rank():
-    """fb_reduce_push_add_rmsnorm at world 1 (the push lands in this GPU's own receive buffer,
-    then the same kernel polls it): the same bits as add_rms_norm over the split partials
-    (fb_add_rmsnorm: split-order fp32 sum, bf16, + residual, RMSNorm), and every pushed word
-    carries flag epoch + 1 with the split-order fp32 sum."""
-    import ctypes
-    from kernels import linear as klin
-    from kernels._native import lib, ptr, stream, check
-    g = torch.Generator().manual_seed(31)
-    rows, width, k = 16, 4096, 1536
-    x = torch.randn(rows, k, generator=g).bfloat16().to(DEV)
-    w = (torch.randn(width, k, generator=g) * 0.05).bfloat16().to(DEV)
-    residual = torch.randn(rows, width, generator=g).bfloat16().to(DEV)
-    gain = (1 + 0.1 * torch.randn(width, generator=g)).bfloat16().to(DEV)
-    epoch = torch.full((1,), 12, dtype=torch.int64, device=DEV)
-    for splits in (1, 2, 6, 11):
-        part = klin.project(x, w, klin.SPLITS_OUT, splits)
-        ordered = part[0].clone()
-        for s in range(1, splits):
-            ordered += part[s]
-        recv = torch.zeros(2, 1, rows, width, dtype=torch.int64, device=DEV)  # two uses; use 1 is pushed
-        peers = (ctypes.c_void_p * 1)(recv.data_ptr())
-        out, summed = torch.empty_like(residual), torch.empty_like(residual)
-        check(lib.fb_reduce_push_add_rmsnorm(ptr(part), splits, peers, None, ptr(recv), 1, 1, 0, ptr(epoch),
-                                             ptr(residual), ptr(gain), ptr(out), ptr(summed), rows, width, 1e-6,
-                                             stream()), "fb_reduce_push_add_rmsnorm")
-        e_out, e_sum = torch.empty_like(residual), torch.empty_like(residual)
-        check(lib.fb_add_rmsnorm(ptr(part), splits, ptr(residual), ptr(gain), ptr(e_out), ptr(e_sum), rows, width,
-                                 1e-6, stream()), "fb_add_rmsnorm")
-        torch.cuda.synchronize()
-        assert torch.equal(out, e_out) and torch.equal(summed, e_sum), splits
-        halves = recv[1].view(torch.int32).view(rows, width, 2)
-        assert bool((halves[..., 1] == 13).all())
-        assert torch.equal(halves[..., 0].contiguous().view(torch.float32), ordered)
-        assert bool((recv[0] == 0).all())  # other uses untouched
-
-
-@pytest.mark.parametrize("batch,q_heads,kv_heads,length,splits",
-                         [(16, 4, 1, 8193, 16), (16, 16, 4, 1000, 12), (1, 16, 8, 640, 0), (3, 8, 2, 100, 4),
-                          (2, 8, 2, 64, 2)])
-def test_qk_rope_decode_attention_equals_two_launch(batch, q_heads, kv_heads, length, splits):
-    """fb_qk_rope_decode_attention (QK-norm + RoPE + KV append inside the cluster-form decode
-    attention) gives the same output and cache bits as fb_qk_norm_rope_append followed by
-    fb_decode_attention, from bf16 or split-partial qkv input; slots other than the position keep
-    their contents. Where the cluster form does not apply it launches nothing (FB_ERR_SHAPE)."""
-    from kernels._native import lib, ptr, stream, check
-    from kernels.decode_attention import attend
-    g = torch.Generator().manual_seed(batch * 1000 + length)
-    d = 128
-    capacity, pos = length + 8, length - 1
-    width = (q_heads + 2 * kv_heads) * d
-    if splits:
-        packed = (torch.randn(splits, batch, width, generator=g) * 0.5).to(DEV)
+@pytest.mark.parametrize("splits", [0, 6, 16])
+def test_qk_rope_cache_bit_exact_at_config4_shapes(splits):
+    """The decode-step K cache append at the Qwen3-8B shapes (batch 16, 32/8 heads, D 128, one
+    shared position in an 8200-slot cache, whole RoPE tables) against the oracle, bit for bit: K,
+    V and Q, from bf16 input and from fp32 split-K partials (6 is the TP1 qkv projection's split
+    count, 16 the TP8 shard's)."""
+    g = torch.Generator().manual_seed(100 + splits)
+    batch, hq, hkv, dim, capacity = 16, 32, 8, 128, 8200
+    width = (hq + 2 * hkv) * dim
+    if splits == 0:
+        packed = (torch.randn(batch, 1, width, generator=g) * 3).bfloat16()
     else:
-        packed = torch.randn(batch, width, generator=g).bfloat16().to(DEV)
-    q_gain = (1 + 0.1 * torch.randn(d, generator=g)).bfloat16().to(DEV)
-    k_gain = (1 + 0.1 * torch.randn(d, generator=g)).bfloat16().to(DEV)
-    cos = torch.randn(capacity, d, generator=g).bfloat16().to(DEV)
-    sin = torch.randn(capacity, d, generator=g).bfloat16().to(DEV)
-    keys0 = torch.randn(batch, kv_heads, capacity, d, generator=g).bfloat16().to(DEV)
-    values0 = torch.randn(batch, kv_heads, capacity, d, generator=g).bfloat16().to(DEV)
-    position = torch.tensor([pos], dtype=torch.int64, device=DEV)
-    scale = 1 / math.sqrt(d)
-    # two launches
-    keys2, values2 = keys0.clone(), values0.clone()
-    query = torch.empty(batch, 1, q_heads, d, dtype=torch.bfloat16, device=DEV)
-    check(lib.fb_qk_norm_rope_append(ptr(packed), splits, ptr(q_gain), ptr(k_gain), 1e-6, 1e-6, ptr(cos), ptr(sin),
-                                     ptr(position), None, ptr(query), ptr(keys2), ptr(values2), batch, 1, q_heads,
-                                     kv_heads, d, capacity, 0, 1, stream()), "fb_qk_norm_rope_append")
-    out2 = attend(query.view(batch, q_heads, 1, d), keys2, values2, position, scale)
-    # one launch
-    keys1, values1 = keys0.clone(), values0.clone()
-    out1 = torch.empty(batch, 1, q_heads, d, dtype=torch.bfloat16, device=DEV)
-    check(lib.fb_qk_rope_decode_attention(ptr(packed), splits, ptr(q_gain), ptr(k_gain), 1e-6, 1e-6, ptr(cos),
-                                          ptr(sin), ptr(position), ptr(keys1), ptr(values1), ptr(out1), batch,
-                                          q_heads, kv_heads, d, capacity, scale, stream()),
-          "fb_qk_rope_decode_attention")
+        packed = torch.randn(splits, batch, width, generator=g) * 0.7
+    q_gain = (1 + 0.1 * torch.randn(dim, generator=g)).bfloat16()
+    k_gain = (1 + 0.1 * torch.randn(dim, generator=g)).bfloat16()
+    keys = torch.randn(batch, hkv, capacity, dim, generator=g).bfloat16()
+    values = torch.randn(batch, hkv, capacity, dim, generator=g).bfloat16()
+    position = torch.tensor([8191], dtype=torch.int64)
+    inv = 1.0 / (1e6 ** (torch.arange(0, dim, 2).float() / dim))
+    angle = torch.arange(capacity).float()[:, None] * inv[None, :]
+    angle = torch.cat((angle, angle), -1)
+    cos, sin = angle.cos().bfloat16(), angle.sin().bfloat16()
+    ok, ov = keys.clone(), values.clone()
+    expect_q = opw.qk_rope_cache(packed, q_gain, k_gain, 1e-6, 1e-6, cos, sin, position, ok, ov, hq,
+                                 rows=False, phases=torch.zeros(batch, 1, dtype=torch.int64))
+    from kernels._native import check, lib, ptr, stream
+    # device copies held in names until the kernel has run (a temporary's memory could be reused)
+    kd, vd, pd = keys.to(DEV), values.to(DEV), packed.to(DEV)
+    qg, kg, cd, sd, posd = q_gain.to(DEV), k_gain.to(DEV), cos.to(DEV), sin.to(DEV), position.to(DEV)
+    query = torch.empty(batch, 1, hq, dim, dtype=torch.bfloat16, device=DEV)
+    # the decode step's call: mode 0 (one shared position), whole cos/sin tables
+    check(lib.fb_qk_norm_rope_append(ptr(pd), splits, ptr(qg), ptr(kg), 1e-6, 1e-6, ptr(cd), ptr(sd), ptr(posd),
+                                     None, ptr(query), ptr(kd), ptr(vd), batch, 1, hq, hkv, dim, capacity, 0, 1,
+                                     stream()), "fb_qk_norm_rope_append")
     torch.cuda.synchronize()
-    assert torch.equal(keys1, keys2) and torch.equal(values1, values2)
-    assert torch.equal(out1, out2)
-    assert torch.isfinite(out1.float()).all()
-    written = torch.zeros(capacity, dtype=torch.bool)
-    written[pos] = True
-    assert torch.equal(keys1[:, :, ~written.to(DEV)], keys0[:, :, ~written.to(DEV)])
-
-
-def test_qk_rope_decode_attention_refuses_non_cluster_shapes():
-    """Many (row, KV head) pairs (the persistent form's regime) or head_dim 64: FB_ERR_SHAPE,
-    nothing launched, the cache untouched."""
-    from kernels._native import lib, ptr, stream
-    d, capacity = 128, 72
-    keys = torch.zeros(16, 8, capacity, d, dtype=torch.bfloat16, device=DEV)
-    packed = torch.zeros(16, 48 * d, dtype=torch.bfloat16, device=DEV)
-    gain = torch.ones(d, dtype=torch.bfloat16, device=DEV)
-    table = torch.zeros(capacity, d, dtype=torch.bfloat16, device=DEV)
-    out = torch.empty(16, 1, 32, d, dtype=torch.bfloat16, device=DEV)
-    position = torch.tensor([5], dtype=torch.int64, device=DEV)
-    status = lib.fb_qk_rope_decode_attention(ptr(packed), 0, ptr(gain), ptr(gain), 1e-6, 1e-6, ptr(table), ptr(table),
-                                             ptr(position), ptr(keys), ptr(keys), ptr(out), 16, 32, 8, d, capacity,
-                                             0.088, stream())
-    assert status == -2
-    torch.cuda.synchronize()
-    assert bool((keys == 0).all())
+    got_q = query.cpu()
+    for name, got, want in (("keys", kd.cpu(), ok), ("values", vd.cpu(), ov), ("query", got_q, expect_q)):
+        differ = (got != want).nonzero()
+        assert differ.numel() == 0, f"{name}: {differ.shape[0]} elements differ, first {differ[:4].tolist()}"
