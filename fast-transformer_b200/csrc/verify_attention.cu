@@ -17,8 +17,10 @@
 //    with the fp32 accumulator in TMEM (double-buffered). Q sits in shared memory in the same
 //    swizzled K-major layout, written once by the CTA.
 //  * Eight softmax warps (TMEM lane quarter x half of the member columns; one token per
-//    thread, 16 member columns) reduce column maxima with a shuffle transpose-reduce and
-//    shared memory, and write P as bf16 into a K-major swizzled tile (double-buffered).
+//    thread, up to 16 member columns) reduce column maxima with a shuffle transpose-reduce and
+//    shared memory, and write P as bf16 into a K-major swizzled tile (double-buffered). Column c of the
+//    32-member group holds member 2*(c % 16) + c / 16, so the live members split evenly over
+//    the two halves (config 5's 20 members: 10 + 10) and dead columns are skipped.
 //  * O^T_tile = V^T * P^T is a second tcgen05.mma chain (M = 128 dims, N = 32 members,
 //    K = 128 tokens) with V read in place as an MN-major operand; each softmax thread (one dim)
 //    folds the tile into its fp32 running output with the softmax correction, one tile behind
@@ -60,6 +62,10 @@ struct Params {
 constexpr uint32_t kIdescS = tc::idesc_bf16(kTile, kMembers, false, false);
 constexpr uint32_t kIdescO = tc::idesc_bf16(kTile, kMembers, true, false);
 using tc::ex2_approx;
+
+// Column c of a 32-member group holds member 2 * (c % 16) + c / 16: even members in the first
+// half of the columns, odd members in the second.
+__device__ __forceinline__ int column_member(int c) { return 2 * (c % kHalf) + c / kHalf; }
 
 // Column-wise reduction of a 32x16 block held one row per lane: afterwards lanes c and c+16
 // hold the reduction of column c over all 32 rows (shuffle transpose-reduce, 16 shuffles).
@@ -169,11 +175,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           make_uint4(0, 0, 0, 0);
     }
   }
-  // Q members [group0, group0 + 32) of this (row, KV head) into the swizzled K-major tile;
-  // rows past the real members, and dims past D, are zero.
+  // Q members [group0, group0 + 32) of this (row, KV head) into the swizzled K-major tile, row
+  // r holding member column_member(r); rows past the real members, and dims past D, are zero.
   for (int e = tid; e < kMembers * 16; e += blockDim.x) {
     const int r = e / 16, c16 = e % 16;  // member row, 16-byte chunk of the 128-dim layout
-    const int m = group0 + r;
+    const int m = group0 + column_member(r);
     uint4 v = make_uint4(0, 0, 0, 0);
     if (m < members && c16 * 8 < D) {
       const int t = m / G, g = m % G;
@@ -184,7 +190,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     *reinterpret_cast<uint4*>(q_s + (c16 >> 3) * (kMembers * 128) + sw128(r, c16 & 7)) = v;
   }
   if (tid < kMembers) {
-    const int m = group0 + tid;
+    const int m = group0 + column_member(tid);
     const int t = m / G;
     const bool live = m < members;
     const bool chained = live && t < p.chain[b];
@@ -283,6 +289,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = quarter * 32 + lane;  // token of the S^T tile, dim of the O^T tile
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const int col0 = half * kHalf;
+    // live columns of this half: members 2*c + half < members - group0
+    const int group_live = min(kMembers, members - group0);
+    const int live = max(0, min(kHalf, (group_live - half + 1) / 2));
     float o[kHalf], l[kHalf], corr_prev[kHalf], run_max[kHalf];
 #pragma unroll
     for (int c = 0; c < kHalf; ++c) {
@@ -338,6 +347,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // after one barrier every thread folds the four quarters and its running max itself
       // (all threads of a column half compute the same values). red is double-buffered by
       // tile parity: the next write to this half happens after the next tile's barrier.
+      // (a single-instruction redux.sync.max.f32 per column measured slower on B200: config 5
+      // 55.7 against 43 us)
       const float wmax = transpose_reduce16<true>(sc, lane);
       float* rq = red + x * 4 * kMembers;
       if (lane < kHalf) rq[quarter * kMembers + col0 + lane] = wmax;
@@ -368,9 +379,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t pcol = (row >> 6) * (kMembers * 128) + (row & 7) * 2;
 #pragma unroll
       for (int c = 0; c < kHalf; ++c) {
-        const float pv = ex2_approx(sc[c] - piv[c]);
-        l[c] = l[c] * corr[c] + pv;
-        *reinterpret_cast<__nv_bfloat16*>(pt + pcol + sw128(col0 + c, (row & 63) >> 3)) = __float2bfloat16_rn(pv);
+        if (c < live) {  // dead columns only ever reach their own, unstored, outputs
+          const float pv = ex2_approx(sc[c] - piv[c]);
+          l[c] = l[c] * corr[c] + pv;
+          *reinterpret_cast<__nv_bfloat16*>(pt + pcol + sw128(col0 + c, (row & 63) >> 3)) = __float2bfloat16_rn(pv);
+        }
       }
       if (!in_range && half == 0) {
         // V row past the visible range: zero it so stale values never meet a zero weight.
@@ -413,8 +426,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int d = row;
 #pragma unroll
       for (int c = 0; c < kHalf; ++c) {
-        const int m = group0 + col0 + c;
-        if (m >= members || d >= D) continue;
+        const int m = group0 + 2 * c + half;  // column col0 + c
+        if (c >= live || d >= D) continue;
         const int mc = col0 + c;
         const float L = red[mc] + red[kMembers + mc] + red[2 * kMembers + mc] + red[3 * kMembers + mc];
         const int t = m / G, g = m % G;

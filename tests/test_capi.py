@@ -53,10 +53,11 @@ def test_host_validation_without_gpu():
     assert lib.fb_linear(p, p, p, 4, 128, 4096, 0, 9, null) == -2     # finished tile: a cluster of <= 8 splits
     assert lib.fb_linear_finished_splits(16, 3072, 4096) <= 8
     assert lib.fb_linear_finished_splits(64, 151936, 4096) <= 8
-    # cluster-shape override: powers of two up to 16, ring depth 2-4; (0, 0) restores automatic
-    assert lib.fb_decode_attention_cluster_shape(3, 2) == -1
+    # cluster-shape override: 2 to 16 CTAs, ring depth 2-4; (0, 0) restores automatic
+    assert lib.fb_decode_attention_cluster_shape(1, 2) == -1
     assert lib.fb_decode_attention_cluster_shape(8, 5) == -1
-    assert lib.fb_decode_attention_cluster_shape(32, 2) == -1
+    assert lib.fb_decode_attention_cluster_shape(17, 2) == -1
+    assert lib.fb_decode_attention_cluster_shape(9, 4) == 0
     assert lib.fb_decode_attention_cluster_shape(0, 0) == 0
     assert lib.fb_swiglu(p, 1, p, 4, 12, null) == -2                     # width % 8
     assert lib.fb_add_rmsnorm(p, 1, p, p, p, p, 4, 70000, 1e-6, null) == -2  # row too wide (> 65536)

@@ -141,7 +141,7 @@ def test_decode_attention_cluster_form(batch, q_heads, kv_heads, dim, length):
     assert torch.equal(cluster, again)  # deterministic
 
 
-@pytest.mark.parametrize("shape", [(2, 2), (4, 4), (8, 2), (8, 3), (16, 2), (16, 3)])
+@pytest.mark.parametrize("shape", [(2, 2), (4, 4), (8, 2), (8, 3), (16, 2), (16, 3), (9, 4), (6, 3), (13, 2)])
 def test_decode_attention_cluster_shapes(shape):
     """Every cluster-form launch shape (cluster size x ring depth, fb_decode_attention_cluster_shape)
     against the fp32 reference at a TP8 shard (16 rows x 1 KV head x 4 query heads, 8193 slots,
@@ -165,6 +165,28 @@ def test_decode_attention_cluster_shapes(shape):
             lib.fb_decode_attention_cluster_shape(0, 0)
         assert torch.isfinite(out.float()).all()
         torch.testing.assert_close(out.float(), expect, atol=2e-2, rtol=2e-2)
+
+
+def test_decode_attention_forced_shape_beyond_one_wave_is_refused():
+    """A forced cluster shape whose clusters cannot all be resident at once (16 pairs x clusters
+    of 16 CTAs with the one-CTA-per-SM ring: 256 CTAs) returns FB_ERR_SHAPE and launches nothing:
+    the output keeps its sentinel."""
+    from kernels._native import lib, ptr, stream
+    from kernels.decode_attention import _ctas, workspace_bytes
+    q, k, v, position = _ragged(16, 4, 1, 128, [2048] * 16, seed=77)
+    shared = position[:1].contiguous()
+    out = torch.full((16, 1, 4, 128), 3.0, dtype=torch.bfloat16, device=DEV)
+    ctas = _ctas((q.device, 16, 1, k.shape[2], 128))
+    ws = torch.zeros(workspace_bytes(16, 4, 1, 128, ctas), dtype=torch.uint8, device=DEV)
+    assert lib.fb_decode_attention_cluster_shape(16, 4) == 0
+    try:
+        status = lib.fb_decode_attention(ptr(q), ptr(k), ptr(v), ptr(shared), 0, ptr(out), ptr(ws), ws.numel(), 16, 4,
+                                         1, 128, k.shape[2], 0.088, ctas, stream())
+    finally:
+        lib.fb_decode_attention_cluster_shape(0, 0)
+    torch.cuda.synchronize()
+    assert status == -2
+    assert bool((out == 3.0).all())
 
 
 def test_decode_attention_graph_capture_and_determinism():
@@ -400,9 +422,10 @@ def test_fused_argmax_equals_projection_then_argmax():
 
 
 def test_decode_attention_fused_equals_two_launch_and_counters_reset():
-    """fb_decode_attention (persistent form, last CTA merges) equals fb_decode_attention_partials
-    + fb_decode_attention_combine bit for bit, and leaves its per-pair counters at zero. Per-row
-    positions (two or more rows) keep every call on the persistent form."""
+    """fb_decode_attention (persistent form: dynamically claimed chunks, the pair's last chunk
+    merges) equals fb_decode_attention_partials + fb_decode_attention_combine bit for bit, and
+    leaves its per-pair and claim counters at zero. Per-row positions (two or more rows) keep
+    every call on the persistent form."""
     from kernels.decode_attention import _ctas, attend, workspace_bytes
     for lengths, q_heads in (([1, 700, 8192, 65], 32), ([30000, 20001], 16), ([300, 301, 302, 303, 1, 2, 3, 4], 16)):
         q, k, v, position = _ragged(len(lengths), q_heads, 8, 128, lengths, seed=sum(lengths))
@@ -416,7 +439,7 @@ def test_decode_attention_fused_equals_two_launch_and_counters_reset():
         torch.cuda.synchronize()
         assert torch.equal(fused, two)
         assert torch.equal(second, fused)
-        counters = again_ws[-len(lengths) * 8 * 4:].view(torch.int32)
+        counters = again_ws[-(len(lengths) * 8 + 2) * 4:].view(torch.int32)  # pair counters, claim counters
         assert int(counters.abs().sum()) == 0
 
 
