@@ -710,6 +710,38 @@ def main():
     del state
     torch.cuda.empty_cache()
 
+    # ---- N > 1: the same shard alone (no all-reduce; its consumers run as the single-rank
+    # add+RMSNorm), captured and replayed like the timed step. The rest of the step is the
+    # all-reduce traffic, its polling and the ranks' skew.
+    step_split = None
+    if world > 1:
+        alone = fdecode.DecodeState(weights, BATCH, PROMPT, 2 * total_steps + 2, device=device)
+        alone.cache.store.normal_()  # decode cost does not depend on the cache contents
+        alone.position.fill_(PROMPT)
+        with torch.inference_mode():
+            alone.decode()
+        alone.capture()
+        for _ in range(args.warmup):
+            alone.step()
+        barrier()
+        torch.cuda.synchronize()
+        a_start, a_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a_start.record()
+        for _ in range(args.steps):
+            alone.step()
+        a_end.record()
+        torch.cuda.synchronize()
+        barrier()
+        alone_ms = max_over_ranks(a_start.elapsed_time(a_end)) / args.steps
+        assert _native.device_error() == 0, "a kernel raised the device error word"
+        alone.release()
+        del alone
+        torch.cuda.empty_cache()
+        step_split = {"step_us": ms_per_step * 1e3, "shard_alone_us": alone_ms * 1e3,
+                      "allreduce_and_skew_us": (ms_per_step - alone_ms) * 1e3,
+                      "how": "shard alone = this rank's 1/N of every projection and KV head, no all-reduce, "
+                             "graph-replayed like the timed step; max over ranks"}
+
     if world > 1:
         barrier()
         torch.distributed.destroy_process_group()
@@ -725,9 +757,12 @@ def main():
     if clock:
         line["clocks"] = clock
     if world > 1:
-        line["allreduce"] = ("split-K partials summed by fb_reduce_push and stored as flagged fp32 words into every "
-                             "rank's symmetric-memory receive buffer by NVLink peer stores; the consumer polls, sums "
-                             "the ranks in order and applies add+RMSNorm")
+        line["allreduce"] = ("owner-computes over NVLink peer stores: fb_reduce_scatter_push sums the projection's "
+                             "split-K partials and stores each fp32 value as a flagged word only to the rank that "
+                             "owns its column slice; fb_allreduce_add_rmsnorm sums the ranks in rank order per slice, "
+                             "adds the residual, all-gathers the summed bf16 rows and per-slice sums of squares, and "
+                             "applies the RMSNorm on every rank")
+        line["step_split"] = step_split
 
     if world == 1 and not args.no_sweep:
         line["attention_sweep"] = attention_sweep(peak)

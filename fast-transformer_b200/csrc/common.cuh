@@ -273,7 +273,10 @@ inline int launch_ex(void (*kernel)(Params...), dim3 grid, dim3 block, size_t sm
     cfg.numAttrs = 2;
   }
   cfg.attrs = attr;
-  if (cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...) != cudaSuccess) return FB_ERR_LAUNCH;
+  if (cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...) != cudaSuccess) {
+    cudaGetLastError();  // a refused launch must not be reported again by the next launch's check
+    return FB_ERR_LAUNCH;
+  }
   return check_launch();
 }
 }  // namespace fb

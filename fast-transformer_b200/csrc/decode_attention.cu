@@ -9,14 +9,11 @@
 // log-sum-exp combine (:119-127).
 //
 // B200 design (not a translation of the Triton kernel):
-//  * Work unit = one 64-token tile of one (row, KV head). Persistent form: each pair's tiles
-//    are cut into fixed chunks of K consecutive tiles (K from the launch's total tile count,
-//    at least 4); a persistent grid of `ctas` CTAs claims chunks dynamically (an atomic counter
-//    in the workspace; each CTA's first chunk is static and prefetched before the dependency
-//    wait), so SMs that stream faster take more chunks. A chunk is one online-softmax run; a
-//    chunk that covers a whole pair writes the final output directly, the others write their
-//    partial to the chunk's own slot and the pair's last chunk merges the slots in chunk
-//    order - the result does not depend on which CTA ran which chunk.
+//  * Work unit = one 64-token tile of one (row, KV head). All valid tiles of all pairs
+//    form one sequence (row-major, then head, then tile); a persistent grid of `ctas`
+//    CTAs takes equal contiguous slices of it, so ragged lengths balance across SMs.
+//    Consecutive tiles of the same pair inside a CTA are one "run" with one online
+//    softmax state; a run that covers a whole pair writes the final output directly.
 //  * Warp 4 (one elected lane) streams K and V tiles with 2-D TMA loads
 //    (CU_TENSOR_MAP_SWIZZLE_128B, no multicast) into an NS-stage mbarrier ring.
 //  * Warps 0-3 each take 16 tokens of a tile. Scores are computed transposed,
@@ -24,8 +21,10 @@
 //    the whole run), the probabilities are transposed in registers (movmatrix) and
 //    O^T[D x 8] += V^T * P^T accumulates in registers. The swizzled layout makes every
 //    ldmatrix conflict-free.
-//  * In the two-launch form the combine kernel re-derives each pair's chunk slots from the
-//    same lengths and merges them in chunk order: the same bits as the one-launch form.
+//  * Partials of runs that do not cover their pair go to slot (cta + pair) of the
+//    workspace; the combine kernel re-derives which CTAs touched each pair from the same
+//    integer partition, so no counters or atomics are needed and results are
+//    deterministic.
 #include <mutex>
 
 #include "common.cuh"
@@ -38,22 +37,17 @@ constexpr int kConsumerWarps = 4;  // 16 tokens each
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kMaxBatch = 1024;
 constexpr int kHeadsPad = 8;  // query heads per KV head, padded to the mma N
-constexpr int kMaxCtas = 512;          // persistent CTAs
-constexpr int kMinChunkTiles = 4;      // a chunk: up to K >= 4 consecutive tiles of one pair
-constexpr int kChunkSlotsPerCta = 32;  // workspace partial slots per persistent CTA
-constexpr int kMaxPairChunks = 512;    // chunks of one pair (the merge's weights in shared memory)
+constexpr int kMaxCtas = 512;  // persistent CTAs (runs per pair are bounded by this)
 
 struct Params {
   const __nv_bfloat16* q;  // [B, Hq, D]
   const int64_t* position;
   int per_row;
   __nv_bfloat16* out;  // [B, Hq, D]
-  float* acc;          // [slots, G, D], one slot per chunk
+  float* acc;          // [slots, G, D]
   float2* stats;       // [slots, G] (max, denominator)
-  int* counters;       // [B * Hkv] chunks finished per pair (fused merge); nullptr: no merge
-  int* claim;          // [2]: next chunk to claim (minus ctas), CTAs finished; zero between launches
+  int* counters;       // [B * Hkv] runs finished per pair (fused merge); nullptr: no merge
   int batch, q_heads, kv_heads, groups, capacity, ctas;
-  int budget;          // chunk slots: the chunk size keeps every launch within this many
   float scale_log2;
   unsigned* err;
 };
@@ -70,36 +64,43 @@ __device__ __forceinline__ int row_length(const int64_t* position, int per_row, 
 
 __device__ __forceinline__ int tiles_of(int len) { return (len + kTile - 1) / kTile; }
 
-// Chunk size (tiles) of a launch: at least kMinChunkTiles, large enough that all chunks fit
-// `budget` slots beside one extra slot per pair, and that no pair has more than
-// kMaxPairChunks chunks. A function of the rows' lengths only: every CTA and the combine
-// kernel derive the same layout.
-__device__ __forceinline__ int chunk_tiles(long long total_tiles, int max_pair_tiles, int budget) {
-  long long k = (total_tiles + budget - 1) / budget;
-  const long long k2 = (max_pair_tiles + kMaxPairChunks - 1) / kMaxPairChunks;
-  if (k < k2) k = k2;
-  return k < kMinChunkTiles ? kMinChunkTiles : static_cast<int>(k);
+// First tile of CTA i in a sequence of T tiles split over G CTAs.
+__device__ __forceinline__ long long slice_start(long long T, int i, int G) {
+  return (T * i) / G;
+}
+// The CTA whose slice contains tile t (largest i with slice_start(i) <= t).
+__device__ __forceinline__ int slice_owner(long long T, long long t, int G) {
+  return static_cast<int>(((t + 1) * G - 1) / T);
 }
 
-// Merge the `count` chunk partials of one (row, KV head) pair, slots first..first+count-1,
-// into its bf16 output: out = sum_i acc_i * exp2(m_i - M) / sum_i l_i * exp2(m_i - M) per
-// query head, chunks in order (deterministic). Partials are read through L2 (ld.global.cg):
-// other CTAs of this launch wrote them moments ago.
+// Merge the runs of CTAs lo..hi on one (row, KV head) pair into its bf16 output:
+// out = sum_i acc_i * exp2(m_i - M) / sum_i l_i * exp2(m_i - M) per query head, the runs
+// taken in increasing CTA order (deterministic). A CTA in [lo, hi] whose slice is empty
+// wrote nothing and gets weight 0. Partials are read through L2 (ld.global.cg): they were
+// written by other CTAs of this launch moments ago.
 template <int D, typename Bar>
-__device__ void merge_chunks(const Params& p, int pair, int first, int count, int tid, int threads, float* s_w,
-                             float* s_den, Bar bar) {
+__device__ void merge_pair(const Params& p, int pair, int lo, int hi, long long T, int tid,
+                           int threads, float* s_w, float* s_den, Bar bar) {
   const int G = p.groups;
+  const int runs = hi - lo + 1;
   const int warp = tid >> 5, lane = tid & 31, warps = threads >> 5;
+  // With at least one tile per CTA every slice is non-empty: skip the 64-bit tests.
+  const bool all_nonempty = T >= p.ctas;
   for (int g = warp; g < G; g += warps) {
     float M = -INFINITY;
-    for (int i = lane; i < count; i += 32) M = fmaxf(M, __ldcg(&p.stats[static_cast<size_t>(first + i) * G + g].x));
+    for (int i = lane; i < runs; i += 32)
+      if (all_nonempty || slice_start(T, lo + i, p.ctas) < slice_start(T, lo + i + 1, p.ctas))
+        M = fmaxf(M, __ldcg(&p.stats[static_cast<size_t>(lo + i + pair) * G + g].x));
     M = warp_max(M);
     const float piv = M == -INFINITY ? 0.f : M;
     float L = 0.f;
-    for (int i = lane; i < count; i += 32) {
-      const float2 st = __ldcg(&p.stats[static_cast<size_t>(first + i) * G + g]);
-      const float w = exp2f(st.x - piv);
-      L += st.y * w;
+    for (int i = lane; i < runs; i += 32) {
+      float w = 0.f;
+      if (all_nonempty || slice_start(T, lo + i, p.ctas) < slice_start(T, lo + i + 1, p.ctas)) {
+        const float2 st = __ldcg(&p.stats[static_cast<size_t>(lo + i + pair) * G + g]);
+        w = exp2f(st.x - piv);
+        L += st.y * w;
+      }
       s_w[i * kHeadsPad + g] = w;
     }
     L = warp_sum(L);
@@ -108,25 +109,24 @@ __device__ void merge_chunks(const Params& p, int pair, int first, int count, in
   bar();
   const int b = pair / p.kv_heads, h = pair % p.kv_heads;
   __nv_bfloat16* out = p.out + (static_cast<size_t>(b) * p.q_heads + h * G) * D;
-  constexpr int kBatch = 8;  // chunk loads in flight before their in-order adds
+  constexpr int kBatch = 8;  // run loads in flight before their in-order adds
   for (int e = tid; e < G * D; e += threads) {
     const int g = e / D, d = e % D;
-    const float* acc = p.acc + (static_cast<size_t>(first) * G + g) * D + d;
+    const float* acc = p.acc + (static_cast<size_t>(lo + pair) * G + g) * D + d;
     const size_t stride = static_cast<size_t>(G) * D;
     float O = 0.f;
-    for (int i0 = 0; i0 < count; i0 += kBatch) {
+    for (int i0 = 0; i0 < runs; i0 += kBatch) {
       float a[kBatch], w[kBatch];
 #pragma unroll
       for (int j = 0; j < kBatch; ++j) {
-        w[j] = i0 + j < count ? s_w[(i0 + j) * kHeadsPad + g] : 0.f;
+        w[j] = i0 + j < runs ? s_w[(i0 + j) * kHeadsPad + g] : 0.f;
         a[j] = w[j] != 0.f ? __ldcg(acc + (i0 + j) * stride) : 0.f;
       }
 #pragma unroll
       for (int j = 0; j < kBatch; ++j)
         if (w[j] != 0.f) O += a[j] * w[j];
     }
-    const float L = s_den[g];
-    out[e] = __float2bfloat16_rn(L > 0.f ? O / L : 0.f);
+    out[e] = __float2bfloat16_rn(O / s_den[g]);
   }
 }
 
@@ -298,29 +298,13 @@ struct Smem {
   static constexpr int kStagesBytes = NS * kStageBytes;
   static constexpr int kRedO = kConsumerWarps * D * kHeadsPad * 4;  // O^T partials per warp
   static constexpr int kRedML = kConsumerWarps * kHeadsPad * 2 * 4;
-  static constexpr int kCum = ((kMaxBatch + 1) * 4 + 15) & ~15;  // tile prefix per row
-  static constexpr int kCCum = kCum;                              // chunk prefix per row
-  static constexpr int kTags = NS * 16;                           // int4 per stage: chunk, tile, pair, flags
+  static constexpr int kCum = ((kMaxBatch + 1) * 4 + 15) & ~15;  // keeps the mbarriers 8-byte aligned
   static constexpr int kBars = 2 * NS * 8;
   static constexpr int kMisc = 64;
-  static constexpr int kMerge = kMaxPairChunks * kHeadsPad * 4 + kHeadsPad * 4;  // chunk weights + denominators
-  static constexpr int kTotal = 1024 + kStagesBytes + kRedO + kRedML + kCum + kCCum + kTags + kBars + kMisc + kMerge;
-  static_assert((kStagesBytes + kRedO + kRedML + kCum + kCCum + kTags) % 16 == 0, "mbarrier alignment");
+  static constexpr int kMerge = kMaxCtas * kHeadsPad * 4 + kHeadsPad * 4;  // run weights + denominators
+  static constexpr int kTotal = 1024 + kStagesBytes + kRedO + kRedML + kCum + kBars + kMisc + kMerge;
+  static_assert((kStagesBytes + kRedO + kRedML + kCum) % 16 == 0, "mbarrier alignment");
 };
-
-// Tag flags: first tile of its chunk, last tile of its chunk, the chunk covers its whole pair.
-constexpr int kFirst = 1, kLast = 2, kWhole = 4;
-constexpr int kEndChunk = -1;
-
-// Row of chunk c: the largest b with ccum[b] <= c (ccum[0] = 0, ccum[B] = total chunks).
-__device__ __forceinline__ int chunk_row(const int* ccum, int B, int c) {
-  int lo = 0, hi = B - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (ccum[mid] <= c) lo = mid; else hi = mid - 1;
-  }
-  return lo;
-}
 
 template <int D, int NS>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -335,54 +319,32 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* red_o = reinterpret_cast<float*>(base + S::kStagesBytes);
   float* red_ml = reinterpret_cast<float*>(base + S::kStagesBytes + S::kRedO);
   int* cum = reinterpret_cast<int*>(base + S::kStagesBytes + S::kRedO + S::kRedML);
-  int* ccum = cum + S::kCum / 4;
-  int4* tags = reinterpret_cast<int4*>(ccum + S::kCCum / 4);
-  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(tags) + S::kTags);
+  uint64_t* full = reinterpret_cast<uint64_t*>(base + S::kStagesBytes + S::kRedO + S::kRedML +
+                                               S::kCum);
   uint64_t* empty = full + NS;
-  int* misc = reinterpret_cast<int*>(empty + NS);  // [0] chunk tiles K, [1] total chunks, [4] abort, [5] last
+  int* misc = reinterpret_cast<int*>(empty + NS);  // [0..2] start b,h,j; [4] abort; [5..7] merge
   float* merge_w = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(misc) + S::kMisc);
-  float* merge_den = merge_w + kMaxPairChunks * kHeadsPad;
+  float* merge_den = merge_w + kMaxCtas * kHeadsPad;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int B = p.batch, Hkv = p.kv_heads, G = p.groups;
 
-  // ---- plan: per-row tile prefix sums, the chunk size, per-row chunk prefix sums ----
+  // ---- plan: per-row tile prefix sums, this CTA's tile slice and its first tile ----
   if (warp == 0) {
-    int running = 0, longest = 0;
+    int running = 0;
     if (lane == 0) cum[0] = 0;
     for (int b0 = 0; b0 < B; b0 += 32) {
-      const int b = b0 + lane;
-      const int n = b < B ? tiles_of(row_length(p.position, p.per_row, b, p.capacity)) : 0;
-      longest = max(longest, n);
+      int b = b0 + lane;
+      int n = b < B ? tiles_of(row_length(p.position, p.per_row, b, p.capacity)) : 0;
       int x = n;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        int y = __shfl_up_sync(0xffffffffu, x, o);
         if (lane >= o) x += y;
       }
       if (b < B) cum[b + 1] = running + x;
       running += __shfl_sync(0xffffffffu, x, 31);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) longest = max(longest, __shfl_xor_sync(0xffffffffu, longest, o));
-    const int K = chunk_tiles(static_cast<long long>(Hkv) * running, longest, p.budget);
-    int crun = 0;
-    if (lane == 0) ccum[0] = 0;
-    for (int b0 = 0; b0 < B; b0 += 32) {
-      const int b = b0 + lane;
-      int x = b < B ? Hkv * ((cum[b + 1] - cum[b] + K - 1) / K) : 0;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, x, o);
-        if (lane >= o) x += y;
-      }
-      if (b < B) ccum[b + 1] = crun + x;
-      crun += __shfl_sync(0xffffffffu, x, 31);
-    }
-    if (lane == 0) {
-      misc[0] = K;
-      misc[1] = crun;
     }
   }
   if (warp == kConsumerWarps && lane == 0) {
@@ -396,83 +358,89 @@ __global__ void __launch_bounds__(kThreads, 1)
     misc[4] = 0;
   }
   __syncthreads();
-  const int K = misc[0], chunks = misc[1];
 
   if (p.counters != nullptr && blockIdx.x == 0) {
     pdl_wait();  // `out` may still be read by an earlier kernel
-    // Rows with no valid slot get no chunk; the fused form writes their (empty) output.
+    // Rows with no valid slot get no run; the fused form writes their (empty) output.
     for (int b = 0; b < B; ++b)
       if (cum[b + 1] == cum[b])
         for (int e = threadIdx.x; e < p.q_heads * (int)D; e += blockDim.x)
           p.out[static_cast<size_t>(b) * p.q_heads * D + e] = __float2bfloat16_rn(0.f);
   }
+  const long long total = static_cast<long long>(Hkv) * cum[B];
+  const long long t0 = total > 0 ? slice_start(total, blockIdx.x, p.ctas) : 0;
+  const long long t1 = total > 0 ? slice_start(total, blockIdx.x + 1, p.ctas) : 0;
+  const int count = static_cast<int>(t1 - t0);
+  if (count <= 0) return;
+
+  if (warp == 0) {
+    for (int b0 = 0; b0 < B; b0 += 32) {
+      int b = b0 + lane;
+      bool hit = false;
+      if (b < B) {
+        long long lo = static_cast<long long>(Hkv) * cum[b];
+        long long hi = static_cast<long long>(Hkv) * cum[b + 1];
+        hit = lo <= t0 && t0 < hi;
+      }
+      unsigned m = __ballot_sync(0xffffffffu, hit);
+      if (m != 0) {
+        if (lane == __ffs(m) - 1) {
+          int n = cum[b + 1] - cum[b];
+          long long off = t0 - static_cast<long long>(Hkv) * cum[b];
+          misc[0] = b;
+          misc[1] = static_cast<int>(off / n);
+          misc[2] = static_cast<int>(off % n);
+        }
+        break;
+      }
+    }
+  }
+  __syncthreads();
+
   volatile int* abort_flag = &misc[4];
 
   if (warp == kConsumerWarps) {
-    // ===================== producer: one lane claims chunks and issues every TMA =====================
+    // ===================== producer: one lane issues every TMA =====================
     if (lane == 0) {
-      // The first chunk is static and its tiles below the position are fetched before the
-      // dependency wait; later chunks come from the workspace counter, which the previous
-      // launch may still use until it completes: claims follow the wait.
-      int cur = static_cast<int>(blockIdx.x) < chunks ? static_cast<int>(blockIdx.x) : chunks;
-      int nxt = -1;
+      int b = misc[0], h = misc[1], j = misc[2];
+      int n = cum[b + 1] - cum[b];
+      // Cache rows below a row's position were written by earlier steps, so the ring is
+      // filled before the dependency wait; the tile holding the row's newest slot (the
+      // previous kernel appends it) waits for the previous kernel.
       bool waited = false;
-      int k = 0;
-      while (cur < chunks && !*abort_flag) {
-        const int b = chunk_row(ccum, B, cur);
-        const int n = cum[b + 1] - cum[b];
-        const int cpp = (n + K - 1) / K;
-        const int r = cur - ccum[b];
-        const int h = r / cpp, ci = r % cpp;
-        const int j0 = ci * K, nt = min(K, n - j0);
-        bool ok = true;
-        for (int t = 0; t < nt; ++t, ++k) {
-          const int j = j0 + t;
-          const int s = k % NS;
-          // the tile holding the row's newest slot (the previous kernel appends it) waits
-          if (!waited && (k >= NS || j == n - 1)) {
-            pdl_wait();
-            waited = true;
-          }
-          if (waited && nxt < 0) nxt = p.ctas + atomicAdd(&p.claim[0], 1);  // claim ahead
-          if (k >= NS && !mbar_wait_bounded(&empty[s], ((k / NS) - 1) & 1)) {
+      for (int k = 0; k < count; ++k) {
+        const int s = k % NS;
+        if (!waited && (k >= NS || j == n - 1)) {
+          pdl_wait();
+          waited = true;
+        }
+        if (*abort_flag) break;
+        if (k >= NS) {
+          if (!mbar_wait_bounded(&empty[s], ((k / NS) - 1) & 1)) {
             raise_error(p.err, kErrTimeoutEmpty);
             *abort_flag = 1;
-            ok = false;
             break;
           }
-          tags[s] = make_int4(cur, j, b * Hkv + h,
-                              (t == 0 ? kFirst : 0) | (t == nt - 1 ? kLast : 0) | (cpp == 1 ? kWhole : 0));
-          uint8_t* kt = stages + s * S::kStageBytes;
-          uint8_t* vt = kt + S::kTileBytes;
-          const int row = (b * Hkv + h) * p.capacity + j * kTile;
-          mbar_arrive_expect_tx(&full[s], S::kStageBytes);
+        }
+        uint8_t* kt = stages + s * S::kStageBytes;
+        uint8_t* vt = kt + S::kTileBytes;
+        const int row = (b * Hkv + h) * p.capacity + j * kTile;
+        mbar_arrive_expect_tx(&full[s], S::kStageBytes);
 #pragma unroll
-          for (int bx = 0; bx < kBoxes; ++bx) {
-            tma_load_2d(kt + bx * kTile * 128, &kmap, &full[s], bx * 64, row);
-            tma_load_2d(vt + bx * kTile * 128, &vmap, &full[s], bx * 64, row);
+        for (int bx = 0; bx < kBoxes; ++bx) {
+          tma_load_2d(kt + bx * kTile * 128, &kmap, &full[s], bx * 64, row);
+          tma_load_2d(vt + bx * kTile * 128, &vmap, &full[s], bx * 64, row);
+        }
+        if (++j == n) {
+          j = 0;
+          if (++h == Hkv) {
+            h = 0;
+            do {
+              ++b;
+            } while (b < B && cum[b + 1] == cum[b]);
+            if (b < B) n = cum[b + 1] - cum[b];
           }
         }
-        if (!ok) break;
-        if (nxt < 0) {
-          if (!waited) {
-            pdl_wait();
-            waited = true;
-          }
-          nxt = p.ctas + atomicAdd(&p.claim[0], 1);
-        }
-        cur = nxt;
-        nxt = -1;
-      }
-      // end of work: one more stage carries the end tag (a plain arrive, no bytes)
-      const int s = k % NS;
-      if (!*abort_flag && k >= NS && !mbar_wait_bounded(&empty[s], ((k / NS) - 1) & 1)) {
-        raise_error(p.err, kErrTimeoutEmpty);
-        *abort_flag = 1;
-      }
-      if (!*abort_flag) {
-        tags[s] = make_int4(kEndChunk, 0, 0, 0);
-        mbar_arrive(&full[s]);
       }
     }
     return;
@@ -482,84 +450,118 @@ __global__ void __launch_bounds__(kThreads, 1)
   pdl_wait();  // the query rows come from the previous kernel
   pdl_trigger();
   const int ctid = threadIdx.x;  // 0..127
+
+  int b = misc[0], h = misc[1], j = misc[2];
+  int n = cum[b + 1] - cum[b];
+  int len = row_length(p.position, p.per_row, b, p.capacity);
+  int run_first = j;
+
   WarpAcc<D> acc;
-  int len = 0;
+  start_pair<D>(acc, p, b, h, lane);
+
   const float sl2 = p.scale_log2;
-  for (int k = 0;; ++k) {
+  bool aborted = false;
+
+  for (int k = 0; k < count; ++k) {
     const int s = k % NS;
     if (!mbar_wait_bounded(&full[s], (k / NS) & 1)) {
       raise_error(p.err, kErrTimeoutFull);
       *abort_flag = 1;
+      aborted = true;
     }
-    if (*abort_flag) break;
-    const int4 tag = tags[s];
-    if (tag.x == kEndChunk) break;
-    const int pair = tag.z, b = pair / Hkv, h = pair % Hkv;
-    if (tag.w & kFirst) {
-      len = row_length(p.position, p.per_row, b, p.capacity);
-      start_pair<D>(acc, p, b, h, lane);
+    if (aborted || *abort_flag) {
+      aborted = true;
+      break;
     }
     uint8_t* kt = stages + s * S::kStageBytes;
-    attend_tile<D>(acc, kt, kt + S::kTileBytes, tag.y * kTile, len, warp, lane, sl2);
+    attend_tile<D>(acc, kt, kt + S::kTileBytes, j * kTile, len, warp, lane, sl2);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
-    if (!(tag.w & kLast)) continue;
 
-    // ---- the chunk is complete: its output, or its partial and (last chunk) the pair's merge ----
-    park_warp<D>(acc, red_o, red_ml, warp, lane, G);
-    asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
-    const int chunk = tag.x;
-    for (int e = ctid; e < G * D; e += kConsumerWarps * 32) {
-      const int gq = e / D, d = e % D;
-      float M, L, O;
-      combine_warps<D>(red_o, red_ml, gq, d, M, L, O);
-      if (tag.w & kWhole) {
-        p.out[(static_cast<size_t>(b) * p.q_heads + h * G + gq) * D + d] = __float2bfloat16_rn(O / L);
-      } else {
-        p.acc[(static_cast<size_t>(chunk) * G + gq) * D + d] = O;
-        if (d == 0) p.stats[static_cast<size_t>(chunk) * G + gq] = make_float2(M, L);
+    // ---- advance; finalize the run when the pair changes or the slice ends ----
+    const int cur_b = b, cur_h = h, cur_first = run_first, cur_last = j, cur_n = n;
+    bool run_end = (k == count - 1);
+    if (++j == n) {
+      j = 0;
+      run_end = true;
+      if (++h == Hkv) {
+        h = 0;
+        do {
+          ++b;
+        } while (b < B && cum[b + 1] == cum[b]);
       }
     }
-    if (!(tag.w & kWhole) && p.counters != nullptr) {
-      // Publish this chunk, count it, and let the pair's last chunk merge them all.
-      const int n = cum[b + 1] - cum[b];
-      const int cpp = (n + K - 1) / K;
-      __threadfence();
+    if (run_end) {
+      park_warp<D>(acc, red_o, red_ml, warp, lane, G);
       asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
-      if (ctid == 0) {
-        const int done = atomicAdd(&p.counters[pair], 1);
-        const int last = done == cpp - 1;
-        if (last) p.counters[pair] = 0;  // every chunk of this launch has counted: reset for the next
-        misc[5] = last;
+      const bool whole = cur_first == 0 && cur_last == cur_n - 1;
+      const int pair = cur_b * Hkv + cur_h;
+      const int slot = blockIdx.x + pair;
+      for (int e = ctid; e < G * D; e += kConsumerWarps * 32) {
+        const int gq = e / D, d = e % D;
+        float M, L, O;
+        combine_warps<D>(red_o, red_ml, gq, d, M, L, O);
+        if (whole) {
+          p.out[(static_cast<size_t>(cur_b) * p.q_heads + cur_h * G + gq) * D + d] =
+              __float2bfloat16_rn(O / L);
+        } else {
+          p.acc[(static_cast<size_t>(slot) * G + gq) * D + d] = O;
+          if (d == 0) p.stats[static_cast<size_t>(slot) * G + gq] = make_float2(M, L);
+        }
       }
-      asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
-      if (misc[5]) {
+      if (!whole && p.counters != nullptr) {
+        // Publish this run, count it, and let the pair's last run merge them all.
         __threadfence();
-        merge_chunks<D>(p, pair, ccum[b] + h * cpp, cpp, ctid, kConsumerWarps * 32, merge_w, merge_den,
-                        [] { asm volatile("bar.sync 1, 128;" ::: "memory"); });
+        asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+        if (ctid == 0) {
+          const long long first = static_cast<long long>(Hkv) * cum[cur_b] + static_cast<long long>(cur_h) * cur_n;
+          const int lo = slice_owner(total, first, p.ctas);
+          const int hi = slice_owner(total, first + cur_n - 1, p.ctas);
+          int runs = hi - lo + 1;
+          if (total < p.ctas) {  // some slices are empty: count the CTAs that really ran
+            runs = 0;
+            for (int i = lo; i <= hi; ++i)
+              runs += slice_start(total, i, p.ctas) < slice_start(total, i + 1, p.ctas);
+          }
+          const int done = atomicAdd(&p.counters[pair], 1);
+          const int last = done == runs - 1;
+          if (last) p.counters[pair] = 0;  // every run of this launch has counted: reset for the next
+          misc[5] = last;
+          misc[6] = lo;
+          misc[7] = hi;
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+        if (misc[5]) {
+          __threadfence();
+          merge_pair<D>(p, pair, misc[6], misc[7], total, ctid, kConsumerWarps * 32, merge_w,
+                        merge_den, [] { asm volatile("bar.sync 1, 128;" ::: "memory"); });
+        }
+      }
+      asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+      if (k != count - 1) {
+        n = cum[b + 1] - cum[b];
+        len = row_length(p.position, p.per_row, b, p.capacity);
+        run_first = j;
+        start_pair<D>(acc, p, b, h, lane);
       }
     }
-    asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
   }
-  // ---- the launch's last CTA resets the claim counter (every producer has stopped claiming) ----
-  asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
-  if (ctid == 0) {
-    __threadfence();
-    if (atomicAdd(&p.claim[1], 1) == static_cast<int>(gridDim.x) - 1) {
-      atomicExch(&p.claim[0], 0);
-      atomicExch(&p.claim[1], 0);
-    }
+  if (aborted) {
+    // Let copies already issued land before the CTA's shared memory is released.
+    __syncwarp();
   }
 }
 
-// One CTA per (row, KV head): merge the pair's chunk partials in chunk order (the two-launch
-// form). The chunk layout is re-derived from the same lengths as the partials kernel's.
+// One CTA per (row, KV head): merge the runs of the CTAs that shared the pair. The
+// contributing CTAs and their per-head softmax weights exp2(m_run - M) are resolved once
+// into shared memory; the weighted sum over runs is then a coalesced sweep over the
+// partial accumulators, in increasing CTA order (deterministic).
 constexpr int kCombineThreads = 256;
 
 template <int D>
 __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const Params p) {
-  __shared__ int s_before, s_total, s_n, s_longest, s_cbefore;
-  __shared__ float s_w[kMaxPairChunks * kHeadsPad];
+  __shared__ int s_before, s_total, s_n;
+  __shared__ float s_w[kMaxCtas * kHeadsPad];
   __shared__ float s_den[kHeadsPad];
   pdl_wait();
   pdl_trigger();
@@ -567,35 +569,33 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const P
   const int b = pair / p.kv_heads, h = pair % p.kv_heads;
   const int G = p.groups;
   if (threadIdx.x == 0) {
-    s_before = s_total = s_n = s_longest = s_cbefore = 0;
+    s_before = 0;
+    s_total = 0;
+    s_n = 0;
   }
   __syncthreads();
-  int total = 0, longest = 0;
+  int before = 0, total = 0;
   for (int r = threadIdx.x; r < p.batch; r += blockDim.x) {
     const int n = tiles_of(row_length(p.position, p.per_row, r, p.capacity));
     total += n;
-    longest = max(longest, n);
+    if (r < b) before += n;
     if (r == b) s_n = n;
   }
+  if (before) atomicAdd(&s_before, before);
   if (total) atomicAdd(&s_total, total);
-  if (longest) atomicMax(&s_longest, longest);
-  __syncthreads();
-  const int K = chunk_tiles(static_cast<long long>(p.kv_heads) * s_total, s_longest, p.budget);
-  int cbefore = 0;
-  for (int r = threadIdx.x; r < b; r += blockDim.x)
-    cbefore += p.kv_heads * ((tiles_of(row_length(p.position, p.per_row, r, p.capacity)) + K - 1) / K);
-  if (cbefore) atomicAdd(&s_cbefore, cbefore);
   __syncthreads();
   const int n = s_n;
-  const int cpp = (n + K - 1) / K;
+  const long long T = static_cast<long long>(p.kv_heads) * s_total;
   if (n == 0) {
     __nv_bfloat16* out = p.out + (static_cast<size_t>(b) * p.q_heads + h * G) * D;
     for (int e = threadIdx.x; e < G * D; e += blockDim.x) out[e] = __float2bfloat16_rn(0.f);
     return;
   }
-  if (cpp == 1) return;  // one chunk covered the pair and wrote the output itself
-  merge_chunks<D>(p, pair, s_cbefore + h * cpp, cpp, threadIdx.x, kCombineThreads, s_w, s_den,
-                  [] { __syncthreads(); });
+  const long long first = static_cast<long long>(p.kv_heads) * s_before + static_cast<long long>(h) * n;
+  const int lo = slice_owner(T, first, p.ctas);
+  const int hi = slice_owner(T, first + n - 1, p.ctas);
+  if (lo == hi) return;  // one run covered the pair and wrote the output itself
+  merge_pair<D>(p, pair, lo, hi, T, threadIdx.x, kCombineThreads, s_w, s_den, [] { __syncthreads(); });
 }
 
 
@@ -945,54 +945,44 @@ extern "C" int fb_decode_attention_cluster_shape(int cluster, int stages) {
   return FB_OK;
 }
 
-// Workspace layout: fp32 chunk partials [slots, G, D], their (max, denominator) [slots, G],
-// one counter per pair, then the claim counter and the finished-CTA counter. slots = the chunk
-// budget (slots_per_cta per persistent CTA) plus one per pair.
-static size_t workspace_layout(int batch, int q_heads, int kv_heads, int head_dim, int ctas, int slots_per_cta,
-                               size_t* acc_bytes, size_t* stats_bytes) {
-  const size_t G = q_heads / kv_heads;
-  const size_t slots = static_cast<size_t>(slots_per_cta) * ctas + static_cast<size_t>(batch) * kv_heads;
-  const size_t acc = ((slots * G * head_dim * sizeof(float)) + 255) & ~size_t(255);
-  const size_t stats = ((slots * G * sizeof(float2)) + 255) & ~size_t(255);
-  if (acc_bytes) *acc_bytes = acc;
-  if (stats_bytes) *stats_bytes = stats;
-  return acc + stats + static_cast<size_t>(batch) * kv_heads * sizeof(int) + 2 * sizeof(int);
-}
-
 extern "C" size_t fb_decode_attention_workspace(int batch, int q_heads, int kv_heads,
                                                 int head_dim, int ctas) {
   if (batch <= 0 || q_heads <= 0 || kv_heads <= 0 || head_dim <= 0 || ctas <= 0) return 0;
-  return workspace_layout(batch, q_heads, kv_heads, head_dim, ctas, kChunkSlotsPerCta, nullptr, nullptr);
+  const size_t G = q_heads / kv_heads;
+  const size_t slots = static_cast<size_t>(ctas) + static_cast<size_t>(batch) * kv_heads;
+  const size_t acc = ((slots * G * head_dim * sizeof(float)) + 255) & ~size_t(255);
+  const size_t stats = ((slots * G * sizeof(float2)) + 255) & ~size_t(255);
+  const size_t counters = static_cast<size_t>(batch) * kv_heads * sizeof(int);
+  return acc + stats + counters;
 }
 
 static int make_params(Params* p, const void* q, const int64_t* position, int per_row, void* out,
                        void* workspace, size_t workspace_bytes, int batch, int q_heads,
-                       int kv_heads, int head_dim, int capacity, float scale, int ctas, bool fused,
-                       int slots_per_cta = kChunkSlotsPerCta) {
+                       int kv_heads, int head_dim, int capacity, float scale, int ctas, bool fused) {
   int st = validate(batch, q_heads, kv_heads, head_dim, capacity);
   if (st != FB_OK) return st;
   if (position == nullptr || out == nullptr || workspace == nullptr || ctas <= 0) return FB_ERR_ARG;
   if (ctas > kMaxCtas) return FB_ERR_SHAPE;
-  size_t acc = 0, stats = 0;
-  const size_t need = workspace_layout(batch, q_heads, kv_heads, head_dim, ctas, slots_per_cta, &acc, &stats);
+  const size_t need = fb_decode_attention_workspace(batch, q_heads, kv_heads, head_dim, ctas);
   if (workspace_bytes < need) return FB_ERR_WORKSPACE;
+  const size_t G = q_heads / kv_heads;
+  const size_t slots = static_cast<size_t>(ctas) + static_cast<size_t>(batch) * kv_heads;
+  const size_t acc = ((slots * G * head_dim * sizeof(float)) + 255) & ~size_t(255);
+  const size_t stats = ((slots * G * sizeof(float2)) + 255) & ~size_t(255);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  int* counters = reinterpret_cast<int*>(ws + acc + stats);
   p->q = static_cast<const __nv_bfloat16*>(q);
   p->position = position;
   p->per_row = per_row ? 1 : 0;
   p->out = static_cast<__nv_bfloat16*>(out);
   p->acc = reinterpret_cast<float*>(ws);
   p->stats = reinterpret_cast<float2*>(ws + acc);
-  p->counters = fused ? counters : nullptr;
-  p->claim = counters + static_cast<size_t>(batch) * kv_heads;
+  p->counters = fused ? reinterpret_cast<int*>(ws + acc + stats) : nullptr;
   p->batch = batch;
   p->q_heads = q_heads;
   p->kv_heads = kv_heads;
   p->groups = q_heads / kv_heads;
   p->capacity = capacity;
   p->ctas = ctas;
-  p->budget = slots_per_cta * ctas;
   p->scale_log2 = static_cast<float>(static_cast<double>(scale) * 1.4426950408889634);
   p->err = error_word();
   return FB_OK;
@@ -1001,11 +991,11 @@ static int make_params(Params* p, const void* q, const int64_t* position, int pe
 static int launch_decode(const void* q, const void* k, const void* v, const int64_t* position,
                          int per_row, void* out, void* workspace, size_t workspace_bytes, int batch,
                          int q_heads, int kv_heads, int head_dim, int capacity, float scale,
-                         int ctas, void* stream, bool fused, int slots_per_cta = kChunkSlotsPerCta) {
+                         int ctas, void* stream, bool fused) {
   if (q == nullptr || k == nullptr || v == nullptr) return FB_ERR_ARG;
   Params p;
   int st = make_params(&p, q, position, per_row, out, workspace, workspace_bytes, batch, q_heads,
-                       kv_heads, head_dim, capacity, scale, ctas, fused, slots_per_cta);
+                       kv_heads, head_dim, capacity, scale, ctas, fused);
   if (st != FB_OK) return st;
   const uint64_t rows = static_cast<uint64_t>(batch) * kv_heads * capacity;
   CUtensorMap km, vm;
@@ -1069,14 +1059,13 @@ namespace attn {
 
 constexpr int kNoAllocMaxPairs = 512;  // batch * kv_heads
 constexpr int kNoAllocMaxCtas = 160;   // persistent CTAs used by this entry point
-constexpr int kNoAllocSlotsPerCta = 4; // chunk slots per CTA (a coarser chunk budget than the default)
-// Sized for the largest request accepted: (slots_per_cta * ctas + pairs) chunk slots of up to 8
-// heads x 128 dims of fp32 partials, their (max, sum) stats, one counter per pair and two claim
-// counters.
-constexpr size_t kNoAllocSlots = static_cast<size_t>(kNoAllocSlotsPerCta) * kNoAllocMaxCtas + kNoAllocMaxPairs;
-constexpr size_t kNoAllocScratchBytes = ((kNoAllocSlots * kHeadsPad * 128 * 4 + 255) & ~size_t(255)) +
-                                        ((kNoAllocSlots * kHeadsPad * 8 + 255) & ~size_t(255)) +
-                                        static_cast<size_t>(kNoAllocMaxPairs) * 4 + 2 * 4;
+// Sized for the largest request accepted: (ctas + pairs) run slots of up to 8 heads x 128
+// dims of fp32 partials, their (max, sum) stats, and one counter per pair.
+constexpr size_t kNoAllocScratchBytes =
+    ((static_cast<size_t>(kNoAllocMaxCtas + kNoAllocMaxPairs) * kHeadsPad * 128 * 4 + 255) &
+     ~size_t(255)) +
+    ((static_cast<size_t>(kNoAllocMaxCtas + kNoAllocMaxPairs) * kHeadsPad * 8 + 255) & ~size_t(255)) +
+    static_cast<size_t>(kNoAllocMaxPairs) * 4;
 
 // Every GPU that loads the library holds this array until the process exits. In host code
 // the name is only a stand-in: the device address comes from cudaGetSymbolAddress.
@@ -1113,17 +1102,16 @@ extern "C" int fb_decode_attention_noalloc(const void* q, const void* k, const v
   if (static_cast<long long>(batch) * kv_heads > kNoAllocMaxPairs) return FB_ERR_TOO_LARGE;
   int ctas = sm_count();
   if (ctas > kNoAllocMaxCtas) ctas = kNoAllocMaxCtas;
-  const size_t need = workspace_layout(batch, q_heads, kv_heads, head_dim, ctas, kNoAllocSlotsPerCta, nullptr,
-                                      nullptr);
-  if (need > kNoAllocScratchBytes) return FB_ERR_TOO_LARGE;
+  const size_t need = fb_decode_attention_workspace(batch, q_heads, kv_heads, head_dim, ctas);
+  if (need == 0 || need > kNoAllocScratchBytes) return FB_ERR_TOO_LARGE;
   void* scratch = noalloc_scratch();
   if (scratch == nullptr) return FB_ERR_LAUNCH;
-  // The per-pair and claim counters (the workspace's tail) must start at zero: clear them
-  // here, since the array keeps whatever the previous call left.
-  const size_t counters = static_cast<size_t>(batch) * kv_heads * sizeof(int) + 2 * sizeof(int);
+  // The per-pair counters (the workspace's tail) must start at zero: clear them here, since
+  // the array keeps whatever the previous call left.
+  const size_t counters = static_cast<size_t>(batch) * kv_heads * sizeof(int);
   if (cudaMemsetAsync(static_cast<uint8_t*>(scratch) + need - counters, 0, counters,
                       static_cast<cudaStream_t>(stream)) != cudaSuccess)
     return FB_ERR_LAUNCH;
   return launch_decode(q, k, v, position, per_row, out, scratch, need, batch, q_heads, kv_heads,
-                       head_dim, capacity, scale, ctas, stream, true, kNoAllocSlotsPerCta);
+                       head_dim, capacity, scale, ctas, stream, true);
 }

@@ -6,31 +6,32 @@
 // and query head hq, softmax(q . k_j * scale) over keys j <= t of KV head hq / G, times V,
 // with fp32 scores and accumulation and P rounded to bf16 for the value product.
 //
-// B200 design (one CTA per (pair of 128-query tiles, query head, row); heaviest pairs first):
-//  * The two query tiles A and B (256 consecutive queries) share every K/V tile. A TMA lane
-//    loads both Q tiles once and streams 128-key K tiles and V tiles through separate 2-stage
-//    rings (128-byte swizzle, no multicast).
-//  * A UMMA lane issues S_X = Q_X K^T (M = N = 128, K = D) into tile X's TMEM columns and
-//    O_X += P_X V (M = 128, N = D, K = 128 keys) with P_X read from TMEM - the softmax wrote it
-//    as bf16 pairs over S_X's first 64 columns - and V read MN-major from shared memory. Per key
-//    tile j the order is O_A(j), S_A(j+1), O_B(j), S_B(j+1): one tile's softmax overlaps the
-//    other tile's products, and each commit also covers every product issued before it.
-//  * Two softmax warpgroups (tile A: warps 0-3, tile B: warps 4-7), one thread per query row
-//    holding its 128 scores in registers: row max, lazy rescale (the pivot moves only when the
-//    max grows by more than 8 in log2 units; O is then rescaled in TMEM), P = 2^(s - pivot)
-//    rounded to bf16, row sum. Tiles below the diagonal skip the masks.
+// B200 design (one CTA per (128-query tile, query head, row); heavy tiles first):
+//  * A TMA lane loads the Q tile once and streams 128-key K and V tiles (128-byte swizzle,
+//    no multicast) through a 2-stage ring.
+//  * A UMMA lane issues S = Q K^T (M = 128 queries, N = 128 keys, K = D) into one of two TMEM
+//    buffers and O += P V (N = 128 dims, K = 128 keys; V read MN-major) into a TMEM
+//    accumulator; S of tile j+1 runs while the softmax warps work on tile j.
+//  * Eight softmax warps, two per query row (64 keys each, exchanging row maxima and sums
+//    through spare TMEM columns): row max, P = 2^(s - m) rounded to bf16 into a K-major
+//    swizzled tile in shared memory (double-buffered), row sum. The pivot m only moves when a
+//    row's max grows by more than 8 (P <= 2^8 otherwise); then the row's O in TMEM is
+//    rescaled in place after the previous product completes. Tiles below the diagonal skip
+//    the masks.
 //  * Every mbarrier wait is bounded; TMEM is freed on every path.
 #include "tcgen05.cuh"
 
 namespace fb {
 namespace prefill {
 
-constexpr int kTile = 128;          // queries per tile and keys per K/V tile
-constexpr int kSoftmaxWarps = 8;    // warps 0-3: tile A rows, 4-7: tile B rows
+constexpr int kTile = 128;      // queries per CTA tile and keys per K/V tile
+constexpr int kSoftmaxWarps = 8;  // warp w: query rows 32*(w%4).., key half / O-column half w/4
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr int kThreads = 10 * 32;
-constexpr int kTmemCols = 512;      // S_A, S_B (128 each), O_A, O_B (D each)
+constexpr int kTmemCols = 512;  // S double buffer (2 x 128) + O (<= 128) + row exchange columns
+constexpr int kTmemO = 256;
+constexpr int kTmemXchg = 384;  // [parity][half] row maxima, then [half] row sums
 constexpr float kRescaleAbove = 8.0f;  // log2 units
 
 struct Params {
@@ -44,57 +45,24 @@ template <int D>
 struct Smem {
   static constexpr int kBox = kTile * 128;            // 128 rows x 64 bf16 (one 128-byte row each)
   static constexpr int kTileBytes = (D / 64) * kBox;  // 128 rows x D (Q, K or V)
-  static constexpr int kQOff = 0;                     // Q_A, Q_B
-  static constexpr int kKOff = 2 * kTileBytes;        // K ring, 2 stages
-  static constexpr int kVOff = kKOff + 2 * kTileBytes;  // V ring, 2 stages
-  static constexpr int kBarOff = kVOff + 2 * kTileBytes;
+  static constexpr int kPBytes = 2 * kBox;            // 128 query rows x 128 keys
+  static constexpr int kStageBytes = 2 * kTileBytes;  // K then V
+  static constexpr int kStages = 2;
+  static constexpr int kQOff = 0;
+  static constexpr int kStageOff = kTileBytes;
+  static constexpr int kPOff = kStageOff + kStages * kStageBytes;  // two P tiles
+  static constexpr int kBarOff = kPOff + 2 * kPBytes;
   static constexpr int kBars = 16;
   static constexpr int kTotal = 1024 + kBarOff + kBars * 8 + 16;
   static_assert(kTotal <= 227 * 1024, "prefill shared memory");
 };
 
-// Packs two fp32 values as bf16 (lo, hi) into one 32-bit TMEM column.
-__device__ __forceinline__ uint32_t pack2(float lo, float hi) { return pack_bf16x2(lo, hi); }
-
-// Writes 32 consecutive 32-bit columns of this warp's 32 TMEM lanes (no wait).
-__device__ __forceinline__ void st32u(uint32_t taddr, const uint32_t (&v)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
-      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
-      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
-      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
-      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
-      : "memory");
-}
-
-// 32 consecutive 32-bit columns of this warp's 32 TMEM lanes, without waiting for the load.
-__device__ __forceinline__ void ld32_nowait(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-}
-
-// UMMA with A = P in tensor memory (M = 128 rows, K = 16 per step) and B from shared memory.
-__device__ __forceinline__ void mma_bf16_tmem_a(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
-                                                uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(tmem_d),
-      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate));
-}
-
 template <int D>
-// 200 registers per thread: the softmax rows hold 128 scores; 320 x 200 fits one CTA per SM.
-__global__ void __maxnreg__(200)
+__global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                    const __grid_constant__ CUtensorMap vmap, const Params p) {
   using S = Smem<D>;
+  constexpr int kDim = D;
   constexpr uint32_t kIdescS = tc::idesc_bf16(kTile, kTile, false, false);
   constexpr uint32_t kIdescO = tc::idesc_bf16(kTile, D, false, true);
   pdl_wait();
@@ -102,38 +70,35 @@ __global__ void __maxnreg__(200)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* q_s = base + S::kQOff;
-  uint8_t* k_s = base + S::kKOff;
-  uint8_t* v_s = base + S::kVOff;
+  uint8_t* stages = base + S::kStageOff;
+  uint8_t* p_s = base + S::kPOff;
   uint64_t* bars = reinterpret_cast<uint64_t*>(base + S::kBarOff);
-  uint64_t* k_full = bars;       // [2] K stage landed
-  uint64_t* k_empty = bars + 2;  // [2] K stage read by its score products
-  uint64_t* v_full = bars + 4;   // [2] V stage landed
-  uint64_t* v_empty = bars + 6;  // [2] V stage read by its value products
-  uint64_t* s_full = bars + 8;   // [tile] S_X computed (and every earlier product complete)
-  uint64_t* p_full = bars + 10;  // [tile] P_X written over S_X (four warps)
+  uint64_t* full = bars;        // [2] K/V stage landed
+  uint64_t* empty = bars + 2;   // [2] K/V stage consumed (O product done)
+  uint64_t* s_full = bars + 4;  // [2] S buffer computed
+  uint64_t* s_free = bars + 6;  // [2] S buffer read by the softmax warps
+  uint64_t* p_full = bars + 8;  // [2] P tile written
+  uint64_t* o_done = bars + 10; // [2] O product of a tile (by P buffer) complete
   uint64_t* q_full = bars + 12;
-  uint64_t* done = bars + 13;    // every product issued has completed
+  uint64_t* done = bars + 13;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q_tiles = (p.tokens + kTile - 1) / kTile;
-  const int pairs = (q_tiles + 1) / 2;
-  const int qp = pairs - 1 - static_cast<int>(blockIdx.x);  // the heaviest (latest) pairs first
-  const int qa = 2 * qp;                                    // tile A; tile B = qa + 1
-  const bool has_b = (qa + 1) * kTile < p.tokens;
+  const int qt = q_tiles - 1 - static_cast<int>(blockIdx.x);  // the heaviest (latest) tiles first
   const int hq = blockIdx.y, b = blockIdx.z;
   const int hkv = hq / p.groups;
-  const int last_j = has_b ? qa + 1 : qa;  // key tiles [0, last_j]; tile A stops at qa
+  const int kv_tiles = qt + 1;  // keys [0, 128 * (qt + 1)) cover every query of the tile
 
   if (warp == kProducerWarp && lane == 0) {
     for (int x = 0; x < 2; ++x) {
-      mbar_init(&k_full[x], 1);
-      mbar_init(&k_empty[x], 1);
-      mbar_init(&v_full[x], 1);
-      mbar_init(&v_empty[x], 1);
+      mbar_init(&full[x], 1);
+      mbar_init(&empty[x], 1);
       mbar_init(&s_full[x], 1);
-      mbar_init(&p_full[x], 4);  // the tile's four softmax warps
+      mbar_init(&s_free[x], kSoftmaxWarps);
+      mbar_init(&p_full[x], kSoftmaxWarps);  // eight softmax warps arrive on each
+      mbar_init(&o_done[x], 1);
     }
     mbar_init(q_full, 1);
     mbar_init(done, 1);
@@ -152,170 +117,124 @@ __global__ void __maxnreg__(200)
   __syncthreads();
   tc::fence_after();
   const uint32_t tmem = *tmem_slot;
-  // tile X: S_X at columns [128 X, 128 X + 128), O_X at [256 + D X, 256 + D X + D)
+  const uint32_t tmem_o = tmem + kTmemO;
 
   if (warp == kProducerWarp) {
     // ============================ TMA producer ============================
     if (lane == 0) {
-      const int qrow = (b * p.q_heads + hq) * p.tokens + qa * kTile;
-      mbar_arrive_expect_tx(q_full, (has_b ? 2 : 1) * S::kTileBytes);
+      const int qrow = (b * p.q_heads + hq) * p.tokens + qt * kTile;
+      mbar_arrive_expect_tx(q_full, S::kTileBytes);
 #pragma unroll
-      for (int bx = 0; bx < D / 64; ++bx) {
-        tma_load_2d(q_s + bx * S::kBox, &qmap, q_full, bx * 64, qrow);
-        if (has_b) tma_load_2d(q_s + S::kTileBytes + bx * S::kBox, &qmap, q_full, bx * 64, qrow + kTile);
-      }
+      for (int bx = 0; bx < D / 64; ++bx) tma_load_2d(q_s + bx * S::kBox, &qmap, q_full, bx * 64, qrow);
       const int kvrow = (b * p.kv_heads + hkv) * p.capacity;
-      for (int j = 0; j <= last_j && !*abort_flag; ++j) {
+      for (int j = 0; j < kv_tiles && !*abort_flag; ++j) {
         const int st = j & 1;
+        if (j >= 2 && !mbar_wait_bounded(&empty[st], ((j - 2) >> 1) & 1)) {
+          raise_error(p.err, kErrTimeoutEmpty);
+          *abort_flag = 1;
+          break;
+        }
+        uint8_t* kt = stages + st * S::kStageBytes;
+        uint8_t* vt = kt + S::kTileBytes;
+        mbar_arrive_expect_tx(&full[st], S::kStageBytes);
         const int row = kvrow + j * kTile;
-        if (j >= 2 && !mbar_wait_bounded(&k_empty[st], ((j - 2) >> 1) & 1)) {
-          raise_error(p.err, kErrTimeoutEmpty);
-          *abort_flag = 1;
-          break;
-        }
-        mbar_arrive_expect_tx(&k_full[st], S::kTileBytes);
 #pragma unroll
-        for (int bx = 0; bx < D / 64; ++bx)
-          tma_load_2d(k_s + st * S::kTileBytes + bx * S::kBox, &kmap, &k_full[st], bx * 64, row);
-        if (j >= 2 && !mbar_wait_bounded(&v_empty[st], ((j - 2) >> 1) & 1)) {
-          raise_error(p.err, kErrTimeoutEmpty);
-          *abort_flag = 1;
-          break;
+        for (int bx = 0; bx < D / 64; ++bx) {
+          tma_load_2d(kt + bx * S::kBox, &kmap, &full[st], bx * 64, row);
+          tma_load_2d(vt + bx * S::kBox, &vmap, &full[st], bx * 64, row);
         }
-        mbar_arrive_expect_tx(&v_full[st], S::kTileBytes);
-#pragma unroll
-        for (int bx = 0; bx < D / 64; ++bx)
-          tma_load_2d(v_s + st * S::kTileBytes + bx * S::kBox, &vmap, &v_full[st], bx * 64, row);
       }
     }
   } else if (warp == kMmaWarp) {
     // ============================ UMMA issuer ============================
-    // Every lane takes the waits (the warp zeroes V rows past the prompt); lane 0 issues.
-    const uint32_t q_addr = smem_u32(q_s);
-    auto issue_s = [&](int x, int j) {
-      const uint32_t k_addr = smem_u32(k_s + (j & 1) * S::kTileBytes);
-      const uint32_t qx = q_addr + x * S::kTileBytes;
-#pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk) {
-        const uint32_t off = (kk >> 2) * S::kBox + (kk & 3) * 32;  // 16 dims of the 128-byte rows
-        tc::mma_bf16(tmem + 128 * x, tc::desc_sw128(qx + off, 16, 1024), tc::desc_sw128(k_addr + off, 16, 1024),
-                     kIdescS, kk > 0 ? 1u : 0u);
-      }
-      tc::commit(&s_full[x]);
-    };
-    auto issue_o = [&](int x, int j) {
-      const uint32_t v_addr = smem_u32(v_s + (j & 1) * S::kTileBytes);
-#pragma unroll
-      for (int kk = 0; kk < kTile / 16; ++kk) {
-        // P: 16 keys = 8 packed columns of S_X; V: 16 key rows, MN-major over D
-        mma_bf16_tmem_a(tmem + 256 + D * x, tmem + 128 * x + 8 * kk,
-                        tc::desc_sw128(v_addr + kk * 16 * 128, S::kBox, 1024), kIdescO, (j > 0 || kk > 0) ? 1u : 0u);
-      }
-    };
-    bool ok = mbar_wait_bounded(q_full, 0) && mbar_wait_bounded(&k_full[0], 0);
-    if (ok && lane == 0) {
-      tc::fence_after();
-      issue_s(0, 0);
-      if (has_b) issue_s(1, 0);
-      tc::commit(&k_empty[0]);
-    }
-    for (int j = 0; j <= last_j && ok; ++j) {
-      const int st = j & 1;
-      ok = mbar_wait_bounded(&v_full[st], (j >> 1) & 1);
-      if (!ok || *abort_flag) break;
-      if (j * kTile + kTile > p.tokens) {
-        // keys past the prompt: zero their V rows, so stale cache values never meet P = 0
-        uint8_t* vt = v_s + st * S::kTileBytes;
-        const int first = p.tokens - j * kTile;
-        for (int e = lane; e < (kTile - first) * (D / 8); e += 32) {
-          const int r = first + e / (D / 8), c16 = e % (D / 8);
-          *reinterpret_cast<uint4*>(vt + (c16 >> 3) * S::kBox + r * 128 + (c16 & 7) * 16) = make_uint4(0, 0, 0, 0);
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-      }
-      const bool a_live = j <= qa;
-      const bool next_a = j + 1 <= qa, next_b = has_b && j + 1 <= last_j;
-      if (a_live) ok = mbar_wait_bounded(&p_full[0], j & 1);
-      if (ok && (next_a || next_b)) ok = mbar_wait_bounded(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1);
-      if (!ok) break;
-      if (lane == 0) {
-        tc::fence_after();
-        if (a_live) issue_o(0, j);
-        if (next_a) issue_s(0, j + 1);
-      }
-      if (has_b) {
-        ok = mbar_wait_bounded(&p_full[1], j & 1);
-        if (!ok) break;
-        if (lane == 0) {
-          tc::fence_after();
-          issue_o(1, j);
-          if (next_b) issue_s(1, j + 1);
-        }
-      }
-      if (lane == 0) {
-        if (next_a || next_b) tc::commit(&k_empty[(j + 1) & 1]);
-        tc::commit(&v_empty[st]);
-      }
-      __syncwarp();
-    }
-    if (!ok) {
-      if (lane == 0) raise_error(p.err, kErrTimeoutMma);
-      *abort_flag = 1;
-    }
     if (lane == 0) {
+      const uint32_t q_addr = smem_u32(q_s), p_addr = smem_u32(p_s);
+      auto issue_o = [&](int j) -> bool {
+        const int x = j & 1;
+        if (!mbar_wait_bounded(&p_full[x], (j >> 1) & 1)) return false;
+        tc::fence_after();
+        const uint32_t v_addr = smem_u32(stages + x * S::kStageBytes + S::kTileBytes);
+        const uint32_t pb = p_addr + x * S::kPBytes;
+#pragma unroll
+        for (int kk = 0; kk < kTile / 16; ++kk) {
+          const uint32_t off_p = (kk >> 2) * S::kBox + (kk & 3) * 32;  // 16 keys of the P rows
+          const uint32_t off_v = kk * 16 * 128;                          // 16 key rows of V
+          tc::mma_bf16(tmem_o, tc::desc_sw128(pb + off_p, 16, 1024), tc::desc_sw128(v_addr + off_v, S::kBox, 1024),
+                       kIdescO, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc::commit(&o_done[x]);
+        tc::commit(&empty[x]);  // both products of tile j have read its K/V stage
+        return true;
+      };
+      bool ok = mbar_wait_bounded(q_full, 0);
+      for (int j = 0; j < kv_tiles && ok; ++j) {
+        const int x = j & 1;
+        ok = mbar_wait_bounded(&full[x], (j >> 1) & 1) && (j < 2 || mbar_wait_bounded(&s_free[x], ((j - 2) >> 1) & 1));
+        if (!ok || *abort_flag) break;
+        tc::fence_after();
+        const uint32_t k_addr = smem_u32(stages + x * S::kStageBytes);
+#pragma unroll
+        for (int kk = 0; kk < kDim / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * S::kBox + (kk & 3) * 32;  // 16 dims of the 128-byte rows
+          tc::mma_bf16(tmem + 128 * x, tc::desc_sw128(q_addr + off, 16, 1024), tc::desc_sw128(k_addr + off, 16, 1024),
+                       kIdescS, kk > 0 ? 1u : 0u);
+        }
+        tc::commit(&s_full[x]);
+        if (j >= 1) ok = issue_o(j - 1);
+      }
+      if (ok && !*abort_flag) ok = issue_o(kv_tiles - 1);
+      if (!ok) {
+        raise_error(p.err, kErrTimeoutMma);
+        *abort_flag = 1;
+      }
       tc::commit(done);  // arrives once every product issued above has completed
       if (!mbar_wait_bounded(done, 0)) raise_error(p.err, kErrTimeoutDrain);
     }
     __syncwarp();
   } else {
     // ============================ softmax warps ============================
-    // Warp w handles tile X = w / 4, TMEM lanes 32*(w%4).. = its query rows; one thread per row.
-    // Control flow stays warp-uniform: tcgen05.ld/st are .sync.aligned.
-    const int x = warp >> 2, quarter = warp & 3;
-    const int row = quarter * 32 + lane;
-    const int t = (qa + x) * kTile + row;  // this row's token
+    // Warp w reads TMEM lanes 32*(w%4).. (its query rows) and key columns [64h, 64h + 64) of S,
+    // h = w / 4, and owns O columns [h*D/2, (h+1)*D/2). The two warps of a row exchange their
+    // partial row maxima (and, at the end, row sums) through spare TMEM columns and a named
+    // barrier per warp pair; both then take identical pivot decisions. Control flow stays
+    // warp-uniform: tcgen05.ld/st are .sync.aligned.
+    const int quarter = warp & 3, half = warp >> 2;
+    const int row = quarter * 32 + lane;  // query row of the tile = TMEM lane
+    const int t = qt * kTile + row;       // its token
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t s_addr = tmem + 128 * x + lane_base;
-    const uint32_t o_addr = tmem + 256 + D * x + lane_base;
+    const uint32_t pair_bar = 1 + quarter;  // named barriers 1..4, 64 threads each
     const float sl2 = p.scale_log2;
     const int last_key = min(t, p.tokens - 1);  // keys <= last_key are visible to this row
-    const int my_last = qa + x;                 // this tile's diagonal key tile
-    const bool live_tile = x == 0 || has_b;
     float pivot = -INFINITY, lsum = 0.f;
     bool ok = true;
-    for (int j = 0; live_tile && j <= my_last; ++j) {
-      const bool waited = !*abort_flag && mbar_wait_bounded(&s_full[x], j & 1);
+    for (int j = 0; j < kv_tiles; ++j) {
+      const int x = j & 1;
+      const bool waited = !*abort_flag && mbar_wait_bounded(&s_full[x], (j >> 1) & 1);
       if (!__all_sync(0xffffffffu, waited)) {
         ok = false;
         break;
       }
       tc::fence_after();
-      float v[128];
-      {
-        uint32_t r0[32], r1[32], r2[32], r3[32];
-        ld32_nowait(s_addr, r0);
-        ld32_nowait(s_addr + 32, r1);
-        ld32_nowait(s_addr + 64, r2);
-        ld32_nowait(s_addr + 96, r3);
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          v[c] = __uint_as_float(r0[c]);
-          v[32 + c] = __uint_as_float(r1[c]);
-          v[64 + c] = __uint_as_float(r2[c]);
-          v[96 + c] = __uint_as_float(r3[c]);
-        }
-      }
-      // a tile wholly below the diagonal and inside the prompt is visible to every row
-      const bool interior = j < qa + x && j * kTile + kTile <= p.tokens;
-      const int key0 = j * kTile;
+      const uint32_t s_addr = tmem + 128 * x + 64 * half + lane_base;
+      const int key0 = j * kTile + 64 * half;  // this warp's first key
+      // a tile below the diagonal is visible to every query row of this tile
+      const bool interior = j < qt;
       float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        v[c] = (interior || key0 + c <= last_key) ? v[c] * sl2 : -INFINITY;
-        mx = fmaxf(mx, v[c]);
+      for (int c0 = 0; c0 < 64; c0 += 32) {
+        float v[32];
+        tc::ld32(s_addr + c0, v);
+#pragma unroll
+        for (int c = 0; c < 32; ++c)
+          if (interior || key0 + c0 + c <= last_key) mx = fmaxf(mx, v[c] * sl2);
       }
+      // the row's other half: exchange partial maxima through TMEM column [parity][half]
+      tc::st1(tmem + kTmemXchg + 2 * x + half + lane_base, mx);
+      tc::fence_before();
+      asm volatile("bar.sync %0, 64;" ::"r"(pair_bar) : "memory");
+      tc::fence_after();
+      mx = fmaxf(mx, tc::ld1(tmem + kTmemXchg + 2 * x + (1 - half) + lane_base));
+      // lazy rescale: a row's pivot moves only when its max exceeds the pivot by more than 8
       float corr = 1.f;
       const bool need = mx > pivot + kRescaleAbove || (pivot == -INFINITY && mx > -INFINITY);
       if (need) {
@@ -324,48 +243,93 @@ __global__ void __maxnreg__(200)
       }
       lsum *= corr;
       if (j >= 1 && __any_sync(0xffffffffu, need)) {
-        // O_X holds the products through tile j - 1, complete: s_full(j) covers them
+        // the previous tile's product must have landed in O before this warp's half of the
+        // rows' O is rescaled (rows that keep their pivot multiply by 1)
+        const bool landed = mbar_wait_bounded(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1);
+        if (!__all_sync(0xffffffffu, landed)) {
+          ok = false;
+          break;
+        }
+        tc::fence_after();
 #pragma unroll
-        for (int c0 = 0; c0 < D; c0 += 32) {
+        for (int c0 = 0; c0 < kDim / 2; c0 += 32) {
           float o[32];
-          tc::ld32(o_addr + c0, o);
+          tc::ld32(tmem_o + half * (kDim / 2) + lane_base + c0, o);
 #pragma unroll
           for (int c = 0; c < 32; ++c) o[c] *= corr;
-          tc::st32(o_addr + c0, o);
+          tc::st32(tmem_o + half * (kDim / 2) + lane_base + c0, o);
+        }
+      }
+      // P tile x was last read by the product of tile j - 2
+      if (j >= 2) {
+        const bool free = mbar_wait_bounded(&o_done[x], ((j - 2) >> 1) & 1);
+        if (!__all_sync(0xffffffffu, free)) {
+          ok = false;
+          break;
         }
       }
       const float piv = pivot == -INFINITY ? 0.f : pivot;
+      // this warp's 64 keys are box `half` of the K-major P tile
+      uint8_t* pt = p_s + x * S::kPBytes + half * S::kBox;
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint32_t packed[32];
+      for (int c0 = 0; c0 < 64; c0 += 32) {
+        float v[32];
+        tc::ld32(s_addr + c0, v);
+        uint32_t packed[16];
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float p0 = tc::ex2_approx(v[64 * h + 2 * c] - piv);   // -inf gives 0
-          const float p1 = tc::ex2_approx(v[64 * h + 2 * c + 1] - piv);
+        for (int c = 0; c < 32; c += 2) {
+          const bool see0 = interior || key0 + c0 + c <= last_key;
+          const bool see1 = interior || key0 + c0 + c + 1 <= last_key;
+          const float p0 = see0 ? tc::ex2_approx(v[c] * sl2 - piv) : 0.f;
+          const float p1 = see1 ? tc::ex2_approx(v[c + 1] * sl2 - piv) : 0.f;
           lsum += p0 + p1;
-          packed[c] = pack2(p0, p1);
+          packed[c / 2] = pack_bf16x2(p0, p1);
         }
-        st32u(s_addr + 32 * h, packed);  // P keys [64 h, 64 h + 64) as 32 packed columns
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          *reinterpret_cast<uint4*>(pt + sw128(row, (c0 >> 3) + q)) =
+              make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
       }
-      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc::fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[x]);
+      // V rows past the prompt: zeroed so stale cache values never meet a zero weight
+      if (half == 0 && j * kTile + kTile > p.tokens && j * kTile + row >= p.tokens) {
+        uint8_t* vt = stages + x * S::kStageBytes + S::kTileBytes;
+#pragma unroll
+        for (int bx = 0; bx < D / 64; ++bx)
+#pragma unroll
+          for (int c16 = 0; c16 < 8; ++c16)
+            *reinterpret_cast<uint4*>(vt + bx * S::kBox + row * 128 + c16 * 16) = make_uint4(0, 0, 0, 0);
+      }
+      fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[x]);
     }
-    // every product has completed before the output is read
-    if (ok && live_tile) ok = __all_sync(0xffffffffu, mbar_wait_bounded(done, 0));
+    if (ok) {
+      const bool landed = mbar_wait_bounded(&o_done[(kv_tiles - 1) & 1], ((kv_tiles - 1) >> 1) & 1);
+      ok = __all_sync(0xffffffffu, landed);
+    }
     if (!ok) {
       raise_error(p.err, kErrTimeoutMma);
       *abort_flag = 1;
     }
-    if (ok && live_tile) {
+    if (ok) {
+      // row sum = both halves' partial sums (TMEM exchange, column [half] past the maxima)
       tc::fence_after();
-      const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
-      __nv_bfloat16* dst = p.out + ((static_cast<size_t>(b) * p.tokens + t) * p.q_heads + hq) * D;
+      tc::st1(tmem + kTmemXchg + 4 + half + lane_base, lsum);
+      tc::fence_before();
+      asm volatile("bar.sync %0, 64;" ::"r"(pair_bar) : "memory");
+      tc::fence_after();
+      const float total = lsum + tc::ld1(tmem + kTmemXchg + 4 + (1 - half) + lane_base);
+      const float inv = total > 0.f ? 1.f / total : 0.f;
+      // every lane reads its O row half (uniform TMEM loads); rows past the prompt are not stored
+      __nv_bfloat16* dst =
+          p.out + ((static_cast<size_t>(b) * p.tokens + t) * p.q_heads + hq) * kDim + half * (kDim / 2);
 #pragma unroll
-      for (int c0 = 0; c0 < D; c0 += 32) {
+      for (int c0 = 0; c0 < kDim / 2; c0 += 32) {
         float o[32];
-        tc::ld32(o_addr + c0, o);
+        tc::ld32(tmem_o + half * (kDim / 2) + lane_base + c0, o);
         if (t < p.tokens) {
 #pragma unroll
           for (int q = 0; q < 4; ++q)
@@ -398,8 +362,8 @@ int launch(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, 
     configured[dev] = true;
   }
   const int q_tiles = (tokens + kTile - 1) / kTile;
-  return launch_ex(prefill_kernel<D>, dim3((q_tiles + 1) / 2, q_heads, batch), dim3(kThreads), Smem<D>::kTotal,
-                   stream, 1, qm, km, vm, p);
+  return launch_ex(prefill_kernel<D>, dim3(q_tiles, q_heads, batch), dim3(kThreads), Smem<D>::kTotal, stream, 1, qm,
+                   km, vm, p);
 }
 
 }  // namespace prefill

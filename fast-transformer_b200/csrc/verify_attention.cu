@@ -17,10 +17,13 @@
 //    with the fp32 accumulator in TMEM (double-buffered). Q sits in shared memory in the same
 //    swizzled K-major layout, written once by the CTA.
 //  * Eight softmax warps (TMEM lane quarter x half of the member columns; one token per
-//    thread, up to 16 member columns) reduce column maxima with a shuffle transpose-reduce and
-//    shared memory, and write P as bf16 into a K-major swizzled tile (double-buffered). Column c of the
-//    32-member group holds member 2*(c % 16) + c / 16, so the live members split evenly over
-//    the two halves (config 5's 20 members: 10 + 10) and dead columns are skipped.
+//    thread, 16 member columns) write P as bf16 into a K-major swizzled tile (double-buffered).
+//  * Lazy pivot: a column's exponent pivot only moves when some score of a tile exceeds it by
+//    more than 8 (log2 units, a factor of 256). One barrier-reduction vote per tile decides;
+//    only then do the warps reduce the tile's column maxima (shuffle transpose-reduce and
+//    shared memory) and rescale. P = 2^(s - pivot) then lies in (0, 256], which bf16 and fp32
+//    hold exactly as well as (0, 1]; the result equals the reference's per-tile exact-maximum
+//    form up to rounding.
 //  * O^T_tile = V^T * P^T is a second tcgen05.mma chain (M = 128 dims, N = 32 members,
 //    K = 128 tokens) with V read in place as an MN-major operand; each softmax thread (one dim)
 //    folds the tile into its fp32 running output with the softmax correction, one tile behind
@@ -44,6 +47,7 @@ constexpr int kProducerWarp = kSoftmaxWarps;      // one lane issues every TMA
 constexpr int kMmaWarp = kSoftmaxWarps + 1;       // one lane issues every UMMA; the warp owns TMEM
 constexpr int kThreads = (kSoftmaxWarps + 2) * 32;
 constexpr int kTmemCols = 4 * kMembers;  // S^T double buffer + O^T tile double buffer
+constexpr float kSlack = 8.f;            // pivot moves when a score exceeds it by more (log2 units)
 
 struct Params {
   const __nv_bfloat16* q;  // [B, T, Hq, D] token-major
@@ -63,9 +67,17 @@ constexpr uint32_t kIdescS = tc::idesc_bf16(kTile, kMembers, false, false);
 constexpr uint32_t kIdescO = tc::idesc_bf16(kTile, kMembers, true, false);
 using tc::ex2_approx;
 
-// Column c of a 32-member group holds member 2 * (c % 16) + c / 16: even members in the first
-// half of the columns, odd members in the second.
-__device__ __forceinline__ int column_member(int c) { return 2 * (c % kHalf) + c / kHalf; }
+// True on every participating thread when `pred` is true on any of the `threads` threads that
+// meet at named barrier `id` (bar.red.or: the barrier and the vote in one instruction).
+__device__ __forceinline__ bool barrier_any(int id, int threads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred q, a;\n setp.ne.u32 q, %1, 0;\n bar.red.or.pred a, %2, %3, q;\n selp.u32 %0, 1, 0, a;\n}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(threads)
+      : "memory");
+  return r != 0;
+}
 
 // Column-wise reduction of a 32x16 block held one row per lane: afterwards lanes c and c+16
 // hold the reduction of column c over all 32 rows (shuffle transpose-reduce, 16 shuffles).
@@ -175,11 +187,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           make_uint4(0, 0, 0, 0);
     }
   }
-  // Q members [group0, group0 + 32) of this (row, KV head) into the swizzled K-major tile, row
-  // r holding member column_member(r); rows past the real members, and dims past D, are zero.
+  // Q members [group0, group0 + 32) of this (row, KV head) into the swizzled K-major tile;
+  // rows past the real members, and dims past D, are zero.
   for (int e = tid; e < kMembers * 16; e += blockDim.x) {
     const int r = e / 16, c16 = e % 16;  // member row, 16-byte chunk of the 128-dim layout
-    const int m = group0 + column_member(r);
+    const int m = group0 + r;
     uint4 v = make_uint4(0, 0, 0, 0);
     if (m < members && c16 * 8 < D) {
       const int t = m / G, g = m % G;
@@ -190,7 +202,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     *reinterpret_cast<uint4*>(q_s + (c16 >> 3) * (kMembers * 128) + sw128(r, c16 & 7)) = v;
   }
   if (tid < kMembers) {
-    const int m = group0 + column_member(tid);
+    const int m = group0 + tid;
     const int t = m / G;
     const bool live = m < members;
     const bool chained = live && t < p.chain[b];
@@ -289,9 +301,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = quarter * 32 + lane;  // token of the S^T tile, dim of the O^T tile
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const int col0 = half * kHalf;
-    // live columns of this half: members 2*c + half < members - group0
-    const int group_live = min(kMembers, members - group0);
-    const int live = max(0, min(kHalf, (group_live - half + 1) / 2));
     float o[kHalf], l[kHalf], corr_prev[kHalf], run_max[kHalf];
 #pragma unroll
     for (int c = 0; c < kHalf; ++c) {
@@ -343,34 +352,45 @@ __global__ void __launch_bounds__(kThreads, 1)
           sc[c] = visible ? sc[c] * sl2 : -INFINITY;
         }
       }
-      // Column maxima: each quarter's max over its 32 tokens goes to red[parity][quarter];
-      // after one barrier every thread folds the four quarters and its running max itself
-      // (all threads of a column half compute the same values). red is double-buffered by
-      // tile parity: the next write to this half happens after the next tile's barrier.
-      // (a single-instruction redux.sync.max.f32 per column measured slower on B200: config 5
-      // 55.7 against 43 us)
-      const float wmax = transpose_reduce16<true>(sc, lane);
-      float* rq = red + x * 4 * kMembers;
-      if (lane < kHalf) rq[quarter * kMembers + col0 + lane] = wmax;
-      asm volatile("bar.sync 1, 256;" ::: "memory");
+      // Lazy pivot: every thread votes whether one of its scores exceeds the column's pivot
+      // by more than kSlack (a column that has seen only -inf has pivot -inf, so any finite
+      // score votes). Only a tile that some thread votes for reduces its column maxima: each
+      // quarter's max over its 32 tokens goes to red[parity][quarter], and after one barrier
+      // every thread folds the four quarters and its running max itself (all threads of a
+      // column half compute the same values). red is double-buffered by tile parity.
+      bool need = false;
+#pragma unroll
+      for (int c = 0; c < kHalf; ++c) need |= sc[c] > run_max[c] + kSlack;
       float piv[kHalf], corr[kHalf];
+      if (barrier_any(1, 256, need)) {
+        const float wmax = transpose_reduce16<true>(sc, lane);
+        float* rq = red + x * 4 * kMembers;
+        if (lane < kHalf) rq[quarter * kMembers + col0 + lane] = wmax;
+        asm volatile("bar.sync 1, 256;" ::: "memory");
 #pragma unroll
-      for (int c4 = 0; c4 < kHalf / 4; ++c4) {
-        float4 t4 = *reinterpret_cast<const float4*>(rq + col0 + 4 * c4);
+        for (int c4 = 0; c4 < kHalf / 4; ++c4) {
+          float4 t4 = *reinterpret_cast<const float4*>(rq + col0 + 4 * c4);
 #pragma unroll
-        for (int w = 1; w < 4; ++w) {
-          const float4 u4 = *reinterpret_cast<const float4*>(rq + w * kMembers + col0 + 4 * c4);
-          t4.x = fmaxf(t4.x, u4.x), t4.y = fmaxf(t4.y, u4.y), t4.z = fmaxf(t4.z, u4.z), t4.w = fmaxf(t4.w, u4.w);
+          for (int w = 1; w < 4; ++w) {
+            const float4 u4 = *reinterpret_cast<const float4*>(rq + w * kMembers + col0 + 4 * c4);
+            t4.x = fmaxf(t4.x, u4.x), t4.y = fmaxf(t4.y, u4.y), t4.z = fmaxf(t4.z, u4.z), t4.w = fmaxf(t4.w, u4.w);
+          }
+          const float tm[4] = {t4.x, t4.y, t4.z, t4.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int c = 4 * c4 + e;
+            const float nm = fmaxf(run_max[c], tm[e]);
+            piv[c] = nm == -INFINITY ? 0.f : nm;
+            // an unchanged max rescales by exactly 1 (and an all -inf column has l = o = 0)
+            corr[c] = nm == run_max[c] ? 1.f : ex2_approx(run_max[c] - piv[c]);
+            run_max[c] = nm;
+          }
         }
-        const float tm[4] = {t4.x, t4.y, t4.z, t4.w};
+      } else {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int c = 4 * c4 + e;
-          const float nm = fmaxf(run_max[c], tm[e]);
-          piv[c] = nm == -INFINITY ? 0.f : nm;
-          // an unchanged max rescales by exactly 1 (and an all -inf column has l = o = 0)
-          corr[c] = nm == run_max[c] ? 1.f : ex2_approx(run_max[c] - piv[c]);
-          run_max[c] = nm;
+        for (int c = 0; c < kHalf; ++c) {
+          piv[c] = run_max[c] == -INFINITY ? 0.f : run_max[c];
+          corr[c] = 1.f;
         }
       }
       // ---- P (bf16) into P[x], K-major swizzled: row = member, column = token. P[x] was
@@ -379,11 +399,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t pcol = (row >> 6) * (kMembers * 128) + (row & 7) * 2;
 #pragma unroll
       for (int c = 0; c < kHalf; ++c) {
-        if (c < live) {  // dead columns only ever reach their own, unstored, outputs
-          const float pv = ex2_approx(sc[c] - piv[c]);
-          l[c] = l[c] * corr[c] + pv;
-          *reinterpret_cast<__nv_bfloat16*>(pt + pcol + sw128(col0 + c, (row & 63) >> 3)) = __float2bfloat16_rn(pv);
-        }
+        const float pv = ex2_approx(sc[c] - piv[c]);
+        l[c] = l[c] * corr[c] + pv;
+        *reinterpret_cast<__nv_bfloat16*>(pt + pcol + sw128(col0 + c, (row & 63) >> 3)) = __float2bfloat16_rn(pv);
       }
       if (!in_range && half == 0) {
         // V row past the visible range: zero it so stale values never meet a zero weight.
@@ -426,8 +444,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int d = row;
 #pragma unroll
       for (int c = 0; c < kHalf; ++c) {
-        const int m = group0 + 2 * c + half;  // column col0 + c
-        if (c >= live || d >= D) continue;
+        const int m = group0 + col0 + c;
+        if (m >= members || d >= D) continue;
         const int mc = col0 + c;
         const float L = red[mc] + red[kMembers + mc] + red[2 * kMembers + mc] + red[3 * kMembers + mc];
         const int t = m / G, g = m % G;

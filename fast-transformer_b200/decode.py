@@ -271,6 +271,9 @@ class DecodeState:
         elif peers is not None and w.lm_head_local is not w.lm_head:
             fused_argmax(normalized, w.lm_head_local, out=self.token_ids.view(-1), index_base=w.vocab_base,
                          exchange=(comm.size, comm.rank, peers.exchange_ptrs, peers.exchange_local, self.position))
+        elif w.lm_head_local is not w.lm_head:
+            # one rank's shard run alone (timing only): its vocabulary slice, no candidate exchange
+            fused_argmax(normalized, w.lm_head_local, out=self.token_ids.view(-1), index_base=w.vocab_base)
         else:
             fused_argmax(normalized, w.lm_head, out=self.token_ids.view(-1))
         self.position.add_(1)

@@ -5,9 +5,8 @@
 cache [B,Hkv,C,D] and a device-side int64 ``position``; every valid slot [0, position]
 contributes; the result is a new [B,1,Hq,D] tensor. Additionally ``position`` may hold
 one entry per row ([B]) for ragged batches. The kernels are fb_decode_attention (TMA +
-mma.sync partials; a persistent grid claiming fixed chunks of tiles, or one cluster per pair
-for a shared position with few pairs) and fb_decode_attention_combine (log-sum-exp merge),
-launched on the current stream, so CUDA-graph capture records them.
+mma.sync partials over a balanced persistent split) and fb_decode_attention_combine
+(log-sum-exp merge), launched on the current stream, so CUDA-graph capture records them.
 """
 
 import torch
@@ -38,8 +37,7 @@ def attend(query, key, value, position, scale, out=None, workspace=None, ctas=No
 
     One launch by default (fb_decode_attention, merge fused into the last CTA of each pair);
     ``two_launch`` runs fb_decode_attention_partials then fb_decode_attention_combine. A
-    caller-provided ``workspace`` must have been zeroed before its first use (its tail holds
-    the chunk-claim and per-pair counters, which every launch leaves at zero).
+    caller-provided ``workspace`` must have been zeroed before its first fused use.
     """
     batch, query_heads, dim = query.shape[0], query.shape[1], query.shape[-1]
     kv_heads, capacity = key.shape[1], key.shape[2]

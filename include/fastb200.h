@@ -55,23 +55,17 @@ int fb_device_error(unsigned int* host_flags);
  *   out      bf16 [B, Hq, D]          (the reference's [B, 1, Hq, D])
  *   D in {64, 128}; G = Hq / Hkv in [1, 8].
  *
- * The work is a persistent grid of `ctas` CTAs. The valid tokens of every (row, KV head)
- * pair are cut into chunks of K consecutive 64-token tiles (K >= 4, a function of the
- * lengths only); CTAs claim chunks from a counter in the workspace, so fast CTAs take more
- * chunks, and each chunk's partial lands in its own slot. fb_decode_attention_ctas() gives
- * the default CTA count (<= 512); fb_decode_attention_workspace() the workspace bytes for a
- * count. A shared position with few pairs runs as one thread-block cluster per pair instead
- * (merged through distributed shared memory; the workspace is then unused).
+ * The work is a persistent grid of `ctas` CTAs that split the valid tokens of all
+ * (row, KV head) pairs evenly (64-token tiles). fb_decode_attention_ctas() gives the
+ * default CTA count (<= 512); fb_decode_attention_workspace() the workspace bytes for a count.
  *
- * fb_decode_attention: the whole operation in one launch; the CTA that finishes a pair's last
- *   chunk merges the pair's chunks (log-sum-exp combine) in chunk order, so the result does
- *   not depend on which CTA took which chunk. The workspace ends with one int counter per pair
- *   and two claim counters: zero them once before the workspace's first use; every call leaves
- *   them zero again. Calls that share a workspace must not overlap on the GPU.
+ * fb_decode_attention: the whole operation in one launch; the CTA that finishes a pair last
+ *   merges its runs (log-sum-exp combine) in CTA order. The workspace ends with one int
+ *   counter per pair: zero it once before its first use; every call leaves it zero again.
+ *   Calls that share a workspace must not overlap on the GPU.
  * fb_decode_attention_partials + fb_decode_attention_combine: the same result in two
  *   launches (partials, then the merge kernel), the reference's _decode_partials/_decode_merge
- *   split; the claim counters follow the same zero-before-first-use rule. Both take the same
- *   arguments and `ctas`.
+ *   split; no counter state. Both take the same arguments and `ctas`.
  * ---------------------------------------------------------------------------------- */
 int fb_decode_attention_ctas(int batch, int kv_heads, int capacity, int head_dim);
 size_t fb_decode_attention_workspace(int batch, int q_heads, int kv_heads, int head_dim, int ctas);
@@ -101,7 +95,7 @@ int fb_decode_attention_cluster_shape(int cluster, int stages);
  * fixed, pre-reserved device pool and hands this library only input and output buffers,
  * or a plugin host whose allocator may not be called from the plugin. They cannot provide
  * fb_decode_attention's workspace, so this entry point uses a fixed scratch array inside
- * the library instead (about 4.6 MiB, held on every GPU that loads the library until the
+ * the library instead (about 2.7 MiB, held on every GPU that loads the library until the
  * process exits). Same arguments and result as fb_decode_attention, minus the workspace
  * and the CTA count (it uses min(SM count, 160) CTAs). It calls no cudaMalloc/cudaFree.
  *   Limit: batch * kv_heads <= 512 (and the fb_decode_attention limits); a larger request

@@ -422,10 +422,9 @@ def test_fused_argmax_equals_projection_then_argmax():
 
 
 def test_decode_attention_fused_equals_two_launch_and_counters_reset():
-    """fb_decode_attention (persistent form: dynamically claimed chunks, the pair's last chunk
-    merges) equals fb_decode_attention_partials + fb_decode_attention_combine bit for bit, and
-    leaves its per-pair and claim counters at zero. Per-row positions (two or more rows) keep
-    every call on the persistent form."""
+    """fb_decode_attention (persistent form, last CTA merges) equals fb_decode_attention_partials
+    + fb_decode_attention_combine bit for bit, and leaves its per-pair counters at zero. Per-row
+    positions (two or more rows) keep every call on the persistent form."""
     from kernels.decode_attention import _ctas, attend, workspace_bytes
     for lengths, q_heads in (([1, 700, 8192, 65], 32), ([30000, 20001], 16), ([300, 301, 302, 303, 1, 2, 3, 4], 16)):
         q, k, v, position = _ragged(len(lengths), q_heads, 8, 128, lengths, seed=sum(lengths))
@@ -439,7 +438,7 @@ def test_decode_attention_fused_equals_two_launch_and_counters_reset():
         torch.cuda.synchronize()
         assert torch.equal(fused, two)
         assert torch.equal(second, fused)
-        counters = again_ws[-(len(lengths) * 8 + 2) * 4:].view(torch.int32)  # pair counters, claim counters
+        counters = again_ws[-len(lengths) * 8 * 4:].view(torch.int32)
         assert int(counters.abs().sum()) == 0
 
 

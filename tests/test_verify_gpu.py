@@ -61,3 +61,23 @@ def test_verify_attention_two_member_groups_and_graph(d):
     graph.replay()
     torch.cuda.synchronize()
     assert torch.equal(captured, eager)
+
+
+
+def test_verify_attention_many_splits_deterministic():
+    """Five KV splits and two 32-member groups: identical bits on repeated calls and the
+    oracle's result (the split merge runs in split order)."""
+    from kernels.decode_attention import block_attention
+    g = torch.Generator().manual_seed(11)
+    batch, tokens, hq, hkv, cap, d = 2, 12, 32, 8, 1500, 128  # 48 members: two groups
+    q = torch.randn(batch, tokens, hq, d, generator=g).bfloat16()
+    k = torch.randn(batch, hkv, cap, d, generator=g).bfloat16()
+    v = torch.randn(batch, hkv, cap, d, generator=g).bfloat16()
+    position = torch.tensor([1400, 900])
+    chain = torch.tensor([12, 3])
+    expect = oatt.block_attention(q, k, v, position, 1 / math.sqrt(d), chain)
+    args = (q.cuda(), k.cuda(), v.cuda(), position.cuda(), 1 / math.sqrt(d), chain.cuda())
+    first = block_attention(*args, splits=5)
+    again = block_attention(*args, splits=5)
+    assert torch.equal(first, again)
+    torch.testing.assert_close(first.cpu().float(), expect.float(), **TOL)
