@@ -117,8 +117,6 @@ struct Smem {
 __global__ void __launch_bounds__(kThreads, 1)
     verify_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                   const Params p) {
-  pdl_wait();
-  pdl_trigger();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = base;
@@ -145,15 +143,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int pair = blockIdx.x, split = blockIdx.y, group0 = blockIdx.z * kMembers;
   const int b = pair / p.kv_heads, h = pair % p.kv_heads;
   const int G = p.groups, T = p.tokens, members = T * G;
-  const long long first = p.position[b] + 1;             // first block token's slot + 1
-  long long end = first + T - 1;                          // one past the last block slot
-  if (end > p.capacity) end = p.capacity;
-  const long long begin = static_cast<long long>(split) * p.chunk;
-  long long stop = begin + p.chunk;
-  if (stop > end) stop = end;
-  const int tiles = stop > begin ? static_cast<int>((stop - begin + kTile - 1) / kTile) : 0;
 
-  // ---- set-up: barriers, TMEM, Q tile, per-member visibility ----
+  // ---- set-up that reads nothing an earlier kernel writes: barriers, TMEM, zero boxes. It
+  // overlaps the previous kernel's tail (programmatic dependent launch). ----
   if (warp == kProducerWarp && lane == 0) {
     for (int st = 0; st < kStages; ++st) {
       mbar_init(&full[st], 1);
@@ -171,6 +163,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tensormap(&kmap);
     prefetch_tensormap(&vmap);
     *abort_flag = 0;
+    // The split's first ring-full of K/V rows into L2 while the previous kernel finishes
+    // (which tiles are valid needs the position, read after the dependency wait).
+    const int row0 = pair * p.capacity + split * p.chunk;
+    for (int i = 0; i < kStages; ++i)
+      for (int bx = 0; bx < p.dim / 64; ++bx) {
+        tma_prefetch_l2_2d(&kmap, bx * 64, row0 + i * kTile);
+        tma_prefetch_l2_2d(&vmap, bx * 64, row0 + i * kTile);
+      }
   }
   if (warp == kMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -187,6 +187,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           make_uint4(0, 0, 0, 0);
     }
   }
+  // ---- after the dependency wait: positions, chains and Q come from earlier kernels ----
+  pdl_wait();
+  pdl_trigger();
+  const long long first = p.position[b] + 1;             // first block token's slot + 1
+  long long end = first + T - 1;                          // one past the last block slot
+  if (end > p.capacity) end = p.capacity;
+  const long long begin = static_cast<long long>(split) * p.chunk;
+  long long stop = begin + p.chunk;
+  if (stop > end) stop = end;
+  const int tiles = stop > begin ? static_cast<int>((stop - begin + kTile - 1) / kTile) : 0;
   // Q members [group0, group0 + 32) of this (row, KV head) into the swizzled K-major tile;
   // rows past the real members, and dims past D, are zero.
   for (int e = tid; e < kMembers * 16; e += blockDim.x) {
@@ -242,15 +252,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == kMmaWarp) {
     // ============================ UMMA issuer ============================
-    // Order: S(i), then O(i-1) once P(i-1) is written - the tensor core computes O(i-1) and
-    // S(i+1) while the softmax warps work on tile i.
     if (lane == 0) {
       const uint32_t q_addr = smem_u32(q_s), p_addr = smem_u32(p_s);
       const uint32_t idesc_s = kIdescS, idesc_o = kIdescO;
-      auto issue_o = [&](int j) -> bool {
+      auto issue_o = [&](int j) {
         const int x = j & 1;
-        if (!mbar_wait_bounded(&p_full[x], (j >> 1) & 1)) return false;
-        if (j >= 2 && !mbar_wait_bounded(&o_free[x], ((j - 2) >> 1) & 1)) return false;
         tc::fence_after();
         const uint32_t v_addr = smem_u32(stages + (j % kStages) * Smem::kStageBytes + Smem::kTileBytes);
         const uint32_t pb = p_addr + x * Smem::kPBytes;
@@ -263,14 +269,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc::commit(&o_full[x]);
         tc::commit(&empty[j % kStages]);  // both products of tile j read their K/V stage
-        return true;
       };
-      bool ok = true;
-      for (int i = 0; i < tiles && ok; ++i) {
+      // S(i) needs tile i's K/V stage and S^T[i % 2] read by the softmax (tile i - 2); O(j)
+      // needs P(j) and O^T[j % 2] folded (tile j - 2). The lane issues whichever is ready first,
+      // so a tile's value product (and with it the release of its K/V stage to the TMA lane)
+      // never waits for the next tile's data. S runs at most two tiles ahead of O.
+      auto issue_s = [&](int i) {
         const int st = i % kStages, x = i & 1;
-        ok = mbar_wait_bounded(&full[st], (i / kStages) & 1) &&
-             (i < 2 || mbar_wait_bounded(&s_free[x], ((i - 2) >> 1) & 1));
-        if (!ok || *abort_flag) break;
         tc::fence_after();
         const uint32_t k_addr = smem_u32(stages + st * Smem::kStageBytes);
 #pragma unroll
@@ -281,9 +286,37 @@ __global__ void __launch_bounds__(kThreads, 1)
                     kk > 0 ? 1u : 0u);
         }
         tc::commit(&s_full[x]);
-        if (i >= 1) ok = issue_o(i - 1);
+      };
+      bool ok = true;
+      int next_s = 0, next_o = 0;
+      unsigned long long idle_since = 0;
+      while (ok && next_o < tiles && !*abort_flag) {
+        bool progressed = false;
+        if (next_s < tiles && next_s <= next_o + 2) {
+          const int i = next_s, x = i & 1;
+          if (mbar_test(&full[i % kStages], (i / kStages) & 1) &&
+              (i < 2 || mbar_test(&s_free[x], ((i - 2) >> 1) & 1))) {
+            issue_s(i);
+            ++next_s;
+            progressed = true;
+          }
+        }
+        if (next_o < next_s) {
+          const int j = next_o, x = j & 1;
+          if (mbar_test(&p_full[x], (j >> 1) & 1) && (j < 2 || mbar_test(&o_free[x], ((j - 2) >> 1) & 1))) {
+            issue_o(j);
+            ++next_o;
+            progressed = true;
+          }
+        }
+        if (progressed) {
+          idle_since = 0;
+        } else if (idle_since == 0) {
+          idle_since = globaltimer();
+        } else if (globaltimer() - idle_since > kWaitBudgetNs) {
+          ok = false;
+        }
       }
-      if (ok && tiles >= 1 && !*abort_flag) ok = issue_o(tiles - 1);
       if (!ok) {
         raise_error(p.err, kErrTimeoutMma);
         *abort_flag = 1;
