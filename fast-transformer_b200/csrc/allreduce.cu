@@ -12,14 +12,16 @@
 //  1. fb_reduce_scatter_push (after the projection's split-K partials): each rank sums its
 //     partials in split order and stores every fp32 value, flagged, only into the owner's
 //     receive slab rs[use][rank] - M*W words per rank in total.
-//  2. fb_allreduce_add_rmsnorm, phase B (the owner): polls rs[use][0..world) for its slice,
-//     sums the ranks in rank order (the same bits a rank-order sum of whole rows gives), rounds
-//     to bf16, adds the residual (rounded again), and stores the summed bf16 pairs, flagged,
-//     into ag[use] of every rank; it also stores each row's fp32 sum of squares over its
-//     slice into ss[use][rank] of every rank.
-//     Phase C (every rank, every row): polls ag[use] for the whole row and the world partial
-//     sums of squares, adds those in rank order (identical bits on every rank), and writes the
-//     normalized row bf16(bf16(s * inv) * w) and the summed row (the next residual).
+//  2. fb_allreduce_add_rmsnorm, phase B (the owner), over (row, 512-column chunk of its slice)
+//     work items so that every thread polls once whatever the slice width: polls
+//     rs[use][0..world) for its pair of columns, sums the ranks in rank order (the same bits a
+//     rank-order sum of whole rows gives), rounds to bf16, adds the residual (rounded again),
+//     and stores the summed bf16 pairs, flagged, into ag[use] of every rank; each item also
+//     stores its fp32 sum of squares into ss[use][rank][chunk] of every rank.
+//     Phase C (every rank, every row): polls ag[use] for the whole row and the row's partial
+//     sums of squares, adds those in rank order and chunk order (identical bits on every rank),
+//     and writes the normalized row bf16(bf16(s * inv) * w) and the summed row (the next
+//     residual).
 // NVLink volume per use and rank: M*W*8 bytes of partials plus M*W*4 bytes of summed values
 // (1/world of each stays local), against world*M*W*8 for pushing whole partials to every rank.
 //
@@ -35,7 +37,8 @@ namespace ar {
 constexpr int kThreads = 256;
 constexpr int kBatch = 8;  // split slabs in flight per thread
 constexpr int kMaxWorld = 8;
-constexpr int kChunk = 2 * kThreads;  // columns of one phase-C work item (one pair per thread)
+constexpr int kChunk = 2 * kThreads;  // columns of one work item (one pair per thread)
+constexpr int kMaxSliceChunks = 16;   // work items per owner slice of a row (N / world <= 8192)
 
 struct PushParams {
   const float* partials;  // [splits, m, n]
@@ -88,20 +91,20 @@ struct NormParams {
   const __nv_bfloat16* w;         // [n]
   __nv_bfloat16* out;             // [m, n]
   __nv_bfloat16* sum;             // [m, n]
-  int m, n, world, rank, use, chunks;
+  int m, n, world, rank, use, chunks, bchunks;  // chunks of a row (phase C), of a slice (phase B)
   float eps;
   unsigned* err;
 };
 
-// Polls `count` (<= kMaxWorld) flagged words at src[0], src[stride], ... until all carry `flag`;
+// Polls `count` (<= kMaxSliceChunks) flagged words at src[0], src[stride], ... until all carry `flag`;
 // false after the wait budget (or at once when an earlier wait gave up).
 __device__ __forceinline__ bool poll_words(const uint64_t* src, size_t stride, int count, uint32_t flag,
-                                           unsigned* err, uint64_t (&words)[kMaxWorld]) {
+                                           unsigned* err, uint64_t (&words)[kMaxSliceChunks]) {
   unsigned long long start = 0;
   for (;;) {
     bool ready = true;
 #pragma unroll
-    for (int q = 0; q < kMaxWorld; ++q)
+    for (int q = 0; q < kMaxSliceChunks; ++q)
       if (q < count) {
         asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(words[q]) : "l"(src + q * stride));
         ready = ready && static_cast<uint32_t>(words[q] >> 32) == flag;
@@ -157,12 +160,15 @@ __global__ void __launch_bounds__(kThreads) allreduce_norm_kernel(const __grid_c
   const int W = p.world, slice = p.n / W, half = p.n / 2;
   const size_t use_rs = static_cast<size_t>(p.use) * W * p.m * slice;
   const size_t use_ag = static_cast<size_t>(p.use) * p.m * half;
-  const size_t use_ss = static_cast<size_t>(p.use) * W * p.m;
+  const size_t use_ss = static_cast<size_t>(p.use) * W * p.bchunks * p.m;
 
-  // ---- phase B: this rank's slice of rows blockIdx.x, blockIdx.x + gridDim.x, ... ----
-  for (int row = blockIdx.x; row < p.m; row += gridDim.x) {
+  // ---- phase B: (row, chunk of this rank's slice) items, every thread one pair of columns,
+  // so a slice of any width is one poll per thread ----
+  for (int item = blockIdx.x; item < p.m * p.bchunks; item += gridDim.x) {
+    const int row = item / p.bchunks, cb = item % p.bchunks;
     float ss = 0.f;
-    for (int j = threadIdx.x; j < slice / 2; j += kThreads) {
+    const int j = cb * kThreads + threadIdx.x;  // pair index within the slice
+    if (2 * j < slice) {
       const int col = p.rank * slice + 2 * j;
       float x0, x1;
       poll_pair(p.rs + use_rs + static_cast<size_t>(row) * slice + 2 * j, static_cast<size_t>(p.m) * slice, W,
@@ -185,7 +191,7 @@ __global__ void __launch_bounds__(kThreads) allreduce_norm_kernel(const __grid_c
       float total = 0.f;
       for (int i = 0; i < kThreads / 32; ++i) total += scratch[i];
       const uint64_t word = hi | __float_as_uint(total);
-      const size_t off = use_ss + static_cast<size_t>(p.rank) * p.m + row;
+      const size_t off = use_ss + (static_cast<size_t>(p.rank) * p.bchunks + cb) * p.m + row;
       for (int q = 0; q < W; ++q)
         asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p.peer_ss[q] + off), "l"(word) : "memory");
     }
@@ -197,15 +203,19 @@ __global__ void __launch_bounds__(kThreads) allreduce_norm_kernel(const __grid_c
     const int row = item / p.chunks, chunk = item % p.chunks;
     const int col = chunk * kChunk + 2 * threadIdx.x;
     if (col >= p.n) continue;
-    // the row's partial sums of squares, added in rank order (the same bits on every rank)
-    uint64_t words[kMaxWorld];
+    // the row's partial sums of squares (per rank, per slice chunk), added in rank order and
+    // chunk order (the same bits on every rank)
     float total = 0.f;
-    if (poll_words(p.ss + use_ss + row, p.m, W, flag, p.err, words)) {
+    for (int q = 0; q < W; ++q) {
+      uint64_t words[kMaxSliceChunks];
+      if (poll_words(p.ss + use_ss + static_cast<size_t>(q) * p.bchunks * p.m + row, p.m, p.bchunks, flag, p.err,
+                     words)) {
 #pragma unroll
-      for (int q = 0; q < kMaxWorld; ++q)
-        if (q < W) total += __uint_as_float(static_cast<uint32_t>(words[q]));
+        for (int c = 0; c < kMaxSliceChunks; ++c)
+          if (c < p.bchunks) total += __uint_as_float(static_cast<uint32_t>(words[c]));
+      }
     }
-    uint64_t pair[kMaxWorld];
+    uint64_t pair[kMaxSliceChunks];
     float s0 = 0.f, s1 = 0.f;
     if (poll_words(p.ag + use_ag + static_cast<size_t>(row) * half + col / 2, 0, 1, flag, p.err, pair)) {
       s0 = bf16_lo(static_cast<uint32_t>(pair[0]));
@@ -280,10 +290,12 @@ extern "C" int fb_allreduce_add_rmsnorm(const void* rs, const void* ag, const vo
   p.rank = rank;
   p.use = use;
   p.chunks = (width + ar::kChunk - 1) / ar::kChunk;
+  p.bchunks = (width / world + ar::kChunk - 1) / ar::kChunk;
+  if (p.bchunks > ar::kMaxSliceChunks) return FB_ERR_SHAPE;
   p.eps = eps;
   p.err = error_word();
   // every CTA resident at once (phase C waits on phase B of other CTAs, here and on the peers)
-  long long grid = static_cast<long long>(rows) * p.chunks;
+  long long grid = static_cast<long long>(rows) * (p.chunks > p.bchunks ? p.chunks : p.bchunks);
   if (grid > sm_count()) grid = sm_count();
   return launch_ex(ar::allreduce_norm_kernel, dim3(static_cast<unsigned>(grid)), dim3(ar::kThreads), 0,
                    static_cast<cudaStream_t>(stream), 1, p);

@@ -219,15 +219,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int key0 = j * kTile + 64 * half;  // this warp's first key
       // a tile below the diagonal is visible to every query row of this tile
       const bool interior = j < qt;
+      // this warp's 64 scores of the row, read from TMEM once and kept for the P pass
+      float sv[64];
+      {
+        float* lo = sv;
+        float* hi = sv + 32;
+        tc::ld32(s_addr, *reinterpret_cast<float(*)[32]>(lo));
+        tc::ld32(s_addr + 32, *reinterpret_cast<float(*)[32]>(hi));
+      }
+      // S_x is free for the score product of tile j + 2 as soon as both halves are read
+      tc::fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[x]);
       float mx = -INFINITY;
 #pragma unroll
-      for (int c0 = 0; c0 < 64; c0 += 32) {
-        float v[32];
-        tc::ld32(s_addr + c0, v);
-#pragma unroll
-        for (int c = 0; c < 32; ++c)
-          if (interior || key0 + c0 + c <= last_key) mx = fmaxf(mx, v[c] * sl2);
-      }
+      for (int c = 0; c < 64; ++c)
+        if (interior || key0 + c <= last_key) mx = fmaxf(mx, sv[c] * sl2);
       // the row's other half: exchange partial maxima through TMEM column [parity][half]
       tc::st1(tmem + kTmemXchg + 2 * x + half + lane_base, mx);
       tc::fence_before();
@@ -242,6 +249,37 @@ __global__ void __launch_bounds__(kThreads, 1)
         pivot = mx;
       }
       lsum *= corr;
+      // P tile x was last read by the product of tile j - 2
+      if (j >= 2) {
+        const bool free = mbar_wait_bounded(&o_done[x], ((j - 2) >> 1) & 1);
+        if (!__all_sync(0xffffffffu, free)) {
+          ok = false;
+          break;
+        }
+      }
+      const float piv = pivot == -INFINITY ? 0.f : pivot;
+      // this warp's 64 keys are box `half` of the K-major P tile
+      uint8_t* pt = p_s + x * S::kPBytes + half * S::kBox;
+#pragma unroll
+      for (int c0 = 0; c0 < 64; c0 += 32) {
+        const float* v = sv + c0;
+        uint32_t packed[16];
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {
+          const bool see0 = interior || key0 + c0 + c <= last_key;
+          const bool see1 = interior || key0 + c0 + c + 1 <= last_key;
+          const float p0 = see0 ? tc::ex2_approx(v[c] * sl2 - piv) : 0.f;
+          const float p1 = see1 ? tc::ex2_approx(v[c + 1] * sl2 - piv) : 0.f;
+          lsum += p0 + p1;
+          packed[c / 2] = pack_bf16x2(p0, p1);
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          *reinterpret_cast<uint4*>(pt + sw128(row, (c0 >> 3) + q)) =
+              make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+      }
+      // O rescale after the P pass (the scores are dead by then): the product of tile j - 1 must
+      // have landed, and the product of tile j waits for p_full below
       if (j >= 1 && __any_sync(0xffffffffu, need)) {
         // the previous tile's product must have landed in O before this warp's half of the
         // rows' O is rescaled (rows that keep their pivot multiply by 1)
@@ -260,39 +298,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc::st32(tmem_o + half * (kDim / 2) + lane_base + c0, o);
         }
       }
-      // P tile x was last read by the product of tile j - 2
-      if (j >= 2) {
-        const bool free = mbar_wait_bounded(&o_done[x], ((j - 2) >> 1) & 1);
-        if (!__all_sync(0xffffffffu, free)) {
-          ok = false;
-          break;
-        }
-      }
-      const float piv = pivot == -INFINITY ? 0.f : pivot;
-      // this warp's 64 keys are box `half` of the K-major P tile
-      uint8_t* pt = p_s + x * S::kPBytes + half * S::kBox;
-#pragma unroll
-      for (int c0 = 0; c0 < 64; c0 += 32) {
-        float v[32];
-        tc::ld32(s_addr + c0, v);
-        uint32_t packed[16];
-#pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          const bool see0 = interior || key0 + c0 + c <= last_key;
-          const bool see1 = interior || key0 + c0 + c + 1 <= last_key;
-          const float p0 = see0 ? tc::ex2_approx(v[c] * sl2 - piv) : 0.f;
-          const float p1 = see1 ? tc::ex2_approx(v[c + 1] * sl2 - piv) : 0.f;
-          lsum += p0 + p1;
-          packed[c / 2] = pack_bf16x2(p0, p1);
-        }
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          *reinterpret_cast<uint4*>(pt + sw128(row, (c0 >> 3) + q)) =
-              make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
-      }
-      tc::fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[x]);
       // V rows past the prompt: zeroed so stale cache values never meet a zero weight
       if (half == 0 && j * kTile + kTile > p.tokens && j * kTile + row >= p.tokens) {
         uint8_t* vt = stages + x * S::kStageBytes + S::kTileBytes;
@@ -302,7 +307,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int c16 = 0; c16 < 8; ++c16)
             *reinterpret_cast<uint4*>(vt + bx * S::kBox + row * 128 + c16 * 16) = make_uint4(0, 0, 0, 0);
       }
-      fence_proxy_async_smem();
+      tc::fence_before();        // the rescaled O (TMEM) before the product of tile j
+      fence_proxy_async_smem();  // P and zeroed V rows (shared memory) before the product
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[x]);
     }

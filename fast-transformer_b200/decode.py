@@ -94,7 +94,8 @@ class PeerBuffers:
     one can fault its peers), uint64 words carrying a 32-bit flag each:
       rs [uses, world, rows, width/world]  fp32 partials this rank receives as a slice owner
       ag [uses, rows, width/2]             summed bf16 pairs of whole rows
-      ss [uses, world, rows]               each owner's sum of squares of its slice of a row
+      ss [uses, world, chunks, rows]       each owner's sums of squares of its slice of a row, per
+                                           512-column chunk of the slice
       exchange [rows, world, 2]            the vocabulary-parallel argmax's bests
     with every rank's base address of each region."""
 
@@ -108,7 +109,8 @@ class PeerBuffers:
             return (nbytes + 255) // 256 * 256
 
         sizes = {"rs": pad(uses * rows * width * 8), "ag": pad(uses * rows * (width // 2) * 8),
-                 "ss": pad(uses * world * rows * 8), "exchange": pad(rows * world * 2 * 8)}
+                 "ss": pad(uses * world * (-(-(width // world) // 512)) * rows * 8),
+                 "exchange": pad(rows * world * 2 * 8)}
         offsets, total = {}, 0
         for name, size in sizes.items():
             offsets[name] = total

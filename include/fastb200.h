@@ -297,17 +297,18 @@ int fb_spec_relocate(void* store, int planes, int batch, int kv_heads, int capac
  * aligned; zero them before first use and again before *epoch can repeat a value it had):
  *   rs [uses, world, M, N/world]  fp32 partials pushed to this rank as the owner
  *   ag [uses, M, N/2]             summed bf16 pairs of whole rows, from every owner
- *   ss [uses, world, M]           each owner's fp32 sum of squares of its slice of a row
+ *   ss [uses, world, C, M]        each owner's fp32 sums of squares of its slice of a row, per
+ *                                 512-column chunk of the slice: C = ceil(N / world / 512) <= 16
  * fb_reduce_scatter_push sums this rank's fp32 split-K partials [splits, M, N] of y = x @ W^T in
  *   split order and stores every value only into the owner's rs[use][rank] (peer_rs[q] =
  *   rank q's rs base). N % (2 * world) == 0.
  * fb_allreduce_add_rmsnorm (one launch): as the owner, polls rs[use] (bounded, 2 s), sums the
  *   ranks in rank order, rounds to bf16, adds `residual` (rounded again: the bf16 residual sum
- *   of add_rms_norm), stores the summed pairs into every rank's ag[use] and the slice's sum of
- *   squares per row into every rank's ss[use][rank]; then polls its own ag[use] and ss[use] and
- *   writes, for every row, `sum` (the summed row, the next residual) and `out` =
- *   bf16(bf16(sum * rsqrt(mean(sum^2) + eps)) * w), the sums of squares added in rank order (the
- *   same bits on every rank). residual/out/sum bf16 [M, N], w bf16 [N]. One call per use per
+ *   of add_rms_norm), stores the summed pairs into every rank's ag[use] and the slice's sums of
+ *   squares per row and chunk into every rank's ss[use][rank]; then polls its own ag[use] and
+ *   ss[use] and writes, for every row, `sum` (the summed row, the next residual) and `out` =
+ *   bf16(bf16(sum * rsqrt(mean(sum^2) + eps)) * w), the sums of squares added in rank order and
+ *   chunk order (the same bits on every rank). residual/out/sum bf16 [M, N], w bf16 [N]. One call per use per
  *   step, in the same order on every rank.
  * ---------------------------------------------------------------------------------- */
 int fb_reduce_scatter_push(const void* partials, int splits, int m, int n, int world, int rank, int use,

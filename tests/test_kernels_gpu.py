@@ -469,7 +469,7 @@ def test_allreduce_single_rank():
         ordered += part[s]
     rs = torch.zeros(2, 1, m, n, dtype=torch.int64, device=DEV)  # two uses
     ag = torch.zeros(2, m, n // 2, dtype=torch.int64, device=DEV)
-    ss = torch.zeros(2, 1, m, dtype=torch.int64, device=DEV)
+    ss = torch.zeros(2, 1, n // 512, m, dtype=torch.int64, device=DEV)  # [uses, world, slice chunks, rows]
     use = 1
     check(lib.fb_reduce_scatter_push(ptr(part), splits, m, n, 1, 0, use, (ctypes.c_void_p * 1)(rs.data_ptr()),
                                      ptr(epoch), stream()), "fb_reduce_scatter_push")
