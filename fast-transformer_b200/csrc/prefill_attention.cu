@@ -231,10 +231,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[x]);
+      // raw maximum, scaled once: sl2 > 0 and rounding is monotone, so max(s) * sl2 equals
+      // max(s * sl2). Interior tiles take the mask-free path.
       float mx = -INFINITY;
+      if (interior) {
 #pragma unroll
-      for (int c = 0; c < 64; ++c)
-        if (interior || key0 + c <= last_key) mx = fmaxf(mx, sv[c] * sl2);
+        for (int c = 0; c < 64; ++c) mx = fmaxf(mx, sv[c]);
+      } else {
+#pragma unroll
+        for (int c = 0; c < 64; ++c)
+          if (key0 + c <= last_key) mx = fmaxf(mx, sv[c]);
+      }
+      if (mx != -INFINITY) mx *= sl2;
       // the row's other half: exchange partial maxima through TMEM column [parity][half]
       tc::st1(tmem + kTmemXchg + 2 * x + half + lane_base, mx);
       tc::fence_before();
@@ -265,13 +273,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float* v = sv + c0;
         uint32_t packed[16];
 #pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          const bool see0 = interior || key0 + c0 + c <= last_key;
-          const bool see1 = interior || key0 + c0 + c + 1 <= last_key;
-          const float p0 = see0 ? tc::ex2_approx(v[c] * sl2 - piv) : 0.f;
-          const float p1 = see1 ? tc::ex2_approx(v[c + 1] * sl2 - piv) : 0.f;
-          lsum += p0 + p1;
-          packed[c / 2] = pack_bf16x2(p0, p1);
+        if (interior) {
+#pragma unroll
+          for (int c = 0; c < 32; c += 2) {
+            const float p0 = tc::ex2_approx(fmaf(v[c], sl2, -piv));
+            const float p1 = tc::ex2_approx(fmaf(v[c + 1], sl2, -piv));
+            lsum += p0 + p1;
+            packed[c / 2] = pack_bf16x2(p0, p1);
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 32; c += 2) {
+            const bool see0 = key0 + c0 + c <= last_key;
+            const bool see1 = key0 + c0 + c + 1 <= last_key;
+            const float p0 = see0 ? tc::ex2_approx(fmaf(v[c], sl2, -piv)) : 0.f;
+            const float p1 = see1 ? tc::ex2_approx(fmaf(v[c + 1], sl2, -piv)) : 0.f;
+            lsum += p0 + p1;
+            packed[c / 2] = pack_bf16x2(p0, p1);
+          }
         }
 #pragma unroll
         for (int q = 0; q < 4; ++q)
