@@ -89,10 +89,7 @@ def test_decode_attention_config3_ragged(batch):
     draws = {}
     for b in (1, 4, 16, 64):  # one draw per B, in that order
         draws[b] = torch.randint(1024, 32769, (b,), generator=gen).tolist()
-    lengths = draws[batch]
-    if batch == 64:
-        lengths = lengths[:32]  # bound the fp32 check's memory; the sweep bench runs all 64
-        batch = 32
+    lengths = draws[batch]  # all rows, B = 64 included (~9 GB of K/V at the longest draw)
     q, k, v, position = _ragged(batch, 32, 8, 128, lengths, seed=batch)
     out = decode_attention(q, k, v, position, 1 / math.sqrt(128))
     expect = torch_fp32_decode(q, k, v, lengths, 1 / math.sqrt(128))
