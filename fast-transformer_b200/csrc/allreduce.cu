@@ -80,6 +80,39 @@ __global__ void __launch_bounds__(kThreads) reduce_scatter_push_kernel(const __g
                : "memory");
 }
 
+// The one-phase form's producer: the same split-order sum, then each pair of values, flagged,
+// into slab `rank` of recv[use] on every rank (fb_allreduce_sum_add_rmsnorm, in norms.cu, polls
+// all slabs and sums them in rank order).
+__global__ void __launch_bounds__(kThreads) push_all_kernel(const __grid_constant__ PushParams p) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t i = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) * 2;
+  const int64_t count = static_cast<int64_t>(p.m) * p.n;
+  if (i >= count) return;
+  float2 x = make_float2(0.f, 0.f);
+  for (int s0 = 0; s0 < p.splits; s0 += kBatch) {
+    float2 part[kBatch];
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j)
+      if (s0 + j < p.splits) part[j] = __ldcg(reinterpret_cast<const float2*>(p.partials + (s0 + j) * count + i));
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      if (s0 + j == 0) {
+        x = part[0];
+      } else if (s0 + j < p.splits) {
+        x.x += part[j].x;
+        x.y += part[j].y;
+      }
+    }
+  }
+  const uint64_t flag = static_cast<uint64_t>(static_cast<uint32_t>(*p.epoch) + 1u) << 32;
+  const uint64_t w0 = flag | __float_as_uint(x.x), w1 = flag | __float_as_uint(x.y);
+  const size_t off = (static_cast<size_t>(p.use) * p.world + p.rank) * count + i;
+  for (int q = 0; q < p.world; ++q)
+    asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p.peer_rs[q] + off), "l"(w0), "l"(w1)
+                 : "memory");
+}
+
 struct NormParams {
   const uint64_t* rs;             // this rank's reduce-scatter slabs, all uses
   const uint64_t* ag;             // this rank's all-gather rows, all uses
@@ -298,5 +331,30 @@ extern "C" int fb_allreduce_add_rmsnorm(const void* rs, const void* ag, const vo
   long long grid = static_cast<long long>(rows) * (p.chunks > p.bchunks ? p.chunks : p.bchunks);
   if (grid > sm_count()) grid = sm_count();
   return launch_ex(ar::allreduce_norm_kernel, dim3(static_cast<unsigned>(grid)), dim3(ar::kThreads), 0,
+                   static_cast<cudaStream_t>(stream), 1, p);
+}
+
+extern "C" int fb_allreduce_push(const void* partials, int splits, int m, int n, int world, int rank, int use,
+                                 void* const* peer_recv, const int64_t* epoch, void* stream) {
+  if (!partials || !peer_recv || !epoch || splits <= 0 || m <= 0 || n <= 0) return FB_ERR_ARG;
+  if (world < 1 || world > ar::kMaxWorld || rank < 0 || rank >= world || use < 0) return FB_ERR_ARG;
+  if (n % 2 != 0) return FB_ERR_SHAPE;
+  ar::PushParams p{};
+  p.partials = static_cast<const float*>(partials);
+  p.splits = splits;
+  p.m = m;
+  p.n = n;
+  p.world = world;
+  p.rank = rank;
+  p.use = use;
+  p.epoch = epoch;
+  for (int r = 0; r < world; ++r) {
+    if (!peer_recv[r] || (reinterpret_cast<uintptr_t>(peer_recv[r]) & 15u)) return FB_ERR_ARG;
+    p.peer_rs[r] = static_cast<uint64_t*>(peer_recv[r]);
+  }
+  const int64_t threads = static_cast<int64_t>(m) * n / 2;
+  const int64_t blocks = (threads + ar::kThreads - 1) / ar::kThreads;
+  if (blocks >= (1ll << 31)) return FB_ERR_SHAPE;
+  return launch_ex(ar::push_all_kernel, dim3(static_cast<unsigned>(blocks)), dim3(ar::kThreads), 0,
                    static_cast<cudaStream_t>(stream), 1, p);
 }

@@ -17,6 +17,7 @@ constexpr int kMaxThreads = 256;  // RMSNorm CTAs
 constexpr int kMaxPer = 4;        // 8-wide chunks per RMSNorm thread
 constexpr int kMaxCluster = 8;    // CTAs sharing one RMSNorm row
 constexpr int kSlabBatch = 8;     // split slabs whose loads are in flight together
+constexpr int kMaxWorld = 8;      // tensor-parallel ranks summed by mode 3
 
 // 8 consecutive logical bf16 values starting at element `off` of a tensor that is either
 // bf16 (splits == 0) or fp32 split partials [splits, slab] (splits >= 1). Up to eight slabs
@@ -111,11 +112,63 @@ __device__ __forceinline__ float block_sum(float v, float* scratch) {
   return t;
 }
 
+// Mode 3 input: 8 consecutive values of each of `world` slabs of flagged words (low half the
+// fp32 bits, high half the flag), summed in rank order and rounded to bf16 once every word
+// carries `flag`. Polls with all slabs' loads in flight; gives up after the wait budget (or
+// at once if an earlier wait already gave up) and returns false.
+__device__ __forceinline__ bool load8_flagged(const uint64_t* src, int world, size_t slab, uint32_t flag,
+                                              unsigned* err, float (&x)[8]) {
+  unsigned long long start = 0;
+  for (;;) {
+    bool ready = true;
+    // two passes of four ranks keep 32 words in flight per thread
+#pragma unroll
+    for (int q0 = 0; q0 < kMaxWorld; q0 += 4) {
+      uint64_t w[4][8];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (q0 + j < world) {
+          const uint64_t* s = src + (q0 + j) * slab;
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];"
+                         : "=l"(w[j][2 * i]), "=l"(w[j][2 * i + 1])
+                         : "l"(s + 2 * i));
+        }
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (q0 + j < world) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            ready = ready && static_cast<uint32_t>(w[j][e] >> 32) == flag;
+            const float v = __uint_as_float(static_cast<uint32_t>(w[j][e]));
+            x[e] = q0 + j == 0 ? v : x[e] + v;
+          }
+        }
+    }
+    if (ready) break;
+    if (start == 0) start = globaltimer();
+    if ((err != nullptr && (*reinterpret_cast<volatile unsigned*>(err) & kErrTimeoutFull) != 0) ||
+        globaltimer() - start > kWaitBudgetNs) {
+      raise_error(err, kErrTimeoutFull);
+      return false;
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) x[e] = bf16_round(x[e]);
+  return true;
+}
+
 // mode 0: rms_norm(x)          mode 1: add_rms_norm(x, residual)
-// mode 2: embed + rms_norm
+// mode 2: embed + rms_norm     mode 3: tensor-parallel all-reduce + add_rms_norm
+//
+// Mode 3: every rank pushed its fp32 [rows, W] partial, as flagged words, into slab `rank` of
+// this rank's receive buffer (fb_allreduce_push); once every word carries this step's flag the
+// slabs are summed in rank order (identical bits on every rank), rounded to bf16 (the
+// projection's output) and fed to add_rms_norm's arithmetic.
 struct Params {
-  const void* x;
-  int splits;             // fp32 slabs in x (0: x is bf16)
+  const void* x;          // mode 3: this use's receive slabs, uint64 words [world, rows, W]
+  int splits;             // fp32 slabs in x (0: x is bf16); mode 3: world
   int64_t row_stride;     // mode 0
   const __nv_bfloat16* residual;
   const __nv_bfloat16* w;
@@ -123,6 +176,7 @@ struct Params {
   __nv_bfloat16* sum;
   const int64_t* ids;     // mode 2
   int64_t vocab;
+  const int64_t* epoch;   // mode 3: the flag is (uint32)(*epoch) + 1
   int rows, width;
   float eps;
   unsigned* err;
@@ -166,7 +220,8 @@ __global__ void __launch_bounds__(kMaxThreads) rmsnorm_kernel(const Params p) {
     }
     base = static_cast<size_t>(id) * p.width;
   }
-  const int split_count = MODE == 1 ? p.splits : 0;
+  const uint32_t flag = MODE == 3 ? static_cast<uint32_t>(*p.epoch) + 1u : 0u;
+  const int split_count = (MODE == 1 || MODE == 3) ? p.splits : 0;
   const size_t slab = static_cast<size_t>(p.rows) * p.width;
   // Every CTA of the row's cluster announces that it runs; the wait below, before the first
   // remote shared-memory store, then costs nothing.
@@ -174,7 +229,7 @@ __global__ void __launch_bounds__(kMaxThreads) rmsnorm_kernel(const Params p) {
   // The residual's loads are issued with (not after) the input's: it was written before the
   // previous kernel completed.
   float res[kMaxPer][8];
-  if (MODE == 1) {
+  if (MODE == 1 || MODE == 3) {
 #pragma unroll
     for (int i = 0; i < kMaxPer; ++i) {
       const int ch = c0 + threadIdx.x + i * T;
@@ -187,8 +242,14 @@ __global__ void __launch_bounds__(kMaxThreads) rmsnorm_kernel(const Params p) {
   for (int i = 0; i < kMaxPer; ++i) {
     const int ch = c0 + threadIdx.x + i * T;
     if (ch < c1) {
-      load8(src, split_count, slab, base + ch * 8, v[i]);
-      if (MODE == 1) {
+      if (MODE == 3) {
+        if (!load8_flagged(static_cast<const uint64_t*>(src) + base + ch * 8, p.splits, slab, flag, p.err, v[i]))
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[i][e] = 0.f;
+      } else {
+        load8(src, split_count, slab, base + ch * 8, v[i]);
+      }
+      if (MODE == 1 || MODE == 3) {
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[i][e] = bf16_round(v[i][e] + res[i][e]);
         store8(p.sum + static_cast<size_t>(row) * p.width + ch * 8, v[i]);
@@ -448,4 +509,27 @@ extern "C" int fb_merge_splits(const void* partial, int splits, int64_t count, v
   const int blocks = static_cast<int>((threads + norm::kThreads - 1) / norm::kThreads);
   return launch_ex(norm::merge_kernel, dim3(blocks), dim3(norm::kThreads), 0, static_cast<cudaStream_t>(stream), 1,
                    static_cast<const float*>(partial), splits, count, out, out_fp32);
+}
+
+extern "C" int fb_allreduce_sum_add_rmsnorm(const void* recv, int use, int world, const int64_t* epoch,
+                                            const void* residual, const void* w, void* out, void* sum, int rows,
+                                            int width, float eps, void* stream) {
+  if (!recv || !epoch || !residual || !w || !out || !sum) return FB_ERR_ARG;
+  if (use < 0 || world < 1 || world > norm::kMaxWorld || rows <= 0) return FB_ERR_ARG;
+  int st = norm::check_width(width);
+  if (st != FB_OK) return st;
+  const size_t slab = static_cast<size_t>(rows) * width;
+  norm::Params p{};
+  p.x = static_cast<const uint64_t*>(recv) + static_cast<size_t>(use) * world * slab;
+  p.splits = world;
+  p.epoch = epoch;
+  p.residual = static_cast<const __nv_bfloat16*>(residual);
+  p.w = static_cast<const __nv_bfloat16*>(w);
+  p.y = static_cast<__nv_bfloat16*>(out);
+  p.sum = static_cast<__nv_bfloat16*>(sum);
+  p.rows = rows;
+  p.width = width;
+  p.eps = eps;
+  p.err = error_word();
+  return norm::launch_rmsnorm<3>(p, stream);
 }

@@ -88,29 +88,48 @@ class Communicator:
         return tensor
 
 
+#: The step's all-reduce form: "push" (one NVLink phase: every rank pushes its whole partial to
+#: every rank, each sums all ranks; fb_allreduce_push + fb_allreduce_sum_add_rmsnorm) or "owner"
+#: (owner-computes reduce-scatter + all-gather, a quarter to an eighth of the volume in two
+#: phases; fb_reduce_scatter_push + fb_allreduce_add_rmsnorm). Same bits on every rank in either.
+#: Measured on B200 (config 4, the same box per pair): push 4282 / 6024 tok/s at 2/4 ranks
+#: (0.09 / 0.32 ms of all-reduce per step), owner 4080-4099 / 5593 (0.28-0.31 / 0.52 ms).
+#: FB_TP_ALLREDUCE overrides the default.
+ALLREDUCE_FORM = os.environ.get("FB_TP_ALLREDUCE", "push")
+
+
 class PeerBuffers:
     """The tensor-parallel all-reduce's receive regions in torch symmetric memory (plain NVLink
     peer mappings, never bound to an NVSwitch multicast object: a rank that dies while bound to
-    one can fault its peers), uint64 words carrying a 32-bit flag each:
+    one can fault its peers), uint64 words carrying a 32-bit flag each. The push form:
+      recv [uses, world, rows, width]      every rank's fp32 partial
+    the owner form:
       rs [uses, world, rows, width/world]  fp32 partials this rank receives as a slice owner
       ag [uses, rows, width/2]             summed bf16 pairs of whole rows
       ss [uses, world, chunks, rows]       each owner's sums of squares of its slice of a row, per
                                            512-column chunk of the slice
+    and in both
       exchange [rows, world, 2]            the vocabulary-parallel argmax's bests
     with every rank's base address of each region."""
 
-    def __init__(self, comm, uses, rows, width, device):
+    def __init__(self, comm, uses, rows, width, device, form=None):
         os.environ["TORCH_SYMM_MEM_DISABLE_MULTICAST"] = "1"
         import torch.distributed._symmetric_memory as symm_mem
         world = comm.size
         self.uses, self.world, self.rows, self.width = uses, world, rows, width
+        self.form = form or ALLREDUCE_FORM
+        if self.form not in ("push", "owner"):
+            raise ValueError(f"unknown all-reduce form {self.form!r}")
 
         def pad(nbytes):
             return (nbytes + 255) // 256 * 256
 
-        sizes = {"rs": pad(uses * rows * width * 8), "ag": pad(uses * rows * (width // 2) * 8),
-                 "ss": pad(uses * world * (-(-(width // world) // 512)) * rows * 8),
-                 "exchange": pad(rows * world * 2 * 8)}
+        if self.form == "push":
+            sizes = {"recv": pad(uses * world * rows * width * 8)}
+        else:
+            sizes = {"rs": pad(uses * rows * width * 8), "ag": pad(uses * rows * (width // 2) * 8),
+                     "ss": pad(uses * world * (-(-(width // world) // 512)) * rows * 8)}
+        sizes["exchange"] = pad(rows * world * 2 * 8)
         offsets, total = {}, 0
         for name, size in sizes.items():
             offsets[name] = total
@@ -164,11 +183,13 @@ def _qkv_rope_decode(x, layer, eps, cos, sin, position, keys, values, q_heads):
 
 def _allreduce_add_norm(x, weight, comm, peers, use, epoch, residual, gain, eps, splits=None):
     """(normalized, summed) = add_rms_norm(all-reduce over ranks of x @ W^T, residual): the
-    projection writes fp32 split partials, fb_reduce_scatter_push sums them in split order and
-    pushes each value, flagged with epoch + 1, to the rank owning its column slice, and
-    fb_allreduce_add_rmsnorm has every owner sum its slice over the ranks, add the residual and
-    share the summed slice with every rank, which normalizes whole rows. ``splits`` overrides
-    the K-split count (tests)."""
+    projection writes fp32 split partials, summed in split order and stored, flagged with
+    epoch + 1, by NVLink peer stores. Push form: fb_allreduce_push stores this rank's whole
+    partial into every rank's recv[use][rank] and fb_allreduce_sum_add_rmsnorm sums all ranks'
+    slabs in rank order and applies add+RMSNorm. Owner form: fb_reduce_scatter_push stores each
+    value only to the rank owning its column slice and fb_allreduce_add_rmsnorm has every owner
+    sum its slice, add the residual and share the summed slice with every rank, which normalizes
+    whole rows. ``splits`` overrides the K-split count (tests)."""
     rows = x.numel() // x.shape[-1]
     flat = x.reshape(rows, x.shape[-1]).contiguous()
     n, k = weight.shape
@@ -178,6 +199,13 @@ def _allreduce_add_norm(x, weight, comm, peers, use, epoch, residual, gain, eps,
     if splits is None:
         splits = klinear.splits_for(rows, n, k, x.device)
     partials = klinear.project(flat, weight, klinear.SPLITS_OUT, splits)
+    if peers.form == "push":
+        check(lib.fb_allreduce_push(ptr(partials), splits, rows, n, comm.size, comm.rank, use, peers.recv_ptrs,
+                                    ptr(epoch), stream()), "fb_allreduce_push")
+        check(lib.fb_allreduce_sum_add_rmsnorm(peers.recv_local, use, peers.world, ptr(epoch), ptr(residual),
+                                               ptr(gain), ptr(out), ptr(summed), rows, width, float(eps), stream()),
+              "fb_allreduce_sum_add_rmsnorm")
+        return out, summed
     check(lib.fb_reduce_scatter_push(ptr(partials), splits, rows, n, comm.size, comm.rank, use, peers.rs_ptrs,
                                      ptr(epoch), stream()), "fb_reduce_scatter_push")
     check(lib.fb_allreduce_add_rmsnorm(peers.rs_local, peers.ag_local, peers.ss_local, peers.ag_ptrs, peers.ss_ptrs,

@@ -59,6 +59,9 @@ _SIGNATURES = {
     "fb_merge_splits": (_c_int, [_vp, _c_int, _c_i64, _vp, _c_int, _vp]),
     "fb_swiglu_blocked": (_c_int, [_vp, _c_int, _vp, _c_int, _c_int, _vp]),
     "fb_reduce_scatter_push": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp]),
+    "fb_allreduce_push": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp]),
+    "fb_allreduce_sum_add_rmsnorm": (_c_int, [_vp, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_float,
+                                              _vp]),
     "fb_prefill_attention": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float,
                                       _vp]),
     "fb_spec_propose": (_c_int, [_vp, _c_i64, _vp, _vp, _c_i64, _c_int, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int,

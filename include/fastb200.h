@@ -318,6 +318,26 @@ int fb_allreduce_add_rmsnorm(const void* rs, const void* ag, const void* ss, voi
                              const void* residual, const void* w, void* out, void* sum, int rows,
                              int width, float eps, void* stream);
 
+/* The same all-reduce + add + RMSNorm in one NVLink phase (push form; no counterpart in the
+ * reference, like the owner form above, whose flag protocol and epoch rules it shares). Each
+ * rank owns one uint64 region recv [uses, world, M, N] (16-byte aligned, zeroed like the owner
+ * form's regions).
+ * fb_allreduce_push sums this rank's fp32 split-K partials [splits, M, N] in split order and
+ *   stores every value into recv[use][rank] of every rank (peer_recv[q] = rank q's recv base):
+ *   world * M * N * 8 bytes per rank and use. N % 2 == 0.
+ * fb_allreduce_sum_add_rmsnorm polls its own recv[use] (bounded, 2 s) until every word of every
+ *   rank's slab carries the flag, sums the slabs in rank order (the same bits on every rank),
+ *   rounds to bf16 and applies add_rms_norm (engine/kernels/rmsnorm.py:75-95 arithmetic):
+ *   `sum` = bf16(x + residual), `out` = bf16(bf16(sum * rsqrt(mean(sum^2) + eps)) * w). Each row
+ *   is reduced inside one thread-block cluster (no cross-CTA polling), so there is no second
+ *   NVLink phase. Measured faster than the owner form at 2 and 4 ranks (config 4).
+ * ---------------------------------------------------------------------------------- */
+int fb_allreduce_push(const void* partials, int splits, int m, int n, int world, int rank, int use,
+                      void* const* peer_recv, const int64_t* epoch, void* stream);
+int fb_allreduce_sum_add_rmsnorm(const void* recv, int use, int world, const int64_t* epoch,
+                                 const void* residual, const void* w, void* out, void* sum, int rows,
+                                 int width, float eps, void* stream);
+
 /* Sums fp32 split partials [splits, count] into bf16 [count] (or fp32 when out_fp32):
  * the reference's `_merge_projection` (linear.py:81-93). */
 int fb_merge_splits(const void* partial, int splits, int64_t count, void* out, int out_fp32,

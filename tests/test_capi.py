@@ -83,6 +83,12 @@ def test_host_validation_without_gpu():
     assert lib.fb_allreduce_add_rmsnorm(p, p, p, peers, peers, 0, 9, 0, p, p, p, p, p, 4, 4096, 1e-6, null) == -1
     assert lib.fb_allreduce_add_rmsnorm(p, p, p, peers, peers, 0, 2, 0, p, p, p, p, p, 4, 4100, 1e-6, null) == -2
     assert lib.fb_allreduce_add_rmsnorm(null, p, p, peers, peers, 0, 2, 0, p, p, p, p, p, 4, 4096, 1e-6, null) == -1
+    # push form: argument checks only (no launch)
+    assert lib.fb_allreduce_push(p, 2, 4, 7, 2, 0, 0, peers, p, null) == -2       # odd width
+    assert lib.fb_allreduce_push(p, 2, 4, 8, 2, 2, 0, peers, p, null) == -1       # rank >= world
+    assert lib.fb_allreduce_push(p, 2, 4, 8, 2, 0, 0, odd, p, null) == -1         # not 16-byte aligned
+    assert lib.fb_allreduce_sum_add_rmsnorm(p, 0, 9, p, p, p, p, p, 4, 4096, 1e-6, null) == -1  # world > 8
+    assert lib.fb_allreduce_sum_add_rmsnorm(null, 0, 2, p, p, p, p, p, 4, 4096, 1e-6, null) == -1
     assert lib.fb_linear_argmax(p, p, 4, 128, 128, -1, p, null) == -1
     # workspace too small -> FB_ERR_WORKSPACE
     need = lib.fb_decode_attention_workspace(1, 16, 8, 128, 148)

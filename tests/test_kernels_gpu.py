@@ -115,7 +115,6 @@ def test_decode_attention_long_and_tiny_lengths():
     (16, 8, 2, 128, 4000),    # TP4: clusters of 4
     (2, 8, 2, 64, 100),       # 2 tiles over 8 ranks: empty slices
     (3, 32, 8, 128, 1),       # one valid slot
-    (4, 16, 1, 128, 65),      # G = 16 is not served (G <= 8): skipped below
     (1, 8, 1, 128, 30000),
 ])
 def test_decode_attention_cluster_form(batch, q_heads, kv_heads, dim, length):
@@ -123,8 +122,6 @@ def test_decode_attention_cluster_form(batch, q_heads, kv_heads, dim, length):
     merge): it must match the fp32 reference like the persistent form, which the same lengths
     given per row still take, and ignore NaN past the valid length."""
     from kernels.decode_attention import decode_attention
-    if q_heads // kv_heads > 8:
-        pytest.skip("GQA groups above 8 are outside the kernel's contract")
     lengths = [length] * batch
     q, k, v, position = _ragged(batch, q_heads, kv_heads, dim, lengths, seed=batch * 7 + length)
     shared = position[:1].contiguous()
@@ -162,6 +159,22 @@ def test_decode_attention_cluster_shapes(shape):
             lib.fb_decode_attention_cluster_shape(0, 0)
         assert torch.isfinite(out.float()).all()
         torch.testing.assert_close(out.float(), expect, atol=2e-2, rtol=2e-2)
+
+
+def test_decode_attention_groups_above_eight_are_refused():
+    """GQA groups above 8 query heads per KV head are outside the kernel's contract (G <= 8,
+    the mma N): the C entry point returns FB_ERR_SHAPE and writes nothing."""
+    from kernels._native import lib, ptr, stream
+    from kernels.decode_attention import _ctas, workspace_bytes
+    q, k, v, position = _ragged(4, 16, 1, 128, [65] * 4, seed=93)
+    out = torch.full((4, 1, 16, 128), 3.0, dtype=torch.bfloat16, device=DEV)
+    ctas = _ctas((q.device, 4, 1, k.shape[2], 128))
+    ws = torch.zeros(workspace_bytes(4, 16, 1, 128, ctas), dtype=torch.uint8, device=DEV)
+    status = lib.fb_decode_attention(ptr(q), ptr(k), ptr(v), ptr(position[:1].contiguous()), 0, ptr(out), ptr(ws),
+                                     ws.numel(), 4, 16, 1, 128, k.shape[2], 0.088, ctas, stream())
+    torch.cuda.synchronize()
+    assert status == -2
+    assert bool((out == 3.0).all())
 
 
 def test_decode_attention_forced_shape_beyond_one_wave_is_refused():

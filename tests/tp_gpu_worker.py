@@ -18,14 +18,15 @@ import decode as fdecode  # noqa: E402
 import qwen3  # noqa: E402
 
 
-def check_allreduce(comm, device, rank, world):
-    """The decode step's all-reduce (split partials + fb_reduce_push + fb_allreduce_add_rmsnorm)
-    through the add+RMSNorm consumer, at two K widths (different split counts): every rank gets
+def check_allreduce(comm, device, rank, world, form):
+    """The decode step's all-reduce in one of its forms (push: fb_allreduce_push +
+    fb_allreduce_sum_add_rmsnorm; owner: fb_reduce_scatter_push + fb_allreduce_add_rmsnorm) over
+    the projection's split partials, at two K widths (different split counts): every rank gets
     the same bits, close to an NCCL all-reduce of the fp32 partials followed by the same
     add + RMSNorm."""
     from kernels.rmsnorm import add_rms_norm
     widths = (512, 1536)
-    peers = fdecode.PeerBuffers(comm, len(widths), 16, 4096, device)
+    peers = fdecode.PeerBuffers(comm, len(widths), 16, 4096, device, form=form)
     epoch = torch.full((1,), 41, dtype=torch.int64, device=device)
     g = torch.Generator(device=device).manual_seed(100 + rank)
     residual = torch.randn(16, 4096, device=device, generator=torch.Generator(device=device).manual_seed(7)).bfloat16()
@@ -40,7 +41,7 @@ def check_allreduce(comm, device, rank, world):
         ref_out, ref_sum = add_rms_norm(partial.bfloat16(), residual, gain, 1e-6)
         gathered = [torch.empty_like(out) for _ in range(world)]
         dist.all_gather(gathered, out)
-        name = f"K={k}"
+        name = f"{form} K={k}"
         checks[f"{name} ranks agree"] = all(torch.equal(t, gathered[0]) for t in gathered)
         checks[f"{name} vs NCCL"] = bool((out.float() - ref_out.float()).abs().max() <= 0.05) and \
             bool((summed.float() - ref_sum.float()).abs().max() <= 0.05)
@@ -56,7 +57,8 @@ def main():
     ok = True
     try:
         comm0 = fdecode.Communicator(dist.group.WORLD, world, rank)
-        push_checks = check_allreduce(comm0, device, rank, world)
+        push_checks = check_allreduce(comm0, device, rank, world, "push")
+        push_checks.update(check_allreduce(comm0, device, rank, world, "owner"))
         if rank == 0:
             print("all-reduce", push_checks, flush=True)
         ok = all(push_checks.values())
