@@ -757,11 +757,16 @@ def main():
     if clock:
         line["clocks"] = clock
     if world > 1:
-        line["allreduce"] = ("owner-computes over NVLink peer stores: fb_reduce_scatter_push sums the projection's "
-                             "split-K partials and stores each fp32 value as a flagged word only to the rank that "
-                             "owns its column slice; fb_allreduce_add_rmsnorm sums the ranks in rank order per slice, "
-                             "adds the residual, all-gathers the summed bf16 rows and per-slice sums of squares, and "
-                             "applies the RMSNorm on every rank")
+        if fdecode.ALLREDUCE_FORM == "push":
+            line["allreduce"] = ("push form over NVLink peer stores: fb_allreduce_push sums the projection's split-K "
+                                 "partials and stores each fp32 value as a flagged word into every rank's receive "
+                                 "slab; fb_allreduce_sum_add_rmsnorm polls all slabs, sums the ranks in rank order "
+                                 "and applies add+RMSNorm (one NVLink phase)")
+        else:
+            line["allreduce"] = ("owner-computes over NVLink peer stores: fb_reduce_scatter_push stores each summed "
+                                 "fp32 value only to the rank owning its column slice; fb_allreduce_add_rmsnorm sums "
+                                 "the ranks per slice, adds the residual, all-gathers the summed rows and per-slice "
+                                 "sums of squares and applies the RMSNorm on every rank (two NVLink phases)")
         line["step_split"] = step_split
 
     if world == 1 and not args.no_sweep:
