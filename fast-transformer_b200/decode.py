@@ -11,12 +11,13 @@ the tcgen05 causal flash kernel (fb_prefill_attention) for the prompt attention,
 fused kernel writing the cache.
 
 Tensor parallelism (by KV head, see qwen3.py): o_proj and down_proj write fp32 split-K
-partials; fb_reduce_scatter_push sums them in split order and stores each value, as an 8-byte
-word carrying a flag (the decode position + 1), into the receive buffer of the rank that owns
-its column slice (torch symmetric memory, NVLink peer stores); fb_allreduce_add_rmsnorm has
-every owner sum its slice over the ranks in rank order, add the residual and send the summed
-bf16 pairs and its slice's sums of squares to every rank, which then normalizes whole rows. No
-fence, counter or barrier sits on the step's path. Every rank therefore runs the same norms, LM
+partials, summed in split order and stored, as 8-byte words carrying a flag (the decode
+position + 1), into other ranks' receive buffers (torch symmetric memory, NVLink peer stores).
+In the default push form (fb_allreduce_push) every rank stores its whole partial into every
+rank's buffer and fb_allreduce_sum_add_rmsnorm sums the ranks in rank order and applies
+add+RMSNorm; in the owner form (fb_reduce_scatter_push + fb_allreduce_add_rmsnorm) each value
+goes to the rank owning its column slice, which sums the slice and shares it. No fence,
+counter or barrier sits on the step's path. Every rank therefore runs the same norms, LM
 head and argmax on bit-identical data. Prefill (eager, untimed) uses NCCL all-reduces.
 """
 
