@@ -93,8 +93,9 @@ class Communicator:
 #: every rank, each sums all ranks; fb_allreduce_push + fb_allreduce_sum_add_rmsnorm) or "owner"
 #: (owner-computes reduce-scatter + all-gather, a quarter to an eighth of the volume in two
 #: phases; fb_reduce_scatter_push + fb_allreduce_add_rmsnorm). Same bits on every rank in either.
-#: Measured on B200 (config 4, the same box per pair): push 4282 / 6024 tok/s at 2/4 ranks
-#: (0.09 / 0.32 ms of all-reduce per step), owner 4080-4099 / 5593 (0.28-0.31 / 0.52 ms).
+#: Measured on B200 (config 4, the same box per pair): push 4282 / 6024 / 6645 tok/s at 2/4/8
+#: ranks (0.09 / 0.32 / 0.60 ms of all-reduce and skew per step), owner 4080-4099 / 5593 / 6508
+#: (0.28-0.31 / 0.52 / 0.65 ms).
 #: FB_TP_ALLREDUCE overrides the default.
 ALLREDUCE_FORM = os.environ.get("FB_TP_ALLREDUCE", "push")
 
