@@ -501,6 +501,45 @@ def test_allreduce_single_rank():
     assert (out == e_out).float().mean() >= 0.999 and ulps(out, e_out).max() <= 2
 
 
+def test_allreduce_push_single_rank():
+    """The push-form TP all-reduce at world 1: fb_allreduce_push stores the split-order sum of the
+    projection's K-split partials as flagged fp32 words (flag = epoch + 1 in the high half) into
+    slab `rank` of recv[use]; fb_allreduce_sum_add_rmsnorm then equals add_rms_norm over the same
+    partials (the residual sum bit for bit, the normalized row within the norm's ULPs)."""
+    import ctypes
+    from kernels import linear as klin
+    from kernels._native import lib, ptr, stream, check
+    from kernels.merged import Split
+    from kernels.rmsnorm import add_rms_norm
+    g = torch.Generator().manual_seed(22)
+    m, n, k = 16, 4096, 1536
+    x = torch.randn(m, k, generator=g).bfloat16().to(DEV)
+    w = (torch.randn(n, k, generator=g) * 0.05).bfloat16().to(DEV)
+    residual = torch.randn(m, n, generator=g).bfloat16().to(DEV)
+    gain = torch.randn(n, generator=g).bfloat16().to(DEV)
+    epoch = torch.full((1,), 12, dtype=torch.int64, device=DEV)
+    splits = int(lib.fb_linear_splits(m, n, k))
+    part = klin.project(x, w, klin.SPLITS_OUT, splits)
+    ordered = part[0].clone()
+    for s_ in range(1, splits):
+        ordered += part[s_]
+    recv = torch.zeros(2, 1, m, n, dtype=torch.int64, device=DEV)  # two uses, world 1
+    use = 1
+    check(lib.fb_allreduce_push(ptr(part), splits, m, n, 1, 0, use, (ctypes.c_void_p * 1)(recv.data_ptr()),
+                                ptr(epoch), stream()), "fb_allreduce_push")
+    out, summed = torch.empty_like(residual), torch.empty_like(residual)
+    check(lib.fb_allreduce_sum_add_rmsnorm(ptr(recv), use, 1, ptr(epoch), ptr(residual), ptr(gain), ptr(out),
+                                           ptr(summed), m, n, 1e-6, stream()), "fb_allreduce_sum_add_rmsnorm")
+    torch.cuda.synchronize()
+    halves = recv[use, 0].view(torch.int32).view(m, n, 2)  # little-endian: [value bits, flag]
+    assert bool((halves[..., 1] == 13).all())
+    assert torch.equal(halves[..., 0].contiguous().view(torch.float32), ordered)
+    assert bool((recv[0] == 0).all())  # use 0 untouched
+    e_out, e_sum = add_rms_norm(Split(part, (m, n)), residual, gain, 1e-6)
+    assert torch.equal(summed, e_sum)
+    assert (out == e_out).float().mean() >= 0.999 and ulps(out, e_out).max() <= 2
+
+
 @pytest.mark.parametrize("splits", [0, 6, 16])
 def test_qk_rope_cache_bit_exact_at_config4_shapes(splits):
     """The decode-step K cache append at the Qwen3-8B shapes (batch 16, 32/8 heads, D 128, one
