@@ -695,9 +695,9 @@ def main():
     qo_bytes = 2 * BATCH * weights.q_heads * cfg.head_dim * 2
     achieved = (kv_bytes + qo_bytes) / (attn_ms / 1e3) / 1e9
     # DRAM traffic of one launch from an ncu capture of this kernel at 16 rows x 8 KV heads x
-    # 8320 slots (dram__bytes_read.sum 545.78 MB + dram__bytes_write.sum 6.11 MB), scaled to
+    # 8320 slots (dram__bytes_read.sum 545.79 MB + dram__bytes_write.sum 5.54 MB), scaled to
     # this launch's valid slots (traffic grows in proportion to the slots streamed)
-    traffic = (545.78e6 + 6.11e6) * (valid / 8320) if weights.kv_heads == 8 else None
+    traffic = (545.79e6 + 5.54e6) * (valid / 8320) if weights.kv_heads == 8 else None
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                 "traffic": traffic, "kernel": "fb_decode_attention (per layer)",
                 "algorithmic_bytes": kv_bytes + qo_bytes, "launch_us": attn_ms * 1e3,

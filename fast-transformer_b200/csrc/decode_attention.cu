@@ -78,11 +78,67 @@ __device__ __forceinline__ int slice_owner(long long T, long long t, int G) {
 // taken in increasing CTA order (deterministic). A CTA in [lo, hi] whose slice is empty
 // wrote nothing and gets weight 0. Partials are read through L2 (ld.global.cg): they were
 // written by other CTAs of this launch moments ago.
-template <int D, typename Bar>
-__device__ void merge_pair(const Params& p, int pair, int lo, int hi, long long T, int tid,
-                           int threads, float* s_w, float* s_den, Bar bar) {
+//
+// A pair of at most kMergeRuns runs (the common case: a pair shared by neighbouring slices)
+// takes one L2 round trip: each thread owns outputs tid, tid + Threads, ... and loads every
+// run's accumulator for them together with the (m, l) of each output's head, with no block
+// barrier. Longer pairs resolve the runs' weights once into shared memory (warp per head),
+// then sweep the accumulators.
+constexpr int kMergeRuns = 4;
+
+template <int D, int Threads>
+__device__ void merge_short_pair(const Params& p, int pair, int lo, int runs, long long T, int tid) {
+  constexpr int kOut = (kHeadsPad * D + Threads - 1) / Threads;  // outputs per thread at most
   const int G = p.groups;
+  const int outputs = G * D;
+  const bool all_nonempty = T >= p.ctas;
+  const int b = pair / p.kv_heads, h = pair % p.kv_heads;
+  __nv_bfloat16* out = p.out + (static_cast<size_t>(b) * p.q_heads + h * G) * D;
+  const float2* st0 = p.stats + static_cast<size_t>(lo + pair) * G;     // run r, head g: st0[r * G + g]
+  const float* acc0 = p.acc + static_cast<size_t>(lo + pair) * outputs;  // run r, output e: acc0[r * G * D + e]
+  bool valid[kMergeRuns];
+  float2 sv[kMergeRuns][kOut];
+  float av[kMergeRuns][kOut];
+#pragma unroll
+  for (int r = 0; r < kMergeRuns; ++r) {
+    valid[r] = r < runs && (all_nonempty || slice_start(T, lo + r, p.ctas) < slice_start(T, lo + r + 1, p.ctas));
+#pragma unroll
+    for (int k = 0; k < kOut; ++k) {
+      const int e = tid + k * Threads;
+      const bool on = valid[r] && e < outputs;
+      sv[r][k] = on ? __ldcg(st0 + r * G + e / D) : make_float2(-INFINITY, 0.f);
+      av[r][k] = on ? __ldcg(acc0 + static_cast<size_t>(r) * outputs + e) : 0.f;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < kOut; ++k) {
+    const int e = tid + k * Threads;
+    float M = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < kMergeRuns; ++r) M = fmaxf(M, sv[r][k].x);
+    const float piv = M == -INFINITY ? 0.f : M;
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int r = 0; r < kMergeRuns; ++r)
+      if (valid[r]) {
+        const float w = exp2f(sv[r][k].x - piv);
+        L += sv[r][k].y * w;
+        if (w != 0.f) O += av[r][k] * w;
+      }
+    if (e < outputs) out[e] = __float2bfloat16_rn(O / L);
+  }
+}
+
+template <int D, int Threads, typename Bar>
+__device__ void merge_pair(const Params& p, int pair, int lo, int hi, long long T, int tid, float* s_w,
+                           float* s_den, Bar bar) {
   const int runs = hi - lo + 1;
+  if (runs <= kMergeRuns) {
+    merge_short_pair<D, Threads>(p, pair, lo, runs, T, tid);
+    return;
+  }
+  const int threads = Threads;
+  const int G = p.groups;
   const int warp = tid >> 5, lane = tid & 31, warps = threads >> 5;
   // With at least one tile per CTA every slice is non-empty: skip the 64-bit tests.
   const bool all_nonempty = T >= p.ctas;
@@ -533,8 +589,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
         if (misc[5]) {
           __threadfence();
-          merge_pair<D>(p, pair, misc[6], misc[7], total, ctid, kConsumerWarps * 32, merge_w,
-                        merge_den, [] { asm volatile("bar.sync 1, 128;" ::: "memory"); });
+          merge_pair<D, kConsumerWarps * 32>(p, pair, misc[6], misc[7], total, ctid, merge_w, merge_den,
+                                              [] { asm volatile("bar.sync 1, 128;" ::: "memory"); });
         }
       }
       asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
@@ -559,7 +615,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 constexpr int kCombineThreads = 256;
 
 template <int D>
-__global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const Params p) {
+__global__ void __launch_bounds__(kCombineThreads, 1) decode_combine_kernel(const Params p) {
   __shared__ int s_before, s_total, s_n;
   __shared__ float s_w[kMaxCtas * kHeadsPad];
   __shared__ float s_den[kHeadsPad];
@@ -595,7 +651,7 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const P
   const int lo = slice_owner(T, first, p.ctas);
   const int hi = slice_owner(T, first + n - 1, p.ctas);
   if (lo == hi) return;  // one run covered the pair and wrote the output itself
-  merge_pair<D>(p, pair, lo, hi, T, threadIdx.x, kCombineThreads, s_w, s_den, [] { __syncthreads(); });
+  merge_pair<D, kCombineThreads>(p, pair, lo, hi, T, threadIdx.x, s_w, s_den, [] { __syncthreads(); });
 }
 
 
