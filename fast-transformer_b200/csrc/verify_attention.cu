@@ -516,18 +516,42 @@ __global__ void __launch_bounds__(128) verify_merge_kernel(const Params p) {
   const int m = t * p.groups + g;
   const int d = threadIdx.x;
   if (d >= p.dim) return;
-  float M = -INFINITY;
-  for (int s = 0; s < p.splits; ++s)
-    M = fmaxf(M, p.stats[(static_cast<size_t>(pair) * p.splits + s) * p.members_pad + m].x);
-  const float piv = M == -INFINITY ? 0.f : M;
+  // up to kMergeSplits splits: every load in flight at once (one L2 round trip)
+  constexpr int kMergeSplits = 4;
   float L = 0.f, O = 0.f;
-  for (int s = 0; s < p.splits; ++s) {
-    const size_t slot = (static_cast<size_t>(pair) * p.splits + s) * p.members_pad + m;
-    const float2 st = p.stats[slot];
-    if (st.y == 0.f) continue;  // a split past the block saw nothing
-    const float w = exp2f(st.x - piv);
-    L += st.y * w;
-    O += p.acc[slot * 128 + d] * w;
+  const size_t slot0 = static_cast<size_t>(pair) * p.splits * p.members_pad + m;  // split s: + s * members_pad
+  if (p.splits <= kMergeSplits) {
+    float2 st[kMergeSplits];
+    float a[kMergeSplits];
+#pragma unroll
+    for (int s = 0; s < kMergeSplits; ++s) {
+      const size_t slot = slot0 + static_cast<size_t>(s) * p.members_pad;
+      st[s] = s < p.splits ? p.stats[slot] : make_float2(-INFINITY, 0.f);
+      a[s] = s < p.splits ? p.acc[slot * 128 + d] : 0.f;
+    }
+    float M = -INFINITY;
+#pragma unroll
+    for (int s = 0; s < kMergeSplits; ++s) M = fmaxf(M, st[s].x);
+    const float piv = M == -INFINITY ? 0.f : M;
+#pragma unroll
+    for (int s = 0; s < kMergeSplits; ++s) {
+      if (st[s].y == 0.f) continue;  // a split past the block (or past p.splits) saw nothing
+      const float w = exp2f(st[s].x - piv);
+      L += st[s].y * w;
+      O += a[s] * w;
+    }
+  } else {
+    float M = -INFINITY;
+    for (int s = 0; s < p.splits; ++s) M = fmaxf(M, p.stats[slot0 + static_cast<size_t>(s) * p.members_pad].x);
+    const float piv = M == -INFINITY ? 0.f : M;
+    for (int s = 0; s < p.splits; ++s) {
+      const size_t slot = slot0 + static_cast<size_t>(s) * p.members_pad;
+      const float2 st = p.stats[slot];
+      if (st.y == 0.f) continue;  // a split past the block saw nothing
+      const float w = exp2f(st.x - piv);
+      L += st.y * w;
+      O += p.acc[slot * 128 + d] * w;
+    }
   }
   p.out[static_cast<size_t>(index) * p.dim + d] = __float2bfloat16_rn(L > 0.f ? O / L : 0.f);
 }
