@@ -190,7 +190,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   // ---- after the dependency wait: positions, chains and Q come from earlier kernels ----
   pdl_wait();
   pdl_trigger();
-  const long long first = p.position[b] + 1;             // first block token's slot + 1
+  // Every global read of the set-up is issued before the first shared-memory store (one round
+  // trip): the row's position and chain, and this thread's Q chunks.
+  const long long position_b = p.position[b];
+  const long long chain_b = p.chain[b];
+  constexpr int kQChunks = kMembers * 16;  // 16-byte chunks of the 32-member Q tile
+  constexpr int kQPerThread = (kQChunks + kThreads - 1) / kThreads;
+  uint4 qv[kQPerThread];
+#pragma unroll
+  for (int it = 0; it < kQPerThread; ++it) {
+    const int e = tid + it * kThreads;
+    const int r = e / 16, c16 = e % 16;  // member row, 16-byte chunk of the 128-dim layout
+    const int m = group0 + r;
+    qv[it] = make_uint4(0, 0, 0, 0);
+    if (e < kQChunks && m < members && c16 * 8 < D) {
+      const int t = m / G, g = m % G;
+      qv[it] = *reinterpret_cast<const uint4*>(p.q + ((static_cast<size_t>(b) * T + t) * p.q_heads + h * G + g) * D +
+                                               c16 * 8);
+    }
+  }
+  const long long first = position_b + 1;                 // first block token's slot + 1
   long long end = first + T - 1;                          // one past the last block slot
   if (end > p.capacity) end = p.capacity;
   const long long begin = static_cast<long long>(split) * p.chunk;
@@ -199,23 +218,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tiles = stop > begin ? static_cast<int>((stop - begin + kTile - 1) / kTile) : 0;
   // Q members [group0, group0 + 32) of this (row, KV head) into the swizzled K-major tile;
   // rows past the real members, and dims past D, are zero.
-  for (int e = tid; e < kMembers * 16; e += blockDim.x) {
-    const int r = e / 16, c16 = e % 16;  // member row, 16-byte chunk of the 128-dim layout
-    const int m = group0 + r;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (m < members && c16 * 8 < D) {
-      const int t = m / G, g = m % G;
-      const __nv_bfloat16* src =
-          p.q + ((static_cast<size_t>(b) * T + t) * p.q_heads + h * G + g) * D + c16 * 8;
-      v = *reinterpret_cast<const uint4*>(src);
+#pragma unroll
+  for (int it = 0; it < kQPerThread; ++it) {
+    const int e = tid + it * kThreads;
+    if (e < kQChunks) {
+      const int r = e / 16, c16 = e % 16;
+      *reinterpret_cast<uint4*>(q_s + (c16 >> 3) * (kMembers * 128) + sw128(r, c16 & 7)) = qv[it];
     }
-    *reinterpret_cast<uint4*>(q_s + (c16 >> 3) * (kMembers * 128) + sw128(r, c16 & 7)) = v;
   }
   if (tid < kMembers) {
     const int m = group0 + tid;
     const int t = m / G;
     const bool live = m < members;
-    const bool chained = live && t < p.chain[b];
+    const bool chained = live && t < chain_b;
     col_valid[tid] = live ? static_cast<int>(first + (chained ? t : 0)) : 0;
     col_own[tid] = live && !chained ? static_cast<int>(first - 1 + t) : -1;
     col_max[tid] = -INFINITY;
