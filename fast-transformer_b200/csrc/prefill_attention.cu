@@ -272,7 +272,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c0 = 0; c0 < 64; c0 += 32) {
         const float* v = sv + c0;
         uint32_t packed[16];
-#pragma unroll
         if (interior) {
 #pragma unroll
           for (int c = 0; c < 32; c += 2) {
