@@ -66,6 +66,11 @@ int fb_device_error(unsigned int* host_flags);
  * fb_decode_attention_partials + fb_decode_attention_combine: the same result in two
  *   launches (partials, then the merge kernel), the reference's _decode_partials/_decode_merge
  *   split; no counter state. Both take the same arguments and `ctas`.
+ *
+ * Launched with programmatic stream serialization: `position`, and the cache slots below it,
+ * are read before the wait on the previous kernel, so they must not be written by the kernel
+ * launched immediately before on the same stream (in a decode step the position advances at
+ * least two kernels earlier); q and the newest slot may come from that kernel.
  * ---------------------------------------------------------------------------------- */
 int fb_decode_attention_ctas(int batch, int kv_heads, int capacity, int head_dim);
 size_t fb_decode_attention_workspace(int batch, int q_heads, int kv_heads, int head_dim, int ctas);
